@@ -1,0 +1,224 @@
+"""Generate golden vectors from the reference's own HF implementation.
+
+Run in a container that has the reference tree (not needed on the GPU box):
+
+    python tests/golden/make_golden.py --reference <path to LastKV checkout>
+
+It imports ``lastkv.llm`` from ``<reference>/llm/src``, builds two seeded
+random-init models and records every attention call of the cached chunk
+recurrence (``LastKVAttention.forward``, llm/src/lastkv/llm/modeling.py:98-148):
+the pre-RoPE projections, cos/sin, the post-RoPE/RMSNorm query and new K/V
+handed to SDPA, and SDPA's output; plus end-to-end logits and greedy tokens.
+
+* ``tiny_ref.npz`` - the reference test suite's own tiny model
+  (llm/tests/test_llm_inference.py:18-36, seed 19, head_dim 8, chunk 4).
+* ``small_d128.npz`` - the same architecture at head_dim 128, GQA 4:1,
+  chunk 16 (one ring = 2 pages of 16), batch 2, so the CUDA kernels can run
+  on the identical calls.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+
+
+def build(reference: str):
+    sys.path.insert(0, os.path.join(reference, "llm", "src"))
+    import torch
+    from lastkv.llm import CustomRecurrentMarinAKV254ReuseKVConfig as Config
+    from lastkv.llm import CustomRecurrentMarinAKV254ReuseKVForCausalLM as Model
+
+    return torch, Config, Model
+
+
+def tiny_model(torch, Config, Model):
+    # Same construction as llm/tests/test_llm_inference.py:18-36.
+    torch.manual_seed(19)
+    config = Config(
+        hidden_size=32, intermediate_size=48, num_attention_heads=4,
+        num_key_value_heads=2, num_hidden_layers=3, head_dim=8,
+        vocab_size=71, chunk_size=4, max_position_embeddings=64,
+        bos_token_id=1, eos_token_id=None, pad_token_id=0,
+        deep_v_scale_init=[[0.3, 0.7], [0.8, 1.2], [1.1, 0.9]],
+        rope_theta=500000.0, attn_implementation="sdpa",
+    )
+    model = Model(config).eval()
+    with torch.no_grad():
+        for i, layer in enumerate(model.model.layers):
+            layer.self_attn.prev_chunk_alphas.copy_(torch.tensor([-1.2 + i * 0.2, 0.8 - i * 0.3]))
+            layer.self_attn.q_norm.weight.copy_(torch.linspace(0.7, 1.3, config.head_dim))
+            layer.self_attn.k_norm.weight.copy_(torch.linspace(1.2, 0.8, config.head_dim))
+    return model
+
+
+def small_model(torch, Config, Model):
+    torch.manual_seed(7)
+    config = Config(
+        hidden_size=64, intermediate_size=96, num_attention_heads=4,
+        num_key_value_heads=1, num_hidden_layers=2, head_dim=128,
+        vocab_size=97, chunk_size=16, max_position_embeddings=256,
+        bos_token_id=1, eos_token_id=None, pad_token_id=0,
+        deep_v_scale_init=[[0.6], [1.3]], rope_theta=500000.0,
+        attn_implementation="sdpa", initializer_range=0.08,
+    )
+    model = Model(config).eval()
+    with torch.no_grad():
+        for i, layer in enumerate(model.model.layers):
+            layer.self_attn.prev_chunk_alphas.copy_(torch.tensor([0.9 - 1.7 * i]))
+            layer.self_attn.q_norm.weight.copy_(torch.linspace(0.6, 1.4, config.head_dim))
+            layer.self_attn.k_norm.weight.copy_(torch.linspace(1.3, 0.7, config.head_dim))
+    return model
+
+
+class Recorder:
+    """Record every SDPA call of LastKVAttention with its pre-RoPE inputs."""
+
+    def __init__(self, torch, model, keep_full: bool):
+        self.torch = torch
+        self.model = model
+        self.keep_full = keep_full
+        self.calls = []
+        self.pending = {}
+        self.handles = []
+        for index, layer in enumerate(model.model.layers):
+            attn = layer.self_attn
+            self.handles.append(attn.register_forward_pre_hook(self._pre(index)))
+            for name in ("q_proj", "k_proj", "v_proj"):
+                self.handles.append(getattr(attn, name).register_forward_hook(self._proj(name)))
+        import torch.nn.functional as F
+
+        self.F = F
+        self.orig = F.scaled_dot_product_attention
+        F.scaled_dot_product_attention = self._sdpa
+
+    def _pre(self, index):
+        def hook(module, args):
+            hidden, (cos, sin), cache = args
+            self.pending = {"layer": index, "start": cache.seen_tokens,
+                            "cos": cos.detach().clone(), "sin": sin.detach().clone()}
+        return hook
+
+    def _proj(self, name):
+        def hook(module, args, output):
+            self.pending[name] = output.detach().clone()
+        return hook
+
+    def _sdpa(self, query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, enable_gqa=False):
+        out = self.orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
+                        is_causal=is_causal, scale=scale, enable_gqa=enable_gqa)
+        lq = query.shape[2]
+        rec = dict(self.pending)
+        rec.update(q=query.detach().clone(), k_new=key[:, :, -lq:].detach().clone(),
+                   v_new=value[:, :, -lq:].detach().clone(), out=out.detach().clone(),
+                   key_len=key.shape[2])
+        if self.keep_full:
+            rec.update(full_k=key.detach().clone(), full_v=value.detach().clone())
+        self.calls.append(rec)
+        return out
+
+    def close(self):
+        self.F.scaled_dot_product_attention = self.orig
+        for h in self.handles:
+            h.remove()
+
+
+def params(model):
+    cfg = model.config
+    layers = model.model.layers
+    return {
+        "alpha_logits": np.stack([l.self_attn.prev_chunk_alphas.detach().numpy() for l in layers]).astype(np.float32),
+        "v_scale": np.stack([l.self_attn.deep_v_scale.detach().numpy() for l in layers]).astype(np.float32),
+        "q_norm_w": np.stack([l.self_attn.q_norm.weight.detach().numpy() for l in layers]).astype(np.float32),
+        "k_norm_w": np.stack([l.self_attn.k_norm.weight.detach().numpy() for l in layers]).astype(np.float32),
+        "eps": np.float32(cfg.rms_norm_eps),
+        "chunk": np.int64(cfg.chunk_size),
+        "num_heads": np.int64(cfg.num_attention_heads),
+        "num_kv_heads": np.int64(cfg.num_key_value_heads),
+        "head_dim": np.int64(cfg.head_dim),
+        "num_layers": np.int64(cfg.num_hidden_layers),
+        "rope_theta": np.float64(cfg.rope_theta if hasattr(cfg, "rope_theta") else cfg.rope_parameters["rope_theta"]),
+    }
+
+
+def flatten_calls(calls, prefix, keep_full):
+    out = {}
+    out[f"{prefix}n"] = np.int64(len(calls))
+    for i, c in enumerate(calls):
+        p = f"{prefix}{i}_"
+        out[p + "meta"] = np.array([c["layer"], c["start"], c["q"].shape[2], c["key_len"]], dtype=np.int64)
+        for name in ("q_proj", "k_proj", "v_proj", "cos", "sin", "q", "k_new", "v_new", "out"):
+            out[p + name] = c[name].numpy().astype(np.float32)
+        if keep_full:
+            out[p + "full_k"] = c["full_k"].numpy().astype(np.float32)
+            out[p + "full_v"] = c["full_v"].numpy().astype(np.float32)
+    return out
+
+
+def record_run(torch, model, tokens, segments, keep_full):
+    """Run the cached path over ``segments``; return calls and per-segment logits."""
+    rec = Recorder(torch, model, keep_full)
+    logits = []
+    cache, start = None, 0
+    try:
+        with torch.inference_mode():
+            for size in segments:
+                res = model(tokens[:, start:start + size], past_key_values=cache, use_cache=True)
+                logits.append(res.logits)
+                cache = res.past_key_values
+                start += size
+    finally:
+        rec.close()
+    return rec.calls, torch.cat(logits, dim=1).numpy().astype(np.float32)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    args = ap.parse_args()
+    torch, Config, Model = build(args.reference)
+    torch.set_num_threads(1)
+
+    # --- tiny: the reference test's own model ------------------------------
+    model = tiny_model(torch, Config, Model)
+    g = torch.Generator().manual_seed(123)
+    tokens = torch.randint(3, 71, (2, 15), generator=g)
+    segments = [3, 2, 7, 3]
+    calls, logits = record_run(torch, model, tokens, segments, keep_full=True)
+    with torch.inference_mode():
+        full = model(tokens, use_cache=False).logits.numpy().astype(np.float32)
+        gen = model.generate(torch.tensor([[1, 5, 17]]), max_new_tokens=10, do_sample=False, use_cache=True)
+    data = {"tokens": tokens.numpy(), "segments": np.array(segments), "logits_incremental": logits,
+            "logits_full": full, "generate_prompt": np.array([[1, 5, 17]]), "generate_out": gen.numpy()}
+    data.update(params(model))
+    data.update(flatten_calls(calls, "call", keep_full=True))
+    np.savez_compressed(os.path.join(args.out, "tiny_ref.npz"), **data)
+    print("tiny_ref:", len(calls), "calls")
+
+    # --- small_d128: head_dim 128, GQA 4:1, batch 2 -------------------------
+    model = small_model(torch, Config, Model)
+    g = torch.Generator().manual_seed(321)
+    tokens = torch.randint(3, 97, (2, 64), generator=g)
+    segments = [37] + [1] * 27  # chunked prefill across two boundaries, then decode
+    calls, logits = record_run(torch, model, tokens, segments, keep_full=False)
+    state = {f"w_{k}": v.detach().numpy().astype(np.float32) for k, v in model.state_dict().items()}
+    with torch.inference_mode():
+        gen = model.generate(tokens[:1, :20], max_new_tokens=24, do_sample=False, use_cache=True)
+    data = {"tokens": tokens.numpy(), "segments": np.array(segments), "logits_incremental": logits,
+            "generate_prompt": tokens[:1, :20].numpy(), "generate_out": gen.numpy(),
+            "hidden_size": np.int64(model.config.hidden_size),
+            "intermediate_size": np.int64(model.config.intermediate_size),
+            "vocab_size": np.int64(model.config.vocab_size)}
+    data.update(params(model))
+    data.update(state)
+    data.update(flatten_calls(calls, "call", keep_full=False))
+    np.savez_compressed(os.path.join(args.out, "small_d128.npz"), **data)
+    print("small_d128:", len(calls), "calls")
+
+
+if __name__ == "__main__":
+    main()
