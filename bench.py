@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Shared-KV decode benchmark (the reference's config 2, in its merged paged form).
+
+Workload ("shared_kv_decode_attention"): bf16, batch 64, 32 query heads,
+8 KV heads, head_dim 128, 8192 keys per sequence in 16-token pages with a
+shuffled page table; chunk 1024, so each layer's block table is the 384 shared
+final-layer pages [0, 6144) followed by that layer's 128 ring pages
+[6144, 8192).  One step = one decode token for all 64 sequences = 32 layer
+calls, each reading the full 2 GiB of K/V once (larger than L2, so no flush is
+needed between steps).  Q/K/V ~ N(0, 1) (K stands for post-RoPE keys), seeded.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's own
+CPU computation of the same layer-step (compose the history with torch.cat and
+call torch SDPA on the host cores, llm/src/lastkv/llm/modeling.py:109-146) via
+the oracle's restatement; it never touches the GPU.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+CFG = dict(batch=64, q_heads=32, kv_heads=8, head_dim=128, context=8192, page=16, layers=32, chunk=1024)
+METRIC = "decode tokens/s (shared-KV attention, 32 layers)"
+UNIT = "tokens/s"
+ALGO_BYTES = 2 * CFG["batch"] * CFG["kv_heads"] * CFG["context"] * CFG["head_dim"] * 2  # per layer call
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config(n_gpus):
+    return {"workload": "shared_kv_decode_attention", "batch_per_gpu": CFG["batch"],
+            "global_batch": CFG["batch"] * n_gpus, "q_heads": CFG["q_heads"], "kv_heads": CFG["kv_heads"],
+            "head_dim": CFG["head_dim"], "context_tokens": CFG["context"], "page_tokens": CFG["page"],
+            "layers_per_step": CFG["layers"], "chunk": CFG["chunk"], "layout": "merged [shared pages | layer ring]",
+            "page_table": "shuffled", "l2": "inputs (2 GiB per layer call) larger than L2; no flush",
+            "parallelism": f"dp{n_gpus} (batch-sharded replicas, no collective)"}
+
+
+# ----------------------------------------------------------------- CPU baseline
+
+
+class CpuLayerStep:
+    """The reference's CPU layer-step (torch.cat history + SDPA) on `batch` sequences."""
+
+    def __init__(self, batch: int):
+        import torch
+
+        from oracle.lastkv_oracle import reference_layer_step_cpu
+
+        self.fn = reference_layer_step_cpu
+        torch.manual_seed(0)
+        H, Hq, D, N, C = CFG["kv_heads"], CFG["q_heads"], CFG["head_dim"], CFG["context"], CFG["chunk"]
+        deep = N - C  # completed chunks [0, 7168) incl. the recent chunk; current chunk holds 1024 keys
+        dt = torch.bfloat16
+        self.args = (torch.randn(batch, Hq, 1, D, dtype=dt),
+                     torch.randn(batch, H, deep, D, dtype=dt), torch.randn(batch, H, deep, D, dtype=dt),
+                     torch.randn(batch, H, C, D, dtype=dt), torch.randn(batch, H, C, D, dtype=dt),
+                     torch.randn(batch, H, C, D, dtype=dt), torch.randn(batch, H, C, D, dtype=dt),
+                     torch.randn(H), torch.rand(H) + 0.5, C)
+        self.threads = torch.get_num_threads()
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        self.fn(*self.args)
+        return time.perf_counter() - t0
+
+
+def cpu_layer_step_sample(seconds: float, batch: int):
+    runner = CpuLayerStep(batch)
+    runner.step()  # warm
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 3:
+        times.append(runner.step())
+    return times, runner.threads
+
+
+def cpu_tokens_per_s(layer_step_s: float, batch: int) -> float:
+    return batch / (CFG["layers"] * layer_step_s)
+
+
+# ----------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        import tempfile
+
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8 or not self.uuid or self.uuid not in parts[0]:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------- GPU arm
+
+
+def build_workload(rank: int, device):
+    import torch
+
+    from lastkv_b200 import ops
+
+    B, Hq, H, D, N, L, C, P = (CFG[k] for k in ("batch", "q_heads", "kv_heads", "head_dim", "context", "layers",
+                                                  "chunk", "page"))
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    pos = N - 1
+    cur = (pos // C) * C
+    rec = max(0, cur - C)
+    nsrc = rec // P  # 384 shared pages per sequence
+    ring_pages = 2 * C // P  # 128
+    window_pages = -(-(pos + 1 - rec) // P)  # 128
+    ring_stride = ring_pages * B + 1
+    src_total = B * nsrc
+    num_pages = src_total + L * ring_stride
+    pool_k = torch.randn((num_pages, P, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    pool_v = torch.randn((num_pages, P, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    perm = torch.randperm(src_total, generator=gen, device=device).to(torch.int32)
+    W = nsrc + window_pages
+    bt = torch.empty((B, W), dtype=torch.int32, device=device)
+    bt[:, :nsrc] = perm.view(B, nsrc)
+    first = (rec // P) % ring_pages
+    j = torch.arange(window_pages, device=device)
+    bt[:, nsrc:] = (torch.arange(B, device=device)[:, None] * ring_pages + (first + j[None, :]) % ring_pages).to(
+        torch.int32)
+    nsrc_t = torch.full((B,), nsrc, dtype=torch.int32, device=device)
+    ring_base = (src_total + torch.arange(L, device=device) * ring_stride).to(torch.int32)
+    bt_all = ops.build_layer_block_tables(bt, nsrc_t, ring_base)
+    seq_k = torch.full((B,), pos + 1, dtype=torch.int32, device=device)
+    q = torch.randn((L, B, Hq, D), generator=gen, device=device, dtype=torch.bfloat16)
+    scale = (torch.rand((L, H), generator=gen, device=device) + 0.5).to(torch.bfloat16).float()
+    out_scale = scale.repeat_interleave(Hq // H, dim=1).contiguous()
+    out = torch.empty((L, B, Hq, D), dtype=torch.bfloat16, device=device)
+    ws = ops.Workspace.for_decode(B, Hq, D, W, device=device)
+    return dict(pool_k=pool_k, pool_v=pool_v, bt=bt, nsrc=nsrc_t, ring_base=ring_base, bt_all=bt_all, seq_k=seq_k,
+                q=q, out_scale=out_scale, out=out, ws=ws, W=W)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from lastkv_b200 import _capi, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    _capi.load()
+    _capi.check(_capi.lib().lkv_check_device(local), "lkv_check_device")
+    wl = build_workload(rank, device)
+    L, B = CFG["layers"], CFG["batch"]
+    splits, launches_per_call = ops.decode_plan(B, CFG["q_heads"], CFG["kv_heads"], CFG["head_dim"], wl["W"],
+                                                wl["ws"])
+
+    def layer(l):
+        ops.decode_paged(wl["q"][l], wl["pool_k"], wl["pool_v"], wl["bt_all"][l], wl["seq_k"], out=wl["out"][l],
+                         out_scale=wl["out_scale"][l], workspace=wl["ws"], max_pages=wl["W"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 0)):
+        for l in range(L):
+            layer(l)
+    torch.cuda.synchronize()
+
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    clocks = ClockSampler(uuid)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps * L)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for s in range(args.steps):
+        for l in range(L):
+            a, b = ev[s * L + l]
+            a.record(stream)
+            layer(l)
+            b.record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    op_ms = [a.elapsed_time(b) for a, b in ev]
+    err = wl["ws"].error()
+    if err[0] != 0:
+        raise RuntimeError(f"device error word set: {err}")
+
+    # ---- end to end through the public op with host buffers every step
+    q_host = torch.empty(wl["q"].shape, dtype=wl["q"].dtype, pin_memory=True)
+    q_host.copy_(wl["q"].cpu())
+    out_host = torch.empty(wl["out"].shape, dtype=wl["out"].dtype, pin_memory=True)
+    bt_host = wl["bt"].cpu().pin_memory()
+    nsrc_host = wl["nsrc"].cpu().pin_memory()
+    seqk_host = wl["seq_k"].cpu().pin_memory()
+    h2d = q_host.numel() * 2 + bt_host.numel() * 4 + nsrc_host.numel() * 4 + seqk_host.numel() * 4
+    d2h = out_host.numel() * 2
+
+    def e2e_step():
+        wl["q"].copy_(q_host, non_blocking=True)
+        wl["bt"].copy_(bt_host, non_blocking=True)
+        wl["nsrc"].copy_(nsrc_host, non_blocking=True)
+        wl["seq_k"].copy_(seqk_host, non_blocking=True)
+        ops.build_layer_block_tables(wl["bt"], wl["nsrc"], wl["ring_base"], out=wl["bt_all"])
+        for l in range(L):
+            layer(l)
+        out_host.copy_(wl["out"], non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    vals = torch.tensor([total_ms, e2e_ms, float(np.mean(op_ms))], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms, avg_op_ms = vals.tolist()
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))
+        peak, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        peak, peak_src = 6650.0, "fallback"
+    achieved = ALGO_BYTES / (avg_op_ms * 1e-3) / 1e9
+    tokens = B * args.steps * world
+    line = {
+        "metric": METRIC, "value": tokens / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(world),
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src,
+                     "kernel": "decode op = decode_splitkv_kernel + merge_partials_kernel",
+                     "algorithmic_bytes_per_launch": ALGO_BYTES, "avg_launch_ms": avg_op_ms,
+                     "traffic": None},
+        "attn_hbm_gbs": achieved,
+        "clocks": clk,
+        "gpu_launches": int(args.steps * L * launches_per_call),
+        "kv_splits": splits,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times, threads = cpu_layer_step_sample(args.cpu_seconds, batch=8)
+        med = statistics.median(times)
+        line["cpu_baseline"] = {"value": cpu_tokens_per_s(med, 8), "unit": UNIT, "cores": threads,
+                                "kind": "port",
+                                "sample": f"reference CPU layer-step (torch.cat history + torch SDPA, bf16) on 8 of "
+                                          f"64 sequences, {len(times)} reps, median {med * 1e3:.1f} ms; "
+                                          f"tokens/s = 8 / (32 layers x median)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    batch = 8
+    runner = CpuLayerStep(batch)
+    threads = runner.threads
+    warm = [runner.step() for _ in range(max(args.warmup, 0))]
+    steps = [runner.step() for _ in range(max(args.steps, 1))]
+    med = statistics.median(steps)
+    value = cpu_tokens_per_s(med, batch)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"one layer-step of the reference's CPU attention (torch.cat history + torch SDPA "
+                                   f"bf16) on {batch} of 64 sequences per step; tokens/s = {batch} / (32 x median)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "warmup_s": [round(x, 4) for x in warm],
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,165 @@
+/*
+ * lastkv_b200 — C ABI of the B200 (sm_100a) kernels for LastKV's shared
+ * last-layer-KV attention path.
+ *
+ * Memory layout shared by every entry point (the reference's merged pool,
+ * vllm/src/lastkv/vllm/backends/rmarin_flashinfer/batching.py:1999-2016):
+ *   pool_k, pool_v : bf16 [num_pages, page_size=16, num_kv_heads, head_dim]
+ *                    pages [0, src_pages) hold the shared final-layer history
+ *                    (raw K, raw V); each layer owns ring pages that hold K and
+ *                    V / s_l for the previous and current chunk.
+ *   block_table    : int32 [batch, >= pages_per_seq] row-strided, one row per
+ *                    sequence = [older shared pages | this layer's ring pages]
+ *   seq_k          : int32 [batch] number of keys of each sequence
+ *   q / out        : bf16 [tokens, num_q_heads, head_dim], head_dim contiguous,
+ *                    heads packed, rows strided by q_stride_tok / out_stride_tok
+ *
+ * All pointers are device pointers unless stated; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).  Calls never allocate, never synchronise and
+ * are safe to record into a CUDA graph.  Every entry point returns LKV_OK or a
+ * nonzero status; nothing is launched when the status is nonzero.
+ *
+ * Device-side failures (a block-table page outside the pool, an append slot
+ * outside the pool, a pipeline wait that gave up) do not fault: the kernel
+ * skips the access and records the first failure in the int32[4] error word
+ * at the start of the workspace (or the `error_word` argument), readable with
+ * lkv_read_error_word().
+ */
+#ifndef LASTKV_B200_H
+#define LASTKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LKV_OK 0
+#define LKV_ERR_INVALID_ARGUMENT 1
+#define LKV_ERR_UNSUPPORTED 2
+#define LKV_ERR_CUDA 3
+#define LKV_ERR_ARCH 4
+#define LKV_ERR_TENSOR_MAP 5
+#define LKV_ERR_WORKSPACE 6
+
+#define LKV_PAGE_SIZE 16
+
+/* Human-readable text of a status code. */
+const char* lkv_status_string(int status);
+
+/* ABI version of this library (major * 100 + minor). */
+int lkv_abi_version(void);
+
+/* LKV_OK if `device` is an sm_100 (B200-class) GPU this library was built for. */
+int lkv_check_device(int device);
+
+/* Copy the int32[4] error word {code, kernel, block, detail} to host memory.
+ * Synchronises `stream`.  code 0 means no device-side failure was recorded. */
+int lkv_read_error_word(const int32_t* error_word, int32_t host_out[4], void* stream);
+
+/* Zero the error word (asynchronously on `stream`). */
+int lkv_clear_error_word(int32_t* error_word, void* stream);
+
+/* ------------------------------------------------------------------ decode
+ * One query token per sequence against its paged history (split-KV).
+ * Replaces, for uniform decode steps, the merged per-layer attention call
+ *   flash_attn_varlen_func(q, pool_k, pool_v, cu_seqlens_q, seqused_k,
+ *                          causal=True, block_table=bt_all[l]) + head_scale_
+ * (vllm/.../rmarin_flashinfer/fastpath.py:643-650) and, at the HF level, the
+ * SDPA call of LastKVAttention.forward (llm/src/lastkv/llm/modeling.py:143-146).
+ *   out[b, h, :] = out_scale[h] * softmax(q k^T * softmax_scale) v   (bf16)
+ *   lse[b, h]    = natural-log log-sum-exp of the scaled scores (optional)
+ * out_scale (fp32 [num_q_heads], optional) folds the per-layer value scale s_l
+ * (fused_qkv.py:140-155).  With `partial_o`/`partial_lse` non-NULL the call
+ * instead writes fp32 normalised outputs [batch, num_q_heads, head_dim] and
+ * natural-log LSE [batch, num_q_heads] for a later lkv_merge_partials (the
+ * context-parallel combine); `out`, `lse` and `out_scale` are then ignored.
+ * Supported: head_dim 64 or 128; num_q_heads / num_kv_heads in {1, 2, 4, 8}.
+ */
+size_t lkv_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int max_pages_per_seq);
+
+int lkv_decode_paged(const void* q, int64_t q_stride_tok,
+                     const void* pool_k, const void* pool_v, int64_t num_pages,
+                     const int32_t* block_table, int64_t block_table_stride,
+                     const int32_t* seq_k,
+                     void* out, int64_t out_stride_tok, float* lse, const float* out_scale,
+                     float* partial_o, float* partial_lse,
+                     int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                     int max_pages_per_seq, float softmax_scale,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Host query: how many KV splits and kernel launches lkv_decode_paged will use
+ * for this shape and workspace on the current device (partial != 0 for the
+ * partial-output form).  Needs a device; launches nothing. */
+int lkv_decode_plan(int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_pages_per_seq,
+                    size_t workspace_bytes, int partial, int* num_splits, int* num_launches);
+
+/* ------------------------------------------------------------------ merge
+ * Exact log-sum-exp merge of `num_parts` attention partials over disjoint key
+ * sets (flashinfer cascade.merge_state / vLLM merge_attn_states, used at
+ * flashinfer_executor.py:185-231 and fastpath.py:719):
+ *   o_parts   fp32 [num_parts, rows, head_dim]   (normalised partial outputs)
+ *   lse_parts fp32 [num_parts, rows]             (natural log, -inf = empty)
+ *   out       bf16 [rows, head_dim] = out_scale[row % num_q_heads] * merged
+ *   lse_out   fp32 [rows] (optional)
+ * rows = tokens * num_q_heads.  out_scale is optional. */
+int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows,
+                       int head_dim, int num_q_heads, const float* out_scale,
+                       void* out, float* lse_out, void* stream);
+
+/* ------------------------------------------------------------------ append
+ * Fused cache-append epilogue of one layer; replaces _fused_qkv_kernel
+ * (vllm/.../rmarin_flashinfer/fused_qkv.py:58-126, called at fastpath.py:635-642)
+ * and the HF per-layer RoPE + q/k norm + cache append
+ * (llm/src/lastkv/llm/modeling.py:103-108).  For every token t:
+ *   q_out[t, h]       = RMSNorm(RoPE(q[t, h]))       (norm after RoPE)
+ *   ring_k[slot_t, j] = RMSNorm(RoPE(k[t, j]))
+ *   ring_v[slot_t, j] = bf16(v[t, j] * inv_scale[j])  (rings hold V / s_l)
+ *   and, when src_slot != NULL (the top layer), src_k / src_v at src_slot[t]
+ *   receive the normalised k and the raw v (the shared history).
+ * q [T, *] row stride q_row, k/v likewise (bf16); positions int64 [T];
+ * cos_sin bf16 [max_position, head_dim] = cos | sin halves (NeoX, full head);
+ * q_weight / k_weight bf16 [head_dim]; inv_scale fp32 [num_kv_heads] or NULL;
+ * ring_k/ring_v/src_k/src_v are flat token views [slots, num_kv_heads, head_dim]
+ * of the page pool (slot = page * 16 + row).  Out-of-range positions or slots
+ * are skipped and recorded in `error_word` (int32[4], may be NULL). */
+int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_row,
+                         const void* v, int64_t v_row, const int64_t* positions,
+                         const void* cos_sin, int64_t cos_sin_row, int64_t max_position,
+                         const void* q_weight, const void* k_weight, float eps,
+                         const float* inv_scale, void* q_out, int64_t q_out_row,
+                         const int64_t* ring_slot, void* ring_k, void* ring_v, int64_t ring_slots,
+                         const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots,
+                         int num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                         int32_t* error_word, void* stream);
+
+/* ------------------------------------------------------------------ blend
+ * Chunk-boundary commit; replaces blend_chunk_ / _commit_previous_boundary
+ * (fused_qkv.py:158-201, batching.py:1099-1144).  For every layer l, sequence
+ * s and page j of the finished chunk:
+ *   ring = bf16(bf16(a*raw) + bf16(bf16(1-a)*ring)),  a = alpha[l, head]
+ * on K and V (rings hold V / s_l, the shared pages raw V).
+ * raw_pages int32 [num_seqs, pages_per_chunk]: shared pages of the chunk;
+ * ring_pages int32 [num_seqs, pages_per_chunk]: layer-0 ring pages; layer l
+ * uses ring_pages + l * ring_layer_stride_pages.  alpha fp32 [num_layers,
+ * num_kv_heads] holding bf16-exact sigmoid values. */
+int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages,
+                    const int32_t* raw_pages, const int32_t* ring_pages, int64_t ring_layer_stride_pages,
+                    const float* alpha, int num_layers, int num_seqs, int pages_per_chunk,
+                    int num_kv_heads, int head_dim, int32_t* error_word, void* stream);
+
+/* ------------------------------------------------------------------ block tables
+ * Per-layer block tables of the merged pool (fastpath.py:422-424):
+ *   bt_all[l, b, c] = block_table[b, c]                 for c <  nsrc[b]
+ *                   = block_table[b, c] + ring_base[l]  for c >= nsrc[b]
+ * block_table holds older shared pages then layer-relative ring pages. */
+int lkv_build_layer_block_tables(const int32_t* block_table, int64_t block_table_stride,
+                                 const int32_t* nsrc, const int32_t* ring_base,
+                                 int num_layers, int batch, int width, int32_t* bt_all, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LASTKV_B200_H */

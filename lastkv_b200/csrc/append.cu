@@ -1,0 +1,281 @@
+// Cache-append epilogue and boundary commit for the merged paged pool (sm_100a).
+//
+// rope_norm_append_kernel  - one warp per (token, head): NeoX RoPE, then
+//   RMSNorm over head_dim for q and k (norm AFTER RoPE, as the published
+//   model; llm/src/lastkv/llm/modeling.py:103-106), V scaled by 1/s_l, and the
+//   paged stores: normalised q to q_out, k and V/s_l into the layer ring slot,
+//   and - for the top layer - raw k and raw V into the shared-history slot.
+//   Arithmetic order follows the vLLM fused epilogue
+//   (vllm/src/lastkv/vllm/backends/rmarin_flashinfer/fused_qkv.py:23-90):
+//   fp32 math, x*c - y*s as one FMA, one bf16 rounding after RoPE, fp32 sum of
+//   squares, rsqrt, x*inv*w with one rounding.
+// blend_chunk_kernel - at a chunk boundary, ring = a*raw + (1-a)*ring for every
+//   layer ring, K and V (V in V/s units), each product rounded to bf16 like the
+//   four eager torch ops (fused_qkv.py:158-201, batching.py:1099-1144).
+// build_block_tables_kernel - bt_all[l][b][c] = bt[b][c] for the older pages and
+//   bt[b][c] + ring_base[l] for ring pages (fastpath.py:422-424).
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lkv {
+
+struct AppendParams {
+  const __nv_bfloat16* q;
+  int64_t q_row;
+  const __nv_bfloat16* k;
+  int64_t k_row;
+  const __nv_bfloat16* v;
+  int64_t v_row;
+  const int64_t* pos;
+  const __nv_bfloat16* cos_sin;
+  int64_t cs_row;
+  int64_t max_pos;
+  const __nv_bfloat16* qw;
+  const __nv_bfloat16* kw;
+  float eps;
+  const float* inv_scale;
+  __nv_bfloat16* q_out;
+  int64_t q_out_row;
+  const int64_t* ring_slot;
+  __nv_bfloat16* ring_k;
+  __nv_bfloat16* ring_v;
+  int64_t ring_slots;
+  const int64_t* src_slot;
+  __nv_bfloat16* src_k;
+  __nv_bfloat16* src_v;
+  int64_t src_slots;
+  int T, Hq, Hkv;
+  int* err;
+};
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <int D>
+__global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParams p) {
+  constexpr int HALF = D / 2;
+  constexpr int E = HALF / 32;  // rotary pairs per lane (2 for D=128, 1 for D=64)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x * 8 + warp;
+  const int t = blockIdx.y;
+  if (h >= p.Hq + p.Hkv) return;
+  const bool is_q = h < p.Hq;
+  const int j = h - p.Hq;  // kv head
+  const int64_t pos = p.pos[t];
+  if (pos < 0 || pos >= p.max_pos) {
+    if (lane == 0) report_error(p.err, DEVERR_BAD_SLOT, 2, (int)pos);
+    return;
+  }
+  const __nv_bfloat16* src = is_q ? p.q + (int64_t)t * p.q_row + (int64_t)h * D : p.k + (int64_t)t * p.k_row + (int64_t)j * D;
+  const __nv_bfloat16* cs = p.cos_sin + pos * p.cs_row;
+  const int i0 = lane * E;
+  float r1[E], r2[E];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float x = __bfloat162float(src[i0 + e]);
+    const float y = __bfloat162float(src[HALF + i0 + e]);
+    const float cc = __bfloat162float(cs[i0 + e]);
+    const float sn = __bfloat162float(cs[HALF + i0 + e]);
+    r1[e] = bf16r(__fmaf_rn(x, cc, -__fmul_rn(y, sn)));
+    r2[e] = bf16r(__fmaf_rn(y, cc, __fmul_rn(x, sn)));
+    ss = __fmaf_rn(r1[e], r1[e], ss);
+    ss = __fmaf_rn(r2[e], r2[e], ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float inv = rsqrtf(__fadd_rn(ss / (float)D, p.eps));
+  const __nv_bfloat16* w = is_q ? p.qw : p.kw;
+  __nv_bfloat16 o1[E], o2[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    o1[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r1[e], inv), __bfloat162float(w[i0 + e])));
+    o2[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r2[e], inv), __bfloat162float(w[HALF + i0 + e])));
+  }
+  auto store = [&](__nv_bfloat16* dst, const __nv_bfloat16* a, const __nv_bfloat16* b) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      dst[i0 + e] = a[e];
+      dst[HALF + i0 + e] = b[e];
+    }
+  };
+  if (is_q) {
+    store(p.q_out + (int64_t)t * p.q_out_row + (int64_t)h * D, o1, o2);
+    return;
+  }
+  const int64_t slot = p.ring_slot[t];
+  const bool ring_ok = slot >= 0 && slot < p.ring_slots;
+  if (!ring_ok && lane == 0) report_error(p.err, DEVERR_BAD_SLOT, 2, (int)slot);
+  const __nv_bfloat16* vsrc = p.v + (int64_t)t * p.v_row + (int64_t)j * D;
+  __nv_bfloat16 va[E], vb[E], vsa[E], vsb[E];
+  const float is = p.inv_scale ? p.inv_scale[j] : 1.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    va[e] = vsrc[i0 + e];
+    vb[e] = vsrc[HALF + i0 + e];
+    vsa[e] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(va[e]), is));
+    vsb[e] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(vb[e]), is));
+  }
+  if (ring_ok) {
+    const int64_t off = (slot * p.Hkv + j) * D;
+    store(p.ring_k + off, o1, o2);
+    store(p.ring_v + off, vsa, vsb);
+  }
+  if (p.src_slot) {
+    const int64_t ss_ = p.src_slot[t];
+    if (ss_ >= 0 && ss_ < p.src_slots) {
+      const int64_t off = (ss_ * p.Hkv + j) * D;
+      store(p.src_k + off, o1, o2);
+      store(p.src_v + off, va, vb);
+    } else if (lane == 0) {
+      report_error(p.err, DEVERR_BAD_SLOT, 2, (int)ss_);
+    }
+  }
+}
+
+struct BlendParams {
+  __nv_bfloat16* pool_k;
+  __nv_bfloat16* pool_v;
+  int64_t num_pages;
+  const int32_t* raw_pages;
+  const int32_t* ring_pages;
+  int64_t ring_stride;
+  const float* alpha;
+  int ppc, Hkv, D;
+  int* err;
+};
+
+// grid (pages_per_chunk, num_seqs, num_layers); one CTA blends one page of one layer.
+__global__ void __launch_bounds__(256) blend_chunk_kernel(const BlendParams p) {
+  const int jp = blockIdx.x, seq = blockIdx.y, layer = blockIdx.z;
+  const int64_t raw = p.raw_pages[(int64_t)seq * p.ppc + jp];
+  const int64_t ring = (int64_t)p.ring_pages[(int64_t)seq * p.ppc + jp] + (int64_t)layer * p.ring_stride;
+  if (raw < 0 || raw >= p.num_pages || ring < 0 || ring >= p.num_pages) {
+    if (threadIdx.x == 0) report_error(p.err, DEVERR_BAD_PAGE, 3, (int)(raw < 0 || raw >= p.num_pages ? raw : ring));
+    return;
+  }
+  const int64_t page_elems = (int64_t)16 * p.Hkv * p.D;
+  const int vecs = (int)(page_elems / 8);
+#pragma unroll 1
+  for (int which = 0; which < 2; ++which) {
+    __nv_bfloat16* pool = which ? p.pool_v : p.pool_k;
+    const uint4* src = reinterpret_cast<const uint4*>(pool + raw * page_elems);
+    uint4* dst = reinterpret_cast<uint4*>(pool + ring * page_elems);
+    for (int vi = threadIdx.x; vi < vecs; vi += blockDim.x) {
+      const int head = (int)(((int64_t)vi * 8 / p.D) % p.Hkv);
+      const float a = p.alpha[layer * p.Hkv + head];
+      const float ia = bf16r(__fsub_rn(1.f, a));
+      uint4 rv = src[vi], gv = dst[vi];
+      uint32_t* r = reinterpret_cast<uint32_t*>(&rv);
+      uint32_t* g = reinterpret_cast<uint32_t*>(&gv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float t1l = bf16r(__fmul_rn(a, bf16_lo(r[e]))), t1h = bf16r(__fmul_rn(a, bf16_hi(r[e])));
+        const float t3l = bf16r(__fmul_rn(ia, bf16_lo(g[e]))), t3h = bf16r(__fmul_rn(ia, bf16_hi(g[e])));
+        g[e] = pack_bf16(__fadd_rn(t1l, t3l), __fadd_rn(t1h, t3h));
+      }
+      dst[vi] = gv;
+    }
+  }
+}
+
+__global__ void build_block_tables_kernel(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc,
+                                          const int32_t* ring_base, int L, int B, int W, int32_t* bt_all) {
+  const int64_t total = (int64_t)L * B * W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % W);
+    const int b = (int)((i / W) % B);
+    const int l = (int)(i / ((int64_t)W * B));
+    const int32_t v = bt[(int64_t)b * bt_stride + c];
+    bt_all[i] = c < nsrc[b] ? v : v + ring_base[l];
+  }
+}
+
+int rope_norm_append(const AppendArgs& a) {
+  if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (a.num_tokens < 0 || a.num_q_heads < 1 || a.num_kv_heads < 1) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.num_tokens == 0) return LKV_OK;
+  if (!a.q || !a.k || !a.v || !a.positions || !a.cos_sin || !a.q_weight || !a.k_weight || !a.q_out ||
+      !a.ring_slot || !a.ring_k || !a.ring_v)
+    return LKV_ERR_INVALID_ARGUMENT;
+  if (a.src_slot && (!a.src_k || !a.src_v)) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.num_tokens > 65535) return LKV_ERR_UNSUPPORTED;  // grid.y limit; callers split larger spans
+  AppendParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(a.q);
+  p.q_row = a.q_row;
+  p.k = static_cast<const __nv_bfloat16*>(a.k);
+  p.k_row = a.k_row;
+  p.v = static_cast<const __nv_bfloat16*>(a.v);
+  p.v_row = a.v_row;
+  p.pos = a.positions;
+  p.cos_sin = static_cast<const __nv_bfloat16*>(a.cos_sin);
+  p.cs_row = a.cos_sin_row;
+  p.max_pos = a.max_position;
+  p.qw = static_cast<const __nv_bfloat16*>(a.q_weight);
+  p.kw = static_cast<const __nv_bfloat16*>(a.k_weight);
+  p.eps = a.eps;
+  p.inv_scale = a.inv_scale;
+  p.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+  p.q_out_row = a.q_out_row;
+  p.ring_slot = a.ring_slot;
+  p.ring_k = static_cast<__nv_bfloat16*>(a.ring_k);
+  p.ring_v = static_cast<__nv_bfloat16*>(a.ring_v);
+  p.ring_slots = a.ring_slots;
+  p.src_slot = a.src_slot;
+  p.src_k = static_cast<__nv_bfloat16*>(a.src_k);
+  p.src_v = static_cast<__nv_bfloat16*>(a.src_v);
+  p.src_slots = a.src_slots;
+  p.T = a.num_tokens;
+  p.Hq = a.num_q_heads;
+  p.Hkv = a.num_kv_heads;
+  p.err = a.error_word;
+  dim3 grid((a.num_q_heads + a.num_kv_heads + 7) / 8, a.num_tokens);
+  cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
+  if (a.head_dim == 128)
+    rope_norm_append_kernel<128><<<grid, 256, 0, stream>>>(p);
+  else
+    rope_norm_append_kernel<64><<<grid, 256, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+int blend_chunk(const BlendArgs& a) {
+  if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (a.num_layers < 0 || a.num_seqs < 0 || a.pages_per_chunk < 0 || a.num_kv_heads < 1)
+    return LKV_ERR_INVALID_ARGUMENT;
+  if (a.num_layers == 0 || a.num_seqs == 0 || a.pages_per_chunk == 0) return LKV_OK;
+  if (!a.pool_k || !a.pool_v || !a.raw_pages || !a.ring_pages || !a.alpha) return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(a.pool_k) & 15) || (reinterpret_cast<uintptr_t>(a.pool_v) & 15))
+    return LKV_ERR_INVALID_ARGUMENT;
+  if (a.num_seqs > 65535 || a.num_layers > 65535) return LKV_ERR_UNSUPPORTED;
+  BlendParams p{};
+  p.pool_k = static_cast<__nv_bfloat16*>(a.pool_k);
+  p.pool_v = static_cast<__nv_bfloat16*>(a.pool_v);
+  p.num_pages = a.num_pages;
+  p.raw_pages = a.raw_pages;
+  p.ring_pages = a.ring_pages;
+  p.ring_stride = a.ring_layer_stride_pages;
+  p.alpha = a.alpha;
+  p.ppc = a.pages_per_chunk;
+  p.Hkv = a.num_kv_heads;
+  p.D = a.head_dim;
+  p.err = a.error_word;
+  dim3 grid(a.pages_per_chunk, a.num_seqs, a.num_layers);
+  blend_chunk_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(a.stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+int build_layer_block_tables(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc, const int32_t* ring_base,
+                             int num_layers, int batch, int width, int32_t* bt_all, cudaStream_t stream) {
+  if (num_layers < 0 || batch < 0 || width < 0) return LKV_ERR_INVALID_ARGUMENT;
+  const int64_t total = (int64_t)num_layers * batch * width;
+  if (total == 0) return LKV_OK;
+  if (!bt || !nsrc || !ring_base || !bt_all) return LKV_ERR_INVALID_ARGUMENT;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
+  build_block_tables_kernel<<<blocks, 256, 0, stream>>>(bt, bt_stride, nsrc, ring_base, num_layers, batch, width,
+                                                        bt_all);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+}  // namespace lkv

@@ -1,0 +1,216 @@
+// extern "C" entry points of liblastkv_b200.so (declared in include/lastkv_b200.h)
+// and the host-side TMA tensor-map encoder.  The driver entry point is looked
+// up through the runtime so the library does not link libcuda directly.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "kernels.h"
+#include "lastkv_b200.h"
+
+namespace lkv {
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+// 4-D map over the pool [num_pages, 16, Hkv, D] (innermost first: D, Hkv, 16,
+// pages), copying one (page, kv head, 64-wide half of D) tile of 16 rows x
+// 128 bytes per load, 128-byte swizzled so ldmatrix reads are bank-conflict free.
+int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, int num_kv_heads, int head_dim) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LKV_ERR_TENSOR_MAP;
+  if (reinterpret_cast<uintptr_t>(pool) & 15) return LKV_ERR_INVALID_ARGUMENT;
+  if (num_pages < 1 || num_pages > (int64_t)0xffffffffLL || num_kv_heads < 1 || num_kv_heads > 256)
+    return LKV_ERR_INVALID_ARGUMENT;
+  cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_kv_heads, 16, (cuuint64_t)num_pages};
+  cuuint64_t strides[3] = {(cuuint64_t)head_dim * 2, (cuuint64_t)num_kv_heads * head_dim * 2,
+                           (cuuint64_t)16 * num_kv_heads * head_dim * 2};
+  cuuint32_t box[4] = {64, 1, 16, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(pool), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LKV_OK : LKV_ERR_TENSOR_MAP;
+}
+
+}  // namespace lkv
+
+extern "C" {
+
+const char* lkv_status_string(int status) {
+  switch (status) {
+    case LKV_OK: return "ok";
+    case LKV_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case LKV_ERR_UNSUPPORTED: return "unsupported shape or configuration";
+    case LKV_ERR_CUDA: return "CUDA runtime error";
+    case LKV_ERR_ARCH: return "device is not an sm_100 GPU";
+    case LKV_ERR_TENSOR_MAP: return "TMA tensor map could not be encoded";
+    case LKV_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    default: return "unknown status";
+  }
+}
+
+int lkv_abi_version(void) { return 100; }
+
+int lkv_check_device(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) return LKV_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) return LKV_ERR_CUDA;
+  return (major == 10 && minor == 0) ? LKV_OK : LKV_ERR_ARCH;
+}
+
+int lkv_read_error_word(const int32_t* error_word, int32_t host_out[4], void* stream) {
+  if (!error_word || !host_out) return LKV_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(host_out, error_word, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return LKV_ERR_CUDA;
+  return cudaStreamSynchronize(s) == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+int lkv_clear_error_word(int32_t* error_word, void* stream) {
+  if (!error_word) return LKV_ERR_INVALID_ARGUMENT;
+  return cudaMemsetAsync(error_word, 0, 4 * sizeof(int32_t), static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? LKV_OK
+             : LKV_ERR_CUDA;
+}
+
+size_t lkv_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int max_pages_per_seq) {
+  return lkv::decode_workspace_bytes(batch, num_q_heads, head_dim, max_pages_per_seq);
+}
+
+int lkv_decode_paged(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v, int64_t num_pages,
+                     const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_k, void* out,
+                     int64_t out_stride_tok, float* lse, const float* out_scale, float* partial_o,
+                     float* partial_lse, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                     int max_pages_per_seq, float softmax_scale, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  lkv::DecodeArgs a{};
+  a.q = q;
+  a.q_stride_tok = q_stride_tok;
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.block_table = block_table;
+  a.block_table_stride = block_table_stride;
+  a.seq_k = seq_k;
+  a.out = out;
+  a.out_stride_tok = out_stride_tok;
+  a.lse = lse;
+  a.out_scale = out_scale;
+  a.partial_o = partial_o;
+  a.partial_lse = partial_lse;
+  a.batch = batch;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.max_pages_per_seq = max_pages_per_seq;
+  a.softmax_scale = softmax_scale;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  a.stream = stream;
+  return lkv::decode_paged(a);
+}
+
+int lkv_decode_plan(int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_pages_per_seq,
+                    size_t workspace_bytes, int partial, int* num_splits, int* num_launches) {
+  return lkv::decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq, workspace_bytes, partial,
+                          num_splits, num_launches);
+}
+
+int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim,
+                       int num_q_heads, const float* out_scale, void* out, float* lse_out, void* stream) {
+  return lkv::merge_partials(o_parts, lse_parts, num_parts, rows, head_dim, num_q_heads, out_scale, out, lse_out,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_row, const void* v, int64_t v_row,
+                         const int64_t* positions, const void* cos_sin, int64_t cos_sin_row, int64_t max_position,
+                         const void* q_weight, const void* k_weight, float eps, const float* inv_scale, void* q_out,
+                         int64_t q_out_row, const int64_t* ring_slot, void* ring_k, void* ring_v, int64_t ring_slots,
+                         const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots, int num_tokens,
+                         int num_q_heads, int num_kv_heads, int head_dim, int32_t* error_word, void* stream) {
+  lkv::AppendArgs a{};
+  a.q = q;
+  a.q_row = q_row;
+  a.k = k;
+  a.k_row = k_row;
+  a.v = v;
+  a.v_row = v_row;
+  a.positions = positions;
+  a.cos_sin = cos_sin;
+  a.cos_sin_row = cos_sin_row;
+  a.max_position = max_position;
+  a.q_weight = q_weight;
+  a.k_weight = k_weight;
+  a.eps = eps;
+  a.inv_scale = inv_scale;
+  a.q_out = q_out;
+  a.q_out_row = q_out_row;
+  a.ring_slot = ring_slot;
+  a.ring_k = ring_k;
+  a.ring_v = ring_v;
+  a.ring_slots = ring_slots;
+  a.src_slot = src_slot;
+  a.src_k = src_k;
+  a.src_v = src_v;
+  a.src_slots = src_slots;
+  a.num_tokens = num_tokens;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.error_word = error_word;
+  a.stream = stream;
+  return lkv::rope_norm_append(a);
+}
+
+int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages, const int32_t* raw_pages,
+                    const int32_t* ring_pages, int64_t ring_layer_stride_pages, const float* alpha, int num_layers,
+                    int num_seqs, int pages_per_chunk, int num_kv_heads, int head_dim, int32_t* error_word,
+                    void* stream) {
+  lkv::BlendArgs a{};
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.raw_pages = raw_pages;
+  a.ring_pages = ring_pages;
+  a.ring_layer_stride_pages = ring_layer_stride_pages;
+  a.alpha = alpha;
+  a.num_layers = num_layers;
+  a.num_seqs = num_seqs;
+  a.pages_per_chunk = pages_per_chunk;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.error_word = error_word;
+  a.stream = stream;
+  return lkv::blend_chunk(a);
+}
+
+int lkv_build_layer_block_tables(const int32_t* block_table, int64_t block_table_stride, const int32_t* nsrc,
+                                 const int32_t* ring_base, int num_layers, int batch, int width, int32_t* bt_all,
+                                 void* stream) {
+  return lkv::build_layer_block_tables(block_table, block_table_stride, nsrc, ring_base, num_layers, batch, width,
+                                       bt_all, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

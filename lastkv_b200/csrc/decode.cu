@@ -1,0 +1,628 @@
+// Split-KV decode over the shared last-layer paged K/V pool (sm_100a).
+//
+// One CTA = (sequence b, KV head hk, split).  A producer warp streams the
+// split's pages with TMA (4-D tensor map over [pages, 16, Hkv, D], one
+// 16 x 64 half-tile per copy, 128-byte swizzle) into a STAGES-deep ring of
+// shared-memory stages holding NW pages each; NW consumer warps each take one
+// page of a stage.  All query heads of the GQA group are folded into one MMA
+// tile with the keys as the M dimension:
+//     S^T[16 keys, 8 heads] = K[16, D] * Q^T[D, 8]           (mma m16n8k16)
+//     O^T[D, 8 heads]      += V^T[D, 16] * P^T[16 keys, 8]    (mma m16n8k16)
+// P^T is produced from the S^T accumulators with movmatrix (8x8 transposes),
+// so probabilities never leave registers.  The online softmax keeps a running
+// max per head (4-lane groups share a head pair) and per-thread partial sums.
+// At the end the NW warps merge in shared memory and the CTA writes either the
+// final bf16 output (single split) or a normalised fp32 partial + log2 LSE.
+// A second small kernel merges the splits (and serves as the context-parallel
+// combine).
+//
+// Reference semantics: the merged attention call of the vLLM fast path
+// (vllm/src/lastkv/vllm/backends/rmarin_flashinfer/fastpath.py:643-650; FA3
+// varlen with block_table / seqused_k, causal with bottom-right alignment,
+// which for one query token means "all seq_k keys") followed by head_scale_
+// (fused_qkv.py:140-155), folded here into the epilogue.
+
+#include <math.h>
+
+#include <algorithm>
+#include <climits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lkv {
+
+constexpr int PAGE = 16;
+
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  int64_t q_stride_tok;
+  const int32_t* bt;
+  int64_t bt_stride;
+  const int32_t* seq_k;
+  __nv_bfloat16* out;
+  int64_t out_stride_tok;
+  float* lse;              // final natural-log LSE [B, Hq] or null
+  const float* out_scale;  // [Hq] or null
+  float* part_o;           // [B*Hq, S, D] normalised partials (S > 1 or partial mode)
+  float* part_lse;         // [B*Hq, S] log2 units
+  int* err;
+  int B, Hq, Hkv, W, S;
+  int64_t num_pages;
+  float scale_log2;  // softmax_scale * log2(e)
+  int final_out;     // 1: this kernel writes `out` (S == 1 and not partial mode)
+};
+
+template <int D, int NW, int STAGES>
+struct DecodeCfg {
+  static constexpr int HALVES = D / 64;
+  static constexpr int TILE_BYTES = PAGE * 128;               // 16 rows x 64 bf16
+  static constexpr int PAGE_BYTES = 2 * HALVES * TILE_BYTES;  // K and V of one page, one head
+  static constexpr int STAGE_BYTES = NW * PAGE_BYTES;
+  static constexpr int OSTRIDE = D + 4;                       // padded fp32 row of the merge area
+  static constexpr int MERGE_BYTES = NW * 8 * (OSTRIDE + 2) * 4;
+  static constexpr int DATA_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + 2 * STAGES * 8 + 16;  // + failure flag
+  static_assert(MERGE_BYTES <= DATA_BYTES, "merge area must fit in the stage ring");
+};
+
+__device__ __forceinline__ float warp_max_g(float v) {
+  // reduce over the 8 lanes sharing (lane & 3)
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum_g(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 16);
+  return v;
+}
+
+template <int D, int GROUP, int NW, int STAGES>
+__global__ void __launch_bounds__((NW + 1) * 32)
+    decode_splitkv_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                          const DecodeParams p) {
+  using Cfg = DecodeCfg<D, NW, STAGES>;
+  constexpr int KT = D / 16;  // 16-wide d tiles
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::DATA_BYTES);
+  uint64_t* empty = full + STAGES;
+
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int n = max(0, p.seq_k[b]);
+  const int npages = min((n + PAGE - 1) / PAGE, p.W);
+  const int per = (npages + p.S - 1) / p.S;
+  const int p0 = min(npages, split * per);
+  const int p1 = min(npages, p0 + per);
+  const int n_iter = (p1 - p0 + NW - 1) / NW;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    *reinterpret_cast<int*>(empty + STAGES) = 0;  // CTA failure flag
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_iter > 0) {
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      const uint64_t policy = policy_evict_first();
+      const int32_t* row = p.bt + (int64_t)b * p.bt_stride;
+      for (int it = 0; it < n_iter; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u)) {
+          report_error(p.err, DEVERR_WAIT_TIMEOUT, 1, it);
+          break;
+        }
+        const int first = p0 + it * NW;
+        const int cnt = min(NW, p1 - first);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * Cfg::PAGE_BYTES));
+        uint8_t* dst = smem + s * Cfg::STAGE_BYTES;
+        for (int w = 0; w < cnt; ++w) {
+          const int pid = row[first + w];
+          if (pid < 0 || (int64_t)pid >= p.num_pages) report_error(p.err, DEVERR_BAD_PAGE, 1, pid);
+          // An out-of-range page reads as zeros (TMA bounds-fills), never faults.
+#pragma unroll
+          for (int h = 0; h < Cfg::HALVES; ++h) {
+            tma_load_4d_hint(dst + w * Cfg::PAGE_BYTES + h * Cfg::TILE_BYTES, &tmk, &full[s], h * 64, hk, 0, pid,
+                             policy);
+            tma_load_4d_hint(dst + w * Cfg::PAGE_BYTES + (Cfg::HALVES + h) * Cfg::TILE_BYTES, &tmv, &full[s],
+                             h * 64, hk, 0, pid, policy);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g = lane >> 2, c = lane & 3;
+  uint32_t qf[KT][2];
+  {
+    const bool valid = g < GROUP;
+    const __nv_bfloat16* qrow = p.q + (int64_t)b * p.q_stride_tok + (int64_t)(hk * GROUP + (valid ? g : 0)) * D;
+#pragma unroll
+    for (int j = 0; j < KT; ++j) {
+      const int d0 = 16 * j + 2 * c;
+      qf[j][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
+      qf[j][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
+    }
+  }
+  float o[KT][4];
+#pragma unroll
+  for (int i = 0; i < KT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  // ldmatrix source rows/chunks (see the fragment derivation in the header comment)
+  const uint32_t k_row = (lane & 7) + ((lane >> 3) & 1) * 8, k_chunk_hi = lane >> 4;
+  const uint32_t v_row = (lane & 7) + (lane >> 4) * 8, v_chunk_hi = (lane >> 3) & 1;
+
+  bool failed = false;
+  for (int it = 0; it < n_iter; ++it) {
+    const int s = it % STAGES;
+    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+    if (!mbar_wait(&full[s], ph)) {
+      report_error(p.err, DEVERR_WAIT_TIMEOUT, 1, 1000000 + it);
+      failed = true;
+      break;
+    }
+    const int page_idx = p0 + it * NW + warp;
+    if (page_idx < p1) {
+      uint8_t* kt = smem + s * Cfg::STAGE_BYTES + warp * Cfg::PAGE_BYTES;
+      uint8_t* vt = kt + Cfg::HALVES * Cfg::TILE_BYTES;
+      const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < KT; ++j) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(a0, a1, a2, a3,
+                    kbase + (j >> 2) * Cfg::TILE_BYTES + swz128(k_row, 2 * (j & 3) + k_chunk_hi));
+        mma_bf16_16816(sc, a0, a1, a2, a3, qf[j][0], qf[j][1]);
+      }
+      const int key0 = page_idx * PAGE;
+      const int valid_rows = n - key0;  // >= 1
+      const bool r0 = g < valid_rows, r1 = g + 8 < valid_rows;
+      const float s00 = r0 ? sc[0] * p.scale_log2 : -INFINITY;
+      const float s01 = r0 ? sc[1] * p.scale_log2 : -INFINITY;
+      const float s10 = r1 ? sc[2] * p.scale_log2 : -INFINITY;
+      const float s11 = r1 ? sc[3] * p.scale_log2 : -INFINITY;
+      const float mn0 = fmaxf(m0, warp_max_g(fmaxf(s00, s10)));
+      const float mn1 = fmaxf(m1, warp_max_g(fmaxf(s01, s11)));
+      const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      const float p00 = exp2f(s00 - mn0), p01 = exp2f(s01 - mn1);
+      const float p10 = exp2f(s10 - mn0), p11 = exp2f(s11 - mn1);
+      l0 = l0 * al0 + p00 + p10;
+      l1 = l1 * al1 + p01 + p11;
+#pragma unroll
+      for (int i = 0; i < KT; ++i) {
+        o[i][0] *= al0;
+        o[i][1] *= al1;
+        o[i][2] *= al0;
+        o[i][3] *= al1;
+      }
+      const uint32_t pb0 = movmatrix_trans(pack_bf16(p00, p01));
+      const uint32_t pb1 = movmatrix_trans(pack_bf16(p10, p11));
+      if (valid_rows < PAGE) {
+        // Rows past the sequence end carry P = 0, but 0 * NaN would still poison
+        // O; clear them (a swizzled row stays inside its own 128 bytes).
+        const int nz = (PAGE - valid_rows) * 8 * Cfg::HALVES;
+        for (int e = lane; e < nz; e += 32) {
+          const int hv = e / ((PAGE - valid_rows) * 8);
+          const int rem = e % ((PAGE - valid_rows) * 8);
+          const int r = valid_rows + rem / 8;
+          *reinterpret_cast<uint4*>(vt + hv * Cfg::TILE_BYTES + r * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int i = 0; i < KT; ++i) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(a0, a1, a2, a3,
+                          vbase + (i >> 2) * Cfg::TILE_BYTES + swz128(v_row, 2 * (i & 3) + v_chunk_hi));
+        mma_bf16_16816(o[i], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---------------------------------------------------------------- merge
+  l0 = warp_sum_g(l0);
+  l1 = warp_sum_g(l1);
+  volatile int* fail_flag = reinterpret_cast<volatile int*>(empty + STAGES);
+  if (failed && lane == 0) *fail_flag = 1;
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));  // all consumer warps are done with the stages
+  if (*fail_flag) return;                          // uniform across the consumer warps
+  float* mo = reinterpret_cast<float*>(smem);                       // [NW][8][OSTRIDE]
+  float* mm = mo + NW * 8 * Cfg::OSTRIDE;                           // [NW][8]
+  float* ml = mm + NW * 8;                                          // [NW][8]
+  {
+    float* w0 = mo + (warp * 8 + 2 * c) * Cfg::OSTRIDE;
+    float* w1 = w0 + Cfg::OSTRIDE;
+#pragma unroll
+    for (int i = 0; i < KT; ++i) {
+      w0[16 * i + g] = o[i][0];
+      w1[16 * i + g] = o[i][1];
+      w0[16 * i + g + 8] = o[i][2];
+      w1[16 * i + g + 8] = o[i][3];
+    }
+    if (g == 0) {
+      mm[warp * 8 + 2 * c] = m0;
+      mm[warp * 8 + 2 * c + 1] = m1;
+      ml[warp * 8 + 2 * c] = l0;
+      ml[warp * 8 + 2 * c + 1] = l1;
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  for (int idx = threadIdx.x; idx < GROUP * D; idx += NW * 32) {
+    const int h = idx / D, d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, mm[w * 8 + h]);
+    float L = 0.f, acc = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float f = exp2f(mm[w * 8 + h] - M);
+        L += ml[w * 8 + h] * f;
+        acc += mo[(w * 8 + h) * Cfg::OSTRIDE + d] * f;
+      }
+    }
+    const float val = L > 0.f ? acc / L : 0.f;
+    const int hq = hk * GROUP + h;
+    if (p.final_out) {
+      const float sc = p.out_scale ? p.out_scale[hq] : 1.f;
+      p.out[(int64_t)b * p.out_stride_tok + (int64_t)hq * D + d] = __float2bfloat16_rn(val * sc);
+      if (p.lse && d == 0) p.lse[(int64_t)b * p.Hq + hq] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+    } else {
+      const int64_t rowi = ((int64_t)b * p.Hq + hq) * p.S + split;
+      p.part_o[rowi * D + d] = val;
+      if (d == 0) p.part_lse[rowi] = L > 0.f ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ merge
+// One warp per output row (token, head): merge `parts` normalised partials.
+// part_o: [rows, S, D] with row stride S*D when split_major == 0 (decode
+// splits), or [S, rows, D] when split_major == 1 (context-parallel ranks).
+struct MergeParams {
+  const float* part_o;
+  const float* part_lse;
+  int S;
+  int64_t rows;
+  int split_major;
+  int lse_log2;  // 1: part_lse in log2 units, 0: natural log
+  int Hq;
+  const float* out_scale;
+  __nv_bfloat16* out;  // bf16 [rows, D] with row index -> (tok = row / Hq, h = row % Hq)
+  int64_t out_stride_tok;
+  float* lse_out;        // natural log [rows] or null
+  float* out_f32;        // fp32 normalised [rows, D] instead of bf16 (partial of partials) or null
+  float* out_lse_f32;    // natural log [rows] for out_f32 mode
+};
+
+template <int D>
+__global__ void __launch_bounds__(128) merge_partials_kernel(const MergeParams p) {
+  constexpr int PER = D / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  if (row >= p.rows) return;
+  const float to2 = p.lse_log2 ? 1.f : 1.4426950408889634f;
+  auto lse_at = [&](int s) -> float {
+    const int64_t i = p.split_major ? (int64_t)s * p.rows + row : row * p.S + s;
+    return p.part_lse[i] * to2;
+  };
+  auto o_at = [&](int s) -> const float* {
+    const int64_t i = p.split_major ? (int64_t)s * p.rows + row : row * p.S + s;
+    return p.part_o + i * D;
+  };
+  float M = -INFINITY;
+  for (int s = lane; s < p.S; s += 32) M = fmaxf(M, lse_at(s));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float acc[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+  float L = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < p.S; ++s) {
+      const float ls = lse_at(s);
+      if (ls == -INFINITY) continue;
+      const float w = exp2f(ls - M);
+      L += w;
+      const float* src = o_at(s) + lane * PER;
+      if constexpr (PER == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        acc[0] += w * v.x;
+        acc[1] += w * v.y;
+        acc[2] += w * v.z;
+        acc[3] += w * v.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) acc[e] += w * src[e];
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const float lse2 = L > 0.f ? M + log2f(L) : -INFINITY;
+  const int h = (int)(row % p.Hq);
+  const int64_t tok = row / p.Hq;
+  if (p.out_f32) {
+#pragma unroll
+    for (int e = 0; e < PER; ++e) p.out_f32[row * D + lane * PER + e] = acc[e] * inv;
+    if (lane == 0) p.out_lse_f32[row] = lse2 * 0.6931471805599453f;
+    return;
+  }
+  const float sc = (p.out_scale ? p.out_scale[h] : 1.f) * inv;
+  __nv_bfloat16* dst = p.out + tok * p.out_stride_tok + (int64_t)h * D + lane * PER;
+#pragma unroll
+  for (int e = 0; e < PER; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(acc[e] * sc, acc[e + 1] * sc);
+  if (p.lse_out && lane == 0) p.lse_out[row] = lse2 * 0.6931471805599453f;
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+constexpr int kNW = 4;
+constexpr int kMaxSplits = 32;
+
+struct DevInfo {
+  int sms = 0;
+  int occ[2][4] = {{0}};  // [D==128][log2 GROUP]
+  bool attr_done[2][4] = {{false}};
+};
+DevInfo g_dev[64];
+
+template <int D, int GROUP, int STAGES>
+int prepare_kernel(int dev) {
+  using Cfg = DecodeCfg<D, kNW, STAGES>;
+  auto kern = decode_splitkv_kernel<D, GROUP, kNW, STAGES>;
+  const int di = D == 128, gi = GROUP == 1 ? 0 : GROUP == 2 ? 1 : GROUP == 4 ? 2 : 3;
+  DevInfo& info = g_dev[dev];
+  if (!info.attr_done[di][gi]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess)
+      return -1;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kNW + 1) * 32, Cfg::SMEM_BYTES) != cudaSuccess)
+      return -1;
+    info.occ[di][gi] = occ > 0 ? occ : 1;
+    info.attr_done[di][gi] = true;
+  }
+  return info.occ[di][gi];
+}
+
+// Split count: minimise (waves) x (pages per CTA + pipeline fill), the time of
+// a grid of equal CTAs, so the last wave is as full as possible.
+int choose_splits(int units, int max_pages, int slots) {
+  if (max_pages <= 0) return 1;
+  const int fill = 6;  // pipeline fill + merge, in page-times
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  const int smax = std::min(kMaxSplits, std::max(1, max_pages / 4));
+  for (int s = 1; s <= smax; ++s) {
+    const int64_t ctas = (int64_t)units * s;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const int64_t per = (max_pages + s - 1) / s;
+    const int64_t cost = waves * (per + fill) + (s > 1 ? 2 : 0);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+template <int D, int GROUP, int STAGES>
+int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams prm, int max_pages, int smax, int dev,
+                 cudaStream_t stream, bool partial_mode, float* part_o_user, float* part_lse_user) {
+  using Cfg = DecodeCfg<D, kNW, STAGES>;
+  const int occ = prepare_kernel<D, GROUP, STAGES>(dev);
+  if (occ < 0) return LKV_ERR_CUDA;
+  const int slots = g_dev[dev].sms * occ;
+  const int S = std::min(smax, choose_splits(prm.B * prm.Hkv, max_pages, slots));
+  const int64_t rows = (int64_t)prm.B * prm.Hq;
+  prm.S = S;
+  prm.final_out = (S == 1 && !partial_mode) ? 1 : 0;
+  dim3 grid(S, prm.Hkv, prm.B);
+  decode_splitkv_kernel<D, GROUP, kNW, STAGES><<<grid, (kNW + 1) * 32, Cfg::SMEM_BYTES, stream>>>(tmk, tmv, prm);
+  if (cudaGetLastError() != cudaSuccess) return LKV_ERR_CUDA;
+  if (prm.final_out) return LKV_OK;
+  MergeParams mp{};
+  mp.part_o = prm.part_o;
+  mp.part_lse = prm.part_lse;
+  mp.S = S;
+  mp.rows = rows;
+  mp.split_major = 0;
+  mp.lse_log2 = 1;
+  mp.Hq = prm.Hq;
+  mp.out_scale = prm.out_scale;
+  mp.out = prm.out;
+  mp.out_stride_tok = prm.out_stride_tok;
+  mp.lse_out = prm.lse;
+  if (partial_mode) {
+    mp.out_f32 = part_o_user;
+    mp.out_lse_f32 = part_lse_user;
+  }
+  merge_partials_kernel<D><<<(unsigned)((rows + 3) / 4), 128, 0, stream>>>(mp);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+}  // namespace
+
+size_t decode_workspace_bytes(int batch, int hq, int d, int max_pages) {
+  const int64_t rows = (int64_t)std::max(batch, 0) * std::max(hq, 0);
+  const int s = std::min(kMaxSplits, std::max(1, max_pages / 4));
+  return kWorkspaceHeader + (size_t)rows * s * (size_t)(std::max(d, 64) + 1) * sizeof(float) + 256;
+}
+
+int decode_paged(const DecodeArgs& a) {
+  if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (a.num_kv_heads <= 0 || a.num_q_heads <= 0 || a.num_q_heads % a.num_kv_heads) return LKV_ERR_INVALID_ARGUMENT;
+  const int group = a.num_q_heads / a.num_kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return LKV_ERR_UNSUPPORTED;
+  if (a.batch < 0 || a.max_pages_per_seq < 0) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.batch == 0) return LKV_OK;
+  if (!a.q || !a.pool_k || !a.pool_v || !a.block_table || !a.seq_k) return LKV_ERR_INVALID_ARGUMENT;
+  const bool partial_mode = a.partial_o != nullptr;
+  if (partial_mode != (a.partial_lse != nullptr)) return LKV_ERR_INVALID_ARGUMENT;
+  if (!partial_mode && !a.out) return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(a.q) & 3) || (a.q_stride_tok & 1)) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.out && ((reinterpret_cast<uintptr_t>(a.out) & 3) || (a.out_stride_tok & 1))) return LKV_ERR_INVALID_ARGUMENT;
+  if (!a.workspace || a.workspace_bytes < kWorkspaceHeader + 256) return LKV_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(a.workspace) & 255) return LKV_ERR_WORKSPACE;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LKV_ERR_CUDA;
+  if (g_dev[dev].sms == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return LKV_ERR_CUDA;
+    g_dev[dev].sms = sms;
+  }
+
+  CUtensorMap tmk, tmv;
+  int st = make_pool_tensor_map(&tmk, a.pool_k, a.num_pages, a.num_kv_heads, a.head_dim);
+  if (st != LKV_OK) return st;
+  st = make_pool_tensor_map(&tmv, a.pool_v, a.num_pages, a.num_kv_heads, a.head_dim);
+  if (st != LKV_OK) return st;
+
+  DecodeParams prm{};
+  prm.q = static_cast<const __nv_bfloat16*>(a.q);
+  prm.q_stride_tok = a.q_stride_tok;
+  prm.bt = a.block_table;
+  prm.bt_stride = a.block_table_stride;
+  prm.seq_k = a.seq_k;
+  prm.out = static_cast<__nv_bfloat16*>(a.out);
+  prm.out_stride_tok = a.out_stride_tok;
+  prm.lse = a.lse;
+  prm.out_scale = a.out_scale;
+  prm.err = static_cast<int*>(a.workspace);
+  prm.B = a.batch;
+  prm.Hq = a.num_q_heads;
+  prm.Hkv = a.num_kv_heads;
+  prm.W = a.max_pages_per_seq;
+  prm.num_pages = a.num_pages;
+  prm.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+
+  // Workspace after the error header: lse [rows * smax] (256-aligned), then o [rows * smax * D].
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace) + kWorkspaceHeader;
+  const size_t ws_avail = a.workspace_bytes - kWorkspaceHeader;
+  const int64_t rows = (int64_t)a.batch * a.num_q_heads;
+  const size_t per_split = (size_t)rows * (a.head_dim + 1) * sizeof(float) + 256;
+  const int smax = (int)std::min<size_t>(kMaxSplits, ws_avail / per_split);
+  if (smax < 1 && (partial_mode || a.max_pages_per_seq > 0)) return LKV_ERR_WORKSPACE;
+  prm.part_lse = reinterpret_cast<float*>(ws);
+  prm.part_o = reinterpret_cast<float*>(ws + (((size_t)rows * std::max(smax, 1) * sizeof(float) + 255) & ~size_t(255)));
+
+  cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
+#define LKV_LAUNCH(DD, GG, SS) \
+  return launch_group<DD, GG, SS>(tmk, tmv, prm, a.max_pages_per_seq, std::max(smax, 1), dev, stream, \
+                                  partial_mode, a.partial_o, a.partial_lse)
+  if (a.head_dim == 128) {
+    switch (group) {
+      case 1: LKV_LAUNCH(128, 1, 3);
+      case 2: LKV_LAUNCH(128, 2, 3);
+      case 4: LKV_LAUNCH(128, 4, 3);
+      default: LKV_LAUNCH(128, 8, 3);
+    }
+  } else {
+    switch (group) {
+      case 1: LKV_LAUNCH(64, 1, 4);
+      case 2: LKV_LAUNCH(64, 2, 4);
+      case 4: LKV_LAUNCH(64, 4, 4);
+      default: LKV_LAUNCH(64, 8, 4);
+    }
+  }
+#undef LKV_LAUNCH
+}
+
+int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspace_bytes, int partial, int* splits,
+                int* launches) {
+  if (!splits || !launches) return LKV_ERR_INVALID_ARGUMENT;
+  if ((d != 64 && d != 128) || hkv < 1 || hq % hkv) return LKV_ERR_UNSUPPORTED;
+  const int group = hq / hkv;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return LKV_ERR_UNSUPPORTED;
+  if (batch <= 0) {
+    *splits = 0;
+    *launches = 0;
+    return LKV_OK;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LKV_ERR_CUDA;
+  if (g_dev[dev].sms == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return LKV_ERR_CUDA;
+    g_dev[dev].sms = sms;
+  }
+  int occ = -1;
+#define LKV_OCC(DD, GG, SS) occ = prepare_kernel<DD, GG, SS>(dev)
+  if (d == 128) {
+    switch (group) {
+      case 1: LKV_OCC(128, 1, 3); break;
+      case 2: LKV_OCC(128, 2, 3); break;
+      case 4: LKV_OCC(128, 4, 3); break;
+      default: LKV_OCC(128, 8, 3); break;
+    }
+  } else {
+    switch (group) {
+      case 1: LKV_OCC(64, 1, 4); break;
+      case 2: LKV_OCC(64, 2, 4); break;
+      case 4: LKV_OCC(64, 4, 4); break;
+      default: LKV_OCC(64, 8, 4); break;
+    }
+  }
+#undef LKV_OCC
+  if (occ < 0) return LKV_ERR_CUDA;
+  const int64_t rows = (int64_t)batch * hq;
+  const size_t avail = workspace_bytes > kWorkspaceHeader ? workspace_bytes - kWorkspaceHeader : 0;
+  const int smax = (int)std::min<size_t>(kMaxSplits, avail / ((size_t)rows * (d + 1) * sizeof(float) + 256));
+  const int S = std::min(std::max(smax, 1), choose_splits(batch * hkv, max_pages, g_dev[dev].sms * occ));
+  *splits = S;
+  *launches = (S == 1 && !partial) ? 1 : 2;
+  return LKV_OK;
+}
+
+int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim, int hq,
+                   const float* out_scale, void* out, float* lse_out, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (num_parts < 1 || rows < 0 || hq < 1 || rows % hq) return LKV_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return LKV_OK;
+  if (!o_parts || !lse_parts || !out) return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(o_parts) & 15) || (reinterpret_cast<uintptr_t>(out) & 3))
+    return LKV_ERR_INVALID_ARGUMENT;
+  MergeParams mp{};
+  mp.part_o = o_parts;
+  mp.part_lse = lse_parts;
+  mp.S = num_parts;
+  mp.rows = rows;
+  mp.split_major = 1;
+  mp.lse_log2 = 0;
+  mp.Hq = hq;
+  mp.out_scale = out_scale;
+  mp.out = static_cast<__nv_bfloat16*>(out);
+  mp.out_stride_tok = (int64_t)hq * head_dim;
+  mp.lse_out = lse_out;
+  const unsigned blocks = (unsigned)((rows + 3) / 4);
+  if (head_dim == 128)
+    merge_partials_kernel<128><<<blocks, 128, 0, stream>>>(mp);
+  else
+    merge_partials_kernel<64><<<blocks, 128, 0, stream>>>(mp);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+}  // namespace lkv

@@ -1,0 +1,94 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernel files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace lkv {
+
+// Bytes reserved at the start of every workspace: the int32[4] error word,
+// padded so the partial buffers after it stay 256-byte aligned.
+constexpr size_t kWorkspaceHeader = 256;
+
+int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, int num_kv_heads, int head_dim);
+
+struct DecodeArgs {
+  const void* q;
+  int64_t q_stride_tok;
+  const void* pool_k;
+  const void* pool_v;
+  int64_t num_pages;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  const int32_t* seq_k;
+  void* out;
+  int64_t out_stride_tok;
+  float* lse;
+  const float* out_scale;
+  float* partial_o;
+  float* partial_lse;
+  int batch, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq;
+  float softmax_scale;
+  void* workspace;
+  size_t workspace_bytes;
+  void* stream;
+};
+
+size_t decode_workspace_bytes(int batch, int hq, int d, int max_pages);
+int decode_paged(const DecodeArgs& a);
+int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspace_bytes, int partial, int* splits,
+                int* launches);
+int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim, int hq,
+                   const float* out_scale, void* out, float* lse_out, cudaStream_t stream);
+
+struct AppendArgs {
+  const void* q;
+  int64_t q_row;
+  const void* k;
+  int64_t k_row;
+  const void* v;
+  int64_t v_row;
+  const int64_t* positions;
+  const void* cos_sin;
+  int64_t cos_sin_row;
+  int64_t max_position;
+  const void* q_weight;
+  const void* k_weight;
+  float eps;
+  const float* inv_scale;
+  void* q_out;
+  int64_t q_out_row;
+  const int64_t* ring_slot;
+  void* ring_k;
+  void* ring_v;
+  int64_t ring_slots;
+  const int64_t* src_slot;
+  void* src_k;
+  void* src_v;
+  int64_t src_slots;
+  int num_tokens, num_q_heads, num_kv_heads, head_dim;
+  int32_t* error_word;
+  void* stream;
+};
+int rope_norm_append(const AppendArgs& a);
+
+struct BlendArgs {
+  void* pool_k;
+  void* pool_v;
+  int64_t num_pages;
+  const int32_t* raw_pages;
+  const int32_t* ring_pages;
+  int64_t ring_layer_stride_pages;
+  const float* alpha;
+  int num_layers, num_seqs, pages_per_chunk, num_kv_heads, head_dim;
+  int32_t* error_word;
+  void* stream;
+};
+int blend_chunk(const BlendArgs& a);
+
+int build_layer_block_tables(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc, const int32_t* ring_base,
+                             int num_layers, int batch, int width, int32_t* bt_all, cudaStream_t stream);
+
+}  // namespace lkv

@@ -1,0 +1,200 @@
+"""Torch-facing wrappers of the CUDA kernels (device tensors in, device tensors out).
+
+Every function validates shapes/dtypes on the host, passes raw pointers to the
+C ABI on the current torch stream and raises ``RMarinBackendContractError`` on
+any nonzero status.  None of them allocates inside a CUDA-graph capture when
+the caller passes ``out``/``workspace`` buffers.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _capi
+from .contract import PAGE_SIZE, RMarinBackendContractError, require_heads
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RMarinBackendContractError(msg)
+
+
+def _check_pool(pool_k, pool_v):
+    _require(pool_k.is_cuda and pool_v.is_cuda, "pools must be CUDA tensors")
+    _require(pool_k.dtype == torch.bfloat16 and pool_v.dtype == torch.bfloat16, "pools must be bf16")
+    _require(pool_k.dim() == 4 and pool_k.shape == pool_v.shape, "pools must be [pages, 16, Hkv, D] and equal")
+    _require(pool_k.shape[1] == PAGE_SIZE, f"page size must be {PAGE_SIZE}")
+    _require(pool_k.is_contiguous() and pool_v.is_contiguous(), "pools must be contiguous")
+
+
+class Workspace:
+    """Caller-owned scratch for the split-KV partials (+ the int32[4] error word).
+
+    Allocate once (outside graph capture) for the largest batch / context and
+    reuse it; ``error()`` reads the device-side error word (synchronises).
+    """
+
+    def __init__(self, nbytes: int, device=None):
+        self.buf = torch.zeros(int(nbytes) + 256, dtype=torch.uint8, device=device or "cuda")
+        self.nbytes = int(nbytes)
+
+    @classmethod
+    def for_decode(cls, batch: int, num_q_heads: int, head_dim: int, max_pages: int, device=None):
+        lib = _capi.lib()
+        return cls(lib.lkv_decode_workspace_bytes(batch, num_q_heads, head_dim, max_pages), device)
+
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def error(self) -> list[int]:
+        out = (_capi.I32 * 4)()
+        _capi.check(_capi.lib().lkv_read_error_word(self.ptr(), out, _stream()), "lkv_read_error_word")
+        return list(out)
+
+    def clear_error(self) -> None:
+        _capi.check(_capi.lib().lkv_clear_error_word(self.ptr(), _stream()), "lkv_clear_error_word")
+
+
+def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, out=None, lse=None,
+                 out_scale=None, workspace: Workspace | None = None, max_pages: int | None = None,
+                 partial: bool = False):
+    """One query token per sequence against its paged history.
+
+    q [B, Hq, D] bf16 (row-strided views allowed); block_table int32 [B, W];
+    seq_k int32 [B]; out_scale fp32 [Hq] or None.  Returns out [B, Hq, D] bf16,
+    or with ``partial=True`` a pair (o fp32 [B, Hq, D], lse fp32 [B, Hq]) for
+    ``merge_partials``.
+    """
+    _check_pool(pool_k, pool_v)
+    B, Hq, D = q.shape
+    Hkv = pool_k.shape[2]
+    require_heads(Hq, Hkv, D)
+    _require(pool_k.shape[3] == D, "head_dim mismatch between q and pools")
+    _require(q.dtype == torch.bfloat16 and q.stride(2) == 1 and q.stride(1) == D, "q must be bf16 [B, Hq, D] rows")
+    _require(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.stride(1) == 1,
+             "block_table must be int32 [B, W] with unit column stride")
+    _require(block_table.shape[0] >= B and seq_k.dtype == torch.int32 and seq_k.numel() >= B, "seq_k/block_table")
+    W = int(max_pages if max_pages is not None else block_table.shape[1])
+    _require(W <= block_table.shape[1], "max_pages exceeds block_table width")
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    if workspace is None:
+        workspace = Workspace.for_decode(B, Hq, D, W, device=q.device)
+    po = pl = None
+    if partial:
+        po = torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
+        pl = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    elif out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    if out is not None:
+        _require(out.dtype == torch.bfloat16 and out.stride(2) == 1 and out.stride(1) == D, "out layout")
+    if out_scale is not None:
+        _require(out_scale.dtype == torch.float32 and out_scale.numel() == Hq and out_scale.is_contiguous(),
+                 "out_scale must be fp32 [Hq]")
+    st = _capi.lib().lkv_decode_paged(
+        q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0],
+        block_table.data_ptr(), block_table.stride(0), seq_k.data_ptr(),
+        _ptr(out), out.stride(0) if out is not None else 0, _ptr(lse), _ptr(out_scale), _ptr(po), _ptr(pl),
+        B, Hq, Hkv, D, W, float(softmax_scale), workspace.ptr(), workspace.nbytes, _stream())
+    _capi.check(st, "lkv_decode_paged")
+    return (po, pl) if partial else out
+
+
+def decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages, workspace: Workspace, partial=False):
+    """(splits, kernel launches) lkv_decode_paged will use for this shape on the current device."""
+    import ctypes
+
+    s, n = ctypes.c_int(0), ctypes.c_int(0)
+    _capi.check(_capi.lib().lkv_decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages,
+                                            workspace.nbytes, int(partial), ctypes.byref(s), ctypes.byref(n)),
+                "lkv_decode_plan")
+    return s.value, n.value
+
+
+def merge_partials(o_parts, lse_parts, *, out_scale=None, out=None, lse_out=None):
+    """LSE-merge P partials: o_parts fp32 [P, T, Hq, D], lse_parts fp32 [P, T, Hq]."""
+    P_, T, Hq, D = o_parts.shape
+    _require(o_parts.dtype == torch.float32 and o_parts.is_contiguous(), "o_parts must be contiguous fp32")
+    _require(lse_parts.shape == (P_, T, Hq) and lse_parts.is_contiguous(), "lse_parts must be [P, T, Hq]")
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=o_parts.device)
+    _require(out.is_contiguous() and out.dtype == torch.bfloat16, "out must be contiguous bf16")
+    st = _capi.lib().lkv_merge_partials(o_parts.data_ptr(), lse_parts.data_ptr(), P_, T * Hq, D, Hq,
+                                        _ptr(out_scale), out.data_ptr(), _ptr(lse_out), _stream())
+    _capi.check(st, "lkv_merge_partials")
+    return out
+
+
+def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_scale, ring_slot, ring_k, ring_v,
+                     src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None):
+    """Fused RoPE -> Q/K RMSNorm -> V/s -> paged append for one layer.
+
+    q [T, Hq*D], k/v [T, Hkv*D] bf16 (row-strided views allowed); positions
+    int64 [T]; cos_sin bf16 [max_pos, D]; ring_* / src_* flat token views
+    [slots, Hkv, D] of the pools.  Returns q_out [T, Hq, D].
+    """
+    T = q.shape[0]
+    D = cos_sin.shape[-1]
+    Hq, Hkv = q.shape[-1] // D, k.shape[-1] // D
+    require_heads(Hq, Hkv, D)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require(t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1, f"{name} must be bf16 [T, H*D] rows")
+    _require(positions.dtype == torch.int64 and ring_slot.dtype == torch.int64, "positions/slots must be int64")
+    _require(cos_sin.dtype == torch.bfloat16 and cos_sin.stride(1) == 1, "cos_sin must be bf16 [max_pos, D]")
+    _require(q_weight.dtype == torch.bfloat16 and k_weight.dtype == torch.bfloat16, "norm weights must be bf16")
+    if q_out is None:
+        q_out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
+    top = src_slot is not None
+    st = _capi.lib().lkv_rope_norm_append(
+        q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), positions.data_ptr(),
+        cos_sin.data_ptr(), cos_sin.stride(0), cos_sin.shape[0], q_weight.data_ptr(), k_weight.data_ptr(),
+        float(eps), _ptr(inv_scale), q_out.data_ptr(), q_out.stride(0), ring_slot.data_ptr(),
+        ring_k.data_ptr(), ring_v.data_ptr(), ring_k.shape[0],
+        _ptr(src_slot), _ptr(src_k) if top else None, _ptr(src_v) if top else None,
+        src_k.shape[0] if top else 0, T, Hq, Hkv, D, _ptr(error_word), _stream())
+    _capi.check(st, "lkv_rope_norm_append")
+    return q_out
+
+
+def blend_chunk(pool_k, pool_v, raw_pages, ring_pages, ring_layer_stride: int, alpha, *, error_word=None):
+    """Commit a finished chunk into every layer ring (K and V/s) in place.
+
+    raw_pages / ring_pages int32 [S, C/16]; alpha fp32 [L, Hkv] (bf16-exact).
+    """
+    _check_pool(pool_k, pool_v)
+    S, ppc = raw_pages.shape
+    L, Hkv = alpha.shape
+    _require(ring_pages.shape == raw_pages.shape, "ring_pages must match raw_pages")
+    _require(raw_pages.dtype == torch.int32 and ring_pages.dtype == torch.int32, "page lists must be int32")
+    _require(alpha.dtype == torch.float32 and alpha.is_contiguous(), "alpha must be fp32 [L, Hkv]")
+    st = _capi.lib().lkv_blend_chunk(pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0],
+                                     raw_pages.contiguous().data_ptr(), ring_pages.contiguous().data_ptr(),
+                                     int(ring_layer_stride), alpha.data_ptr(), L, S, ppc, Hkv, pool_k.shape[3],
+                                     _ptr(error_word), _stream())
+    _capi.check(st, "lkv_blend_chunk")
+
+
+def build_layer_block_tables(block_table, nsrc, ring_base, out=None):
+    """bt_all [L, B, W] from [older | layer-relative ring] rows (fastpath.py:422-424)."""
+    B, W = block_table.shape
+    L = ring_base.numel()
+    if out is None:
+        out = torch.empty((L, B, W), dtype=torch.int32, device=block_table.device)
+    st = _capi.lib().lkv_build_layer_block_tables(block_table.data_ptr(), block_table.stride(0), nsrc.data_ptr(),
+                                                  ring_base.data_ptr(), L, B, W, out.data_ptr(), _stream())
+    _capi.check(st, "lkv_build_layer_block_tables")
+    return out
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

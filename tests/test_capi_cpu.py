@@ -1,0 +1,87 @@
+"""CPU checks of the C ABI: the library builds, loads without a GPU driver and
+exports every symbol the public header declares; the product package never
+imports the oracle."""
+
+import ast
+import os
+import subprocess
+
+import pytest
+
+from tests.conftest import ROOT
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from lastkv_b200 import _capi, build
+
+    build.build()
+    return _capi.load()
+
+
+def test_header_symbols_are_exported(lib):
+    from lastkv_b200 import _capi
+
+    declared = _capi.declared_symbols()
+    assert "lkv_decode_paged" in declared and "lkv_rope_norm_append" in declared
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/lastkv_b200.h but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", _capi.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T lkv_" in line}
+    assert exported == set(declared), exported ^ set(declared)
+
+
+def test_library_has_no_driver_link():
+    from lastkv_b200 import _capi
+
+    out = subprocess.run(["readelf", "-d", _capi.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out and "libcudart.so" not in out
+
+
+def test_host_only_entry_points(lib):
+    assert lib.lkv_abi_version() >= 100
+    assert lib.lkv_status_string(0) == b"ok"
+    assert lib.lkv_status_string(6).startswith(b"workspace")
+    small = lib.lkv_decode_workspace_bytes(1, 4, 128, 1)
+    big = lib.lkv_decode_workspace_bytes(64, 32, 128, 512)
+    assert 256 < small < big
+
+
+def test_argument_validation_needs_no_gpu(lib):
+    # unsupported head_dim / GQA group are rejected before any CUDA call
+    st = lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
+                              1, 4, 1, 96, 1, 1.0, None, 0, None)
+    assert st == 2
+    st = lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
+                              1, 12, 1, 128, 1, 1.0, None, 0, None)
+    assert st == 2
+    assert lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
+                                1, 8, 3, 128, 1, 1.0, None, 0, None) == 1
+    # empty batch is a no-op
+    assert lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
+                                0, 8, 8, 128, 1, 1.0, None, 0, None) == 0
+
+
+def test_product_package_never_imports_oracle():
+    pkg = os.path.join(ROOT, "lastkv_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if not f.endswith(".py"):
+                continue
+            tree = ast.parse(open(os.path.join(dirpath, f)).read())
+            for node in ast.walk(tree):
+                names = []
+                if isinstance(node, ast.Import):
+                    names = [a.name for a in node.names]
+                elif isinstance(node, ast.ImportFrom):
+                    names = [node.module or ""]
+                assert not any(n.split(".")[0] == "oracle" for n in names), f"{f} imports the oracle"
+
+
+def test_ops_fail_loudly_without_library(tmp_path, monkeypatch):
+    from lastkv_b200 import _capi
+    from lastkv_b200.contract import RMarinBackendContractError
+
+    monkeypatch.setattr(_capi, "_lib", None)
+    with pytest.raises(RMarinBackendContractError, match="not built"):
+        _capi.load(str(tmp_path / "missing.so"))
