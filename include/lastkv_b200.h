@@ -89,6 +89,34 @@ int lkv_decode_paged(const void* q, int64_t q_stride_tok,
                      int max_pages_per_seq, float softmax_scale,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of lkv_decode_paged.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory - an engine whose
+ * KV-cache pool already holds nearly all of HBM (a side cudaMalloc may fail),
+ * a C-FFI host that can only pass the inputs and outputs it owns, or a loop
+ * that cannot afford cudaMalloc's implicit synchronisation.  Instead of a
+ * caller workspace it uses one static device array of
+ * LKV_NOALLOC_SCRATCH_BYTES inside the library, held on every GPU that loads
+ * the library until the process exits.
+ *  - Same arguments and result as lkv_decode_paged (final bf16 output only),
+ *    without workspace; `error_word` (device int32[4], may be NULL) receives
+ *    the call's device error word.
+ *  - Rejects, with LKV_ERR_WORKSPACE and nothing launched, shapes where
+ *    batch * num_q_heads * (head_dim + 1) * 4 + 512 > LKV_NOALLOC_SCRATCH_BYTES.
+ *  - The first call on a device looks up the array's address with that device
+ *    current; make it before any stream capture.
+ *  - All calls share the array: calls whose GPU work overlaps race; serialise.
+ *  - Allocates nothing (no cudaMalloc / cudaFree). */
+#define LKV_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+int lkv_decode_paged_noalloc(const void* q, int64_t q_stride_tok,
+                             const void* pool_k, const void* pool_v, int64_t num_pages,
+                             const int32_t* block_table, int64_t block_table_stride,
+                             const int32_t* seq_k,
+                             void* out, int64_t out_stride_tok, float* lse, const float* out_scale,
+                             int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                             int max_pages_per_seq, float softmax_scale,
+                             int32_t* error_word, void* stream);
+
 /* Host query: how many KV splits and kernel launches lkv_decode_paged will use
  * for this shape and workspace on the current device (partial != 0 for the
  * partial-output form).  Needs a device; launches nothing. */
