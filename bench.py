@@ -33,16 +33,34 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 CFG = dict(batch=64, q_heads=32, kv_heads=8, head_dim=128, context=8192, page=16, layers=32, chunk=1024)
+# Small case for profiler captures only (268 MiB of K/V per call, still > L2); never a bench line.
+SMALL = dict(batch=8, layers=2)
 METRIC = "decode tokens/s (shared-KV attention, 32 layers)"
 UNIT = "tokens/s"
-ALGO_BYTES = 2 * CFG["batch"] * CFG["kv_heads"] * CFG["context"] * CFG["head_dim"] * 2  # per layer call
+
+
+def algo_bytes() -> int:
+    """K and V bytes one layer call must read: 2 * B * Hkv * N * D * 2."""
+    return 2 * CFG["batch"] * CFG["kv_heads"] * CFG["context"] * CFG["head_dim"] * 2
+
+
+# DRAM read + write bytes of one decode_splitkv launch from one ncu capture of the
+# small case (8 sequences: 268,550,144 read + 5,634,560 written), scaled by the
+# sequences processed (traffic grows in proportion to the pages and partials).
+NCU_SMALL_TRAFFIC = 268_550_144 + 5_634_560
+
+
+def traffic_per_launch() -> int:
+    return NCU_SMALL_TRAFFIC * CFG["batch"] // SMALL["batch"]
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--case", default="config2", choices=["config2", "small"],
+                    help="small: 8 sequences x 2 layers, for ncu captures")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -299,7 +317,7 @@ def run_ours(args):
         peak, peak_src = float(peaks["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         peak, peak_src = 6650.0, "fallback"
-    achieved = ALGO_BYTES / (avg_op_ms * 1e-3) / 1e9
+    achieved = algo_bytes() / (avg_op_ms * 1e-3) / 1e9
     tokens = B * args.steps * world
     line = {
         "metric": METRIC, "value": tokens / (total_ms * 1e-3), "unit": UNIT, "n_gpus": world,
@@ -311,8 +329,9 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_src,
                      "kernel": "decode op = decode_splitkv_kernel + merge_partials_kernel",
-                     "algorithmic_bytes_per_launch": ALGO_BYTES, "avg_launch_ms": avg_op_ms,
-                     "traffic": None},
+                     "algorithmic_bytes_per_launch": algo_bytes(), "avg_launch_ms": avg_op_ms,
+                     "traffic": traffic_per_launch(),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, small case x batch/8"},
         "attn_hbm_gbs": achieved,
         "clocks": clk,
         "gpu_launches": int(args.steps * L * launches_per_call),
@@ -359,6 +378,8 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if args.case == "small":
+        CFG.update(SMALL)
     if args.impl == "reference":
         run_reference(args)
     else:
