@@ -123,6 +123,32 @@ int lkv_decode_paged_noalloc(const void* q, int64_t q_stride_tok,
 int lkv_decode_plan(int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_pages_per_seq,
                     size_t workspace_bytes, int partial, int* num_splits, int* num_launches);
 
+/* ------------------------------------------------------------------ prefill
+ * Varlen (chunked) prefill against the paged history on tcgen05 tensor cores.
+ * Replaces the same merged call as lkv_decode_paged for spans of more than one
+ * token (fastpath.py:643-650 with cu_seqlens_q / max_seqlen_q, causal,
+ * bottom-right aligned) and the masked SDPA of modeling.py:124-146; with
+ * causal = 0 it is the non-causal block attention of the Wan path
+ * (videogen/src/lastkv/videogen/attention.py:9-32).
+ *   q / out      bf16 [total_q, num_q_heads, head_dim] rows (16-byte aligned)
+ *   cu_seqlens_q int32 [batch + 1] query offsets; max_q >= every span length
+ *   seq_k        int32 [batch] keys per sequence (>= its span when causal);
+ *                query i of a span of Lq attends keys [0, seq_k - Lq + i]
+ *   out_scale    fp32 [num_q_heads] or NULL (folds s_l)
+ *   lse          fp32 [total_q, num_q_heads] natural log, or NULL
+ *   error_word   device int32[4] (required) for device-side failures.
+ * Pool slots past a sequence's end inside its last page must hold finite
+ * values (pools are zero-initialised).  head_dim 64 or 128; GQA group in
+ * {1, 2, 4, 8}. */
+int lkv_prefill_paged(const void* q, int64_t q_stride_tok,
+                      const void* pool_k, const void* pool_v, int64_t num_pages,
+                      const int32_t* block_table, int64_t block_table_stride,
+                      const int32_t* seq_k, const int32_t* cu_seqlens_q,
+                      void* out, int64_t out_stride_tok, float* lse, const float* out_scale,
+                      int batch, int total_q, int max_q, int num_q_heads, int num_kv_heads,
+                      int head_dim, int max_pages_per_seq, int causal, float softmax_scale,
+                      int32_t* error_word, void* stream);
+
 /* ------------------------------------------------------------------ merge
  * Exact log-sum-exp merge of `num_parts` attention partials over disjoint key
  * sets (flashinfer cascade.merge_state / vLLM merge_attn_states, used at

@@ -44,9 +44,8 @@ _SIGNATURES = {
                                    P, P, P, I64, P, P, P, I64, I32, I32, I32, I32, P, P]),
     "lkv_blend_chunk": (I32, [P, P, I64, P, P, I64, P, I32, I32, I32, I32, I32, P, P]),
     "lkv_build_layer_block_tables": (I32, [P, I64, P, P, I32, I32, I32, P, P]),
-    "lkv_prefill_workspace_bytes": (SZ, [I32, I32, I32, I32]),
     "lkv_prefill_paged": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
-                                I32, I32, I32, I32, I32, I32, I32, I32, F32, P, SZ, P]),
+                                I32, I32, I32, I32, I32, I32, I32, I32, F32, P, P]),
 }
 
 

@@ -54,6 +54,25 @@ int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, 
   return r == CUDA_SUCCESS ? LKV_OK : LKV_ERR_TENSOR_MAP;
 }
 
+// 3-D map over q [total_q, Hq, D] (innermost first: D, Hq, tokens), copying a
+// (64-wide half of D) x GROUP heads x (128 / GROUP) tokens box: 128 rows of
+// 128 bytes, row = token * GROUP + head, 128-byte swizzled (a K-major UMMA tile).
+int make_query_tensor_map(CUtensorMap* map, const void* q, int64_t total_q, int64_t q_stride_tok, int num_q_heads,
+                          int head_dim, int group) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LKV_ERR_TENSOR_MAP;
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || total_q < 1 || total_q > (int64_t)0x7fffffff) return LKV_ERR_INVALID_ARGUMENT;
+  if (q_stride_tok < (int64_t)num_q_heads * head_dim) return LKV_ERR_INVALID_ARGUMENT;
+  cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)total_q};
+  cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)q_stride_tok * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)group, (cuuint32_t)(128 / group)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LKV_OK : LKV_ERR_TENSOR_MAP;
+}
+
 }  // namespace lkv
 
 extern "C" {
@@ -204,6 +223,40 @@ int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages, const int32_t
   a.error_word = error_word;
   a.stream = stream;
   return lkv::blend_chunk(a);
+}
+
+int lkv_prefill_paged(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
+                      int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,
+                      const int32_t* seq_k, const int32_t* cu_seqlens_q, void* out, int64_t out_stride_tok,
+                      float* lse, const float* out_scale, int batch, int total_q, int max_q, int num_q_heads,
+                      int num_kv_heads, int head_dim, int max_pages_per_seq, int causal, float softmax_scale,
+                      int32_t* error_word, void* stream) {
+  lkv::PrefillArgs a{};
+  a.q = q;
+  a.q_stride_tok = q_stride_tok;
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.block_table = block_table;
+  a.block_table_stride = block_table_stride;
+  a.seq_k = seq_k;
+  a.cu_q = cu_seqlens_q;
+  a.out = out;
+  a.out_stride_tok = out_stride_tok;
+  a.lse = lse;
+  a.out_scale = out_scale;
+  a.batch = batch;
+  a.total_q = total_q;
+  a.max_q = max_q;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.max_pages_per_seq = max_pages_per_seq;
+  a.causal = causal;
+  a.softmax_scale = softmax_scale;
+  a.error_word = error_word;
+  a.stream = stream;
+  return lkv::prefill_paged(a);
 }
 
 int lkv_build_layer_block_tables(const int32_t* block_table, int64_t block_table_stride, const int32_t* nsrc,

@@ -13,6 +13,29 @@ namespace lkv {
 constexpr size_t kWorkspaceHeader = 256;
 
 int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, int num_kv_heads, int head_dim);
+int make_query_tensor_map(CUtensorMap* map, const void* q, int64_t total_q, int64_t q_stride_tok, int num_q_heads,
+                          int head_dim, int group);
+
+struct PrefillArgs {
+  const void* q;
+  int64_t q_stride_tok;
+  const void* pool_k;
+  const void* pool_v;
+  int64_t num_pages;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  const int32_t* seq_k;
+  const int32_t* cu_q;
+  void* out;
+  int64_t out_stride_tok;
+  float* lse;
+  const float* out_scale;
+  int batch, total_q, max_q, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq, causal;
+  float softmax_scale;
+  int32_t* error_word;
+  void* stream;
+};
+int prefill_paged(const PrefillArgs& a);
 
 struct DecodeArgs {
   const void* q;

@@ -1,0 +1,445 @@
+// Chunked (varlen) prefill over the shared last-layer paged K/V pool on
+// 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Reference semantics: the merged per-layer attention call of the vLLM fast
+// path for prefill spans (vllm/src/lastkv/vllm/backends/rmarin_flashinfer/
+// fastpath.py:643-650: FA3 varlen, block_table = bt_all[l], seqused_k,
+// causal with bottom-right alignment) followed by head_scale_
+// (fused_qkv.py:140-155); at the HF level the masked SDPA of
+// LastKVAttention.forward (llm/src/lastkv/llm/modeling.py:124-146).  The
+// non-causal form serves block attention over a shared history (Wan,
+// videogen/src/lastkv/videogen/attention.py:9-32).
+//
+// Work unit: one CTA = 128 query rows x one KV head x one sequence, where the
+// rows pack TOK = 128 / GROUP query tokens times the GROUP query heads that
+// share the KV head (row r -> token r / GROUP, head r % GROUP), so every K/V
+// byte brought on chip serves the whole GQA group.
+//
+// Warp roles (224 threads):
+//   warps 0-3  softmax + epilogue, one thread per row (TMEM lane = row)
+//   warp 4     TMA producer: Q tile once, then K blocks (128 keys = 8 pages)
+//   warp 5     TMA producer: V blocks
+//   warp 6     TMEM allocator and the single MMA-issuing thread
+// Per key block j (double-buffered S in TMEM):
+//   S_j   = Q K_j^T                 tcgen05.mma, A=Q (K-major), B=K (K-major)
+//   P_j   = exp2(S_j*scale - m)     softmax warps, bf16 into shared memory
+//   O    += P_j V_j                 tcgen05.mma, A=P (K-major), B=V (MN-major)
+// The running max is only raised (and O in TMEM rescaled) when a row's max
+// grows by more than 2^8; otherwise exp2 is taken against the stale max,
+// which stays exact because the final normalisation uses the same reference.
+
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace lkv {
+
+namespace {
+
+constexpr int kBM = 128;  // rows per tile
+constexpr int kBN = 128;  // keys per block
+constexpr int kPageTok = 16;
+constexpr int kPagesPerBlock = kBN / kPageTok;
+constexpr int kThreads = 224;
+constexpr float kRescaleLog2 = 8.0f;
+
+struct PrefillParams {
+  const int32_t* bt;
+  int64_t bt_stride;
+  const int32_t* seq_k;
+  const int32_t* cu_q;
+  __nv_bfloat16* out;
+  int64_t out_stride_tok;
+  float* lse;
+  const float* out_scale;
+  int* err;
+  int B, Hq, Hkv, W;
+  int64_t num_pages;
+  int causal;
+  float scale_log2;
+};
+
+template <int D>
+struct PrefillCfg {
+  static constexpr int HALVES = D / 64;
+  static constexpr int Q_HALF = kBM * 128;      // [128 rows][64 bf16]
+  static constexpr int KV_HALF = kBN * 128;     // [128 keys][64 bf16]
+  static constexpr int Q_BYTES = HALVES * Q_HALF;
+  static constexpr int KV_BYTES = HALVES * KV_HALF;
+  static constexpr int P_HALF = kBM * 128;      // [128 rows][64 keys]
+  static constexpr int P_BYTES = 2 * P_HALF;
+  static constexpr int KST = 2, VST = 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + VST * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  // At least 120 KB so a second CTA never shares the SM (each CTA holds all 512 TMEM columns).
+  static constexpr int SMEM_BYTES = (1024 + OFF_BAR + 256) > 120 * 1024 ? (1024 + OFF_BAR + 256) : 120 * 1024;
+  static constexpr uint32_t IDESC_S = umma_idesc_bf16(kBM, kBN, 0, 0);
+  static constexpr uint32_t IDESC_PV = umma_idesc_bf16(kBM, D, 0, 1);
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t o_full;
+  uint32_t tmem_addr;
+  int fail;
+};
+
+template <int D, int GROUP>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_tcgen05_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
+  using Cfg = PrefillCfg<D>;
+  constexpr int TOK = kBM / GROUP;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + Cfg::OFF_BAR);
+
+  const int tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = p.cu_q[b];
+  const int Lq = p.cu_q[b + 1] - q0;
+  const int t0 = tile * TOK;
+  if (t0 >= Lq) return;
+  const int n = p.seq_k[b];
+  const int t_end = min(t0 + TOK, Lq);
+  int lim_max = p.causal ? n - Lq + t_end - 1 : n - 1;
+  lim_max = min(lim_max, n - 1);
+  const int nb = lim_max >= 0 ? lim_max / kBN + 1 : 0;
+  if (nb == 0) {
+    // no visible keys: zero output rows (and -inf LSE), as an empty softmax
+    for (int r = threadIdx.x; r < TOK * GROUP; r += kThreads) {
+      const int tok = t0 + r / GROUP;
+      if (tok >= Lq) continue;
+      const int hq = hk * GROUP + r % GROUP;
+      __nv_bfloat16* o = p.out + (int64_t)(q0 + tok) * p.out_stride_tok + (int64_t)hq * D;
+      for (int d = 0; d < D; ++d) o[d] = __float2bfloat16_rn(0.f);
+      if (p.lse) p.lse[(int64_t)(q0 + tok) * p.Hq + hq] = -INFINITY;
+    }
+    return;
+  }
+  const int npages = min((n + kPageTok - 1) / kPageTok, p.W);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+      mbar_init(&bars->s_full[s], 1);
+    }
+    mbar_init(&bars->p_full, 4);
+    mbar_init(&bars->o_full, 1);
+    bars->fail = 0;
+    fence_barrier_init();
+  }
+  if (warp == 6) {
+    tmem_alloc(&bars->tmem_addr, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_addr;
+
+  uint8_t* sQ = smem + Cfg::OFF_Q;
+  uint8_t* sK = smem + Cfg::OFF_K;
+  uint8_t* sV = smem + Cfg::OFF_V;
+  uint8_t* sP = smem + Cfg::OFF_P;
+  const int32_t* btrow = p.bt + (int64_t)b * p.bt_stride;
+
+  if (warp == 4 || warp == 5) {
+    // ------------------------------------------------------------ producers
+    if (lane == 0) {
+      const bool is_k = warp == 4;
+      const CUtensorMap* map = is_k ? &tmk : &tmv;
+      tma_prefetch_desc(map);
+      if (is_k) {
+        tma_prefetch_desc(&tmq);
+        mbar_arrive_expect_tx(&bars->q_full, Cfg::Q_BYTES);
+#pragma unroll
+        for (int h = 0; h < Cfg::HALVES; ++h)
+          tma_load_3d(sQ + h * Cfg::Q_HALF, &tmq, &bars->q_full, h * 64, hk * GROUP, q0 + t0);
+      }
+      uint64_t* full = is_k ? bars->k_full : bars->v_full;
+      uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+      uint8_t* ring = is_k ? sK : sV;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&empty[s], ((j >> 1) & 1) ^ 1)) {
+          report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, j);
+          bars->fail = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], Cfg::KV_BYTES);
+        uint8_t* dst = ring + s * Cfg::KV_BYTES;
+        for (int pg = 0; pg < kPagesPerBlock; ++pg) {
+          const int pi = j * kPagesPerBlock + pg;
+          int pid = (int)p.num_pages;  // past the pool: TMA fills zeros
+          if (pi < npages) {
+            pid = btrow[pi];
+            if (is_k && (pid < 0 || (int64_t)pid >= p.num_pages)) report_error(p.err, DEVERR_BAD_PAGE, 4, pid);
+          }
+#pragma unroll
+          for (int h = 0; h < Cfg::HALVES; ++h)
+            tma_load_4d(dst + h * Cfg::KV_HALF + pg * (kPageTok * 128), map, &full[s], h * 64, hk, 0, pid);
+        }
+      }
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
+      auto issue_s = [&](int j) {
+        const int s = j & 1;
+        const uint32_t kb = k_base + s * Cfg::KV_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint64_t a = umma_sdesc_sw128(q_base + (ks >> 2) * Cfg::Q_HALF + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_sdesc_sw128(kb + (ks >> 2) * Cfg::KV_HALF + (ks & 3) * 32, 16, 1024);
+          umma_bf16_ss(tmem + s * kBN, a, bd, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->s_full[s]);
+        umma_commit(&bars->k_empty[s]);
+      };
+      bool ok = mbar_wait(&bars->q_full, 0);
+      for (int j = 0; ok && j < min(nb, 2); ++j) {
+        ok = mbar_wait(&bars->k_full[j & 1], 0);
+        tc_fence_after();
+        if (ok) issue_s(j);
+      }
+      for (int j = 0; ok && j < nb; ++j) {
+        const int s = j & 1;
+        ok = mbar_wait(&bars->p_full, j & 1) && mbar_wait(&bars->v_full[s], (j >> 1) & 1);
+        tc_fence_after();
+        if (!ok) break;
+        const uint32_t vb = v_base + s * Cfg::KV_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          const uint64_t a = umma_sdesc_sw128(p_base + (ks >> 2) * Cfg::P_HALF + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_sdesc_sw128(vb + ks * (kPageTok * 128), Cfg::KV_HALF, 1024);
+          umma_bf16_ss(tmem + 2 * kBN, a, bd, Cfg::IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars->o_full);
+        umma_commit(&bars->v_empty[s]);
+        if (j + 2 < nb) {
+          ok = mbar_wait(&bars->k_full[s], ((j + 2) >> 1) & 1);
+          tc_fence_after();
+          if (ok) issue_s(j + 2);
+        }
+      }
+      if (!ok) {
+        report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 100);
+        bars->fail = 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (rows)
+    const int r = threadIdx.x;  // 0..127 = TMEM lane
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const int tok = t0 + r / GROUP;
+    int lim = p.causal ? n - Lq + tok : n - 1;
+    lim = min(lim, n - 1);
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint8_t* prow0 = sP + r * 128;
+    // Wait results are made warp-uniform: tcgen05.ld/st below are warp-collective.
+    for (int j = 0; j < nb; ++j) {
+      const int sb = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], (j >> 1) & 1));
+      tc_fence_after();
+      if (!ok) break;
+      float x[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(lane_base + sb * kBN + c * 32, raw);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(raw[e]) * p.scale_log2;
+      }
+      const int key0 = j * kBN;
+      if (key0 + kBN - 1 > lim) {
+#pragma unroll
+        for (int e = 0; e < kBN; ++e)
+          if (key0 + e > lim) x[e] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kBN; ++e) mx = fmaxf(mx, x[e]);
+      float alpha = 1.f;
+      if (mx > m + kRescaleLog2) {
+        alpha = (m == -INFINITY) ? 0.f : exp2f(m - mx);
+        m = mx;
+      }
+      const float mref = (m == -INFINITY) ? 0.f : m;
+      float sum = 0.f;
+      uint32_t pk[kBN / 2];
+#pragma unroll
+      for (int e = 0; e < kBN; e += 2) {
+        const float p0 = exp2f(x[e] - mref), p1 = exp2f(x[e + 1] - mref);
+        sum += p0 + p1;
+        pk[e / 2] = pack_bf16(p0, p1);
+      }
+      l = l * alpha + sum;
+      if (j > 0) {
+        // P smem and O are still in use by PV_{j-1}
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full, (j - 1) & 1));
+        tc_fence_after();
+        if (!ok) break;
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t raw[32];
+            tmem_ld32(lane_base + 2 * kBN + c * 32, raw);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * alpha);
+            tmem_st32(lane_base + 2 * kBN + c * 32, raw);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row: keys [0, 64) in the first 128-byte-swizzled half, [64, 128) in the second
+#pragma unroll
+      for (int ch = 0; ch < kBN / 8; ++ch) {
+        const int half = ch >> 3, c16 = ch & 7;
+        uint4 v = make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow0 + half * Cfg::P_HALF + ((c16 ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full, (nb - 1) & 1));
+    tc_fence_after();
+    if (!ok) {
+      report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 200);
+      bars->fail = 1;
+    } else {
+      const int hq = hk * GROUP + r % GROUP;
+      const bool valid = tok < Lq;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float sc = inv * (p.out_scale ? p.out_scale[hq] : 1.f);
+      __nv_bfloat16* orow = p.out + (int64_t)(q0 + (valid ? tok : 0)) * p.out_stride_tok + (int64_t)hq * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(lane_base + 2 * kBN + c * 32, raw);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(raw[e + 0]) * sc, __uint_as_float(raw[e + 1]) * sc);
+            v.y = pack_bf16(__uint_as_float(raw[e + 2]) * sc, __uint_as_float(raw[e + 3]) * sc);
+            v.z = pack_bf16(__uint_as_float(raw[e + 4]) * sc, __uint_as_float(raw[e + 5]) * sc);
+            v.w = pack_bf16(__uint_as_float(raw[e + 6]) * sc, __uint_as_float(raw[e + 7]) * sc);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+          }
+        }
+      }
+      if (valid && p.lse)
+        p.lse[(int64_t)(q0 + tok) * p.Hq + hq] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 6) tmem_dealloc(tmem, 512);
+}
+
+template <int D, int GROUP>
+int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& prm,
+                   int max_q, cudaStream_t stream) {
+  using Cfg = PrefillCfg<D>;
+  constexpr int TOK = kBM / GROUP;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(prefill_tcgen05_kernel<D, GROUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return LKV_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  dim3 grid((max_q + TOK - 1) / TOK, prm.Hkv, prm.B);
+  prefill_tcgen05_kernel<D, GROUP><<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+}  // namespace
+
+int prefill_paged(const PrefillArgs& a) {
+  if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (a.num_kv_heads <= 0 || a.num_q_heads <= 0 || a.num_q_heads % a.num_kv_heads) return LKV_ERR_INVALID_ARGUMENT;
+  const int group = a.num_q_heads / a.num_kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return LKV_ERR_UNSUPPORTED;
+  if (a.batch < 0 || a.total_q < 0 || a.max_q < 0 || a.max_pages_per_seq < 0) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.batch == 0 || a.total_q == 0 || a.max_q == 0) return LKV_OK;
+  if (!a.q || !a.pool_k || !a.pool_v || !a.block_table || !a.seq_k || !a.cu_q || !a.out)
+    return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(a.q) & 15) || ((a.q_stride_tok * 2) & 15)) return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(a.out) & 15) || ((a.out_stride_tok * 2) & 15)) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.batch > 65535 || a.num_kv_heads > 65535) return LKV_ERR_UNSUPPORTED;
+  if (!a.error_word) return LKV_ERR_INVALID_ARGUMENT;
+
+  CUtensorMap tq, tk, tv;
+  int st = make_query_tensor_map(&tq, a.q, a.total_q, a.q_stride_tok, a.num_q_heads, a.head_dim, group);
+  if (st != LKV_OK) return st;
+  st = make_pool_tensor_map(&tk, a.pool_k, a.num_pages, a.num_kv_heads, a.head_dim);
+  if (st != LKV_OK) return st;
+  st = make_pool_tensor_map(&tv, a.pool_v, a.num_pages, a.num_kv_heads, a.head_dim);
+  if (st != LKV_OK) return st;
+
+  PrefillParams prm{};
+  prm.bt = a.block_table;
+  prm.bt_stride = a.block_table_stride;
+  prm.seq_k = a.seq_k;
+  prm.cu_q = a.cu_q;
+  prm.out = static_cast<__nv_bfloat16*>(a.out);
+  prm.out_stride_tok = a.out_stride_tok;
+  prm.lse = a.lse;
+  prm.out_scale = a.out_scale;
+  prm.err = a.error_word;
+  prm.B = a.batch;
+  prm.Hq = a.num_q_heads;
+  prm.Hkv = a.num_kv_heads;
+  prm.W = a.max_pages_per_seq;
+  prm.num_pages = a.num_pages;
+  prm.causal = a.causal ? 1 : 0;
+  prm.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+  cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
+#define LKV_PF(DD, GG) return launch_prefill<DD, GG>(tq, tk, tv, prm, a.max_q, stream)
+  if (a.head_dim == 128) {
+    switch (group) {
+      case 1: LKV_PF(128, 1);
+      case 2: LKV_PF(128, 2);
+      case 4: LKV_PF(128, 4);
+      default: LKV_PF(128, 8);
+    }
+  } else {
+    switch (group) {
+      case 1: LKV_PF(64, 1);
+      case 2: LKV_PF(64, 2);
+      case 4: LKV_PF(64, 4);
+      default: LKV_PF(64, 8);
+    }
+  }
+#undef LKV_PF
+}
+
+}  // namespace lkv

@@ -121,6 +121,40 @@ def decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages, workspace
     return s.value, n.value
 
 
+def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, causal=True, softmax_scale=None,
+                  out=None, lse=None, out_scale=None, error_word=None, max_pages: int | None = None):
+    """Varlen chunked prefill on tcgen05 tensor cores.
+
+    q [T, Hq, D] bf16 rows; cu_q int32 [B+1]; seq_k int32 [B] (>= span when
+    causal; bottom-right alignment); returns out [T, Hq, D] bf16.
+    """
+    _check_pool(pool_k, pool_v)
+    T, Hq, D = q.shape
+    Hkv = pool_k.shape[2]
+    require_heads(Hq, Hkv, D)
+    _require(q.dtype == torch.bfloat16 and q.stride(2) == 1 and q.stride(1) == D, "q must be bf16 [T, Hq, D] rows")
+    _require(block_table.dtype == torch.int32 and block_table.stride(1) == 1, "block_table must be int32 [B, W]")
+    _require(cu_q.dtype == torch.int32 and seq_k.dtype == torch.int32, "cu_q / seq_k must be int32")
+    B = cu_q.numel() - 1
+    W = int(max_pages if max_pages is not None else block_table.shape[1])
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
+    _require(out.dtype == torch.bfloat16 and out.stride(2) == 1 and out.stride(1) == D, "out layout")
+    if error_word is None:
+        error_word = torch.zeros(4, dtype=torch.int32, device=q.device)
+    if out_scale is not None:
+        _require(out_scale.dtype == torch.float32 and out_scale.numel() == Hq, "out_scale must be fp32 [Hq]")
+    st = _capi.lib().lkv_prefill_paged(
+        q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
+        block_table.stride(0), seq_k.data_ptr(), cu_q.data_ptr(), out.data_ptr(), out.stride(0), _ptr(lse),
+        _ptr(out_scale), B, T, int(max_q), Hq, Hkv, D, W, int(bool(causal)), float(softmax_scale),
+        error_word.data_ptr(), _stream())
+    _capi.check(st, "lkv_prefill_paged")
+    return out
+
+
 def merge_partials(o_parts, lse_parts, *, out_scale=None, out=None, lse_out=None):
     """LSE-merge P partials: o_parts fp32 [P, T, Hq, D], lse_parts fp32 [P, T, Hq]."""
     P_, T, Hq, D = o_parts.shape
