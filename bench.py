@@ -64,6 +64,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
     return ap.parse_args()
 
 
@@ -213,6 +214,79 @@ def build_workload(rank: int, device):
                 q=q, out_scale=out_scale, out=out, ws=ws, W=W)
 
 
+PREFILL = dict(batch=8, q_heads=32, kv_heads=8, head_dim=128, context=8192, chunk=1024)
+
+
+def prefill_flops(span_start: int, span: int, batch: int, hq: int, d: int) -> int:
+    """4 * Hq * D * sum over the span's queries of visible keys (causal, bottom-right)."""
+    visible = span * span_start + span * (span + 1) // 2
+    return 4 * hq * d * visible * batch
+
+
+def measure_prefill(device, reps: int = 5, batch: int | None = None):
+    """Chunked prefill attention of one layer over an 8192-token prompt (8 x 1024-token spans, batch 8).
+
+    The 8B config's 2048-token prefill calls cross a chunk boundary (C = 1024),
+    so each is issued as two chunk-aligned spans, as the reference's HF loop
+    splits them (llm/src/lastkv/llm/modeling.py:194-208).
+    """
+    import torch
+
+    from lastkv_b200 import ops
+
+    B, Hq, H, D, N, C = (PREFILL[k] for k in ("batch", "q_heads", "kv_heads", "head_dim", "context", "chunk"))
+    B = batch or B
+    gen = torch.Generator(device=device).manual_seed(77)
+    pages = N // 16
+    pool_k = torch.randn((B * pages + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    pool_v = torch.randn((B * pages + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    bt = torch.randperm(B * pages, generator=gen, device=device).to(torch.int32).view(B, pages)
+    q = torch.randn((B * C, Hq, D), generator=gen, device=device, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    err = torch.zeros(4, dtype=torch.int32, device=device)
+    cu = torch.arange(0, B * C + 1, C, dtype=torch.int32, device=device)
+    seqks = [torch.full((B,), C * (s + 1), dtype=torch.int32, device=device) for s in range(N // C)]
+
+    def layer():
+        for s in range(N // C):
+            ops.prefill_paged(q, pool_k, pool_v, bt, seqks[s], cu, C, out=out, error_word=err,
+                              max_pages=C * (s + 1) // 16)
+
+    for _ in range(2):
+        layer()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        layer()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = sum(prefill_flops(C * s, C, B, Hq, D) for s in range(N // C))
+    # the last span alone (7168 keys of history + 1024 causal): the steady-state kernel rate
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record()
+    for _ in range(reps):
+        ops.prefill_paged(q, pool_k, pool_v, bt, seqks[-1], cu, C, out=out, error_word=err)
+    l1.record()
+    torch.cuda.synchronize()
+    last_ms = l0.elapsed_time(l1) / reps
+    last_flops = prefill_flops(N - C, C, B, Hq, D)
+    if err.cpu().tolist()[0] != 0:
+        raise RuntimeError(f"prefill device error word set: {err.cpu().tolist()}")
+    try:
+        peak = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["bf16_tflops"])
+        src = "measured (burst)"
+    except (OSError, KeyError, ValueError):
+        peak, src = 1590.0, "fallback"
+    tf = flops / (ms * 1e-3) / 1e12
+    tf_last = last_flops / (last_ms * 1e-3) / 1e12
+    return {"workload": f"chunked prefill attention, 1 layer, batch {B} x 8192-token prompt as 8 x 1024-token spans, "
+                        "32/8 heads, D 128, shuffled pages", "ms_per_layer": ms, "flops_per_layer": flops,
+            "tflops": tf, "frac": tf / peak, "last_span_tflops": tf_last, "last_span_frac": tf_last / peak,
+            "peak_tflops": peak, "peak_source": src, "kernel": "prefill_tcgen05_kernel"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -337,6 +411,9 @@ def run_ours(args):
         "gpu_launches": int(args.steps * L * launches_per_call),
         "kv_splits": splits,
     }
+    if not args.no_prefill:
+        # the small case (profiler captures) runs the same spans with 2 sequences
+        line["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = cpu_layer_step_sample(args.cpu_seconds, batch=8)
         med = statistics.median(times)

@@ -20,13 +20,16 @@
 //   warp 4     TMA producer: Q tile once, then K blocks (128 keys = 8 pages)
 //   warp 5     TMA producer: V blocks
 //   warp 6     TMEM allocator and the single MMA-issuing thread
-// Per key block j (double-buffered S in TMEM):
-//   S_j   = Q K_j^T                 tcgen05.mma, A=Q (K-major), B=K (K-major)
-//   P_j   = exp2(S_j*scale - m)     softmax warps, bf16 into shared memory
-//   O    += P_j V_j                 tcgen05.mma, A=P (K-major), B=V (MN-major)
-// The running max is only raised (and O in TMEM rescaled) when a row's max
-// grows by more than 2^8; otherwise exp2 is taken against the stale max,
-// which stays exact because the final normalisation uses the same reference.
+// Per key block j (TMEM columns: S double-buffered in [0,128) / [128,256),
+// O in [256, 256 + D), bf16 P double-buffered in [384,448) / [448,512)):
+//   S_j = Q K_j^T              tcgen05.mma SS: A = Q, B = K (both K-major, smem)
+//   P_j = exp2(S_j*scale - m)  softmax warps, stored to TMEM with tcgen05.st
+//                              (two bf16 per 32-bit column)
+//   O  += P_j V_j              tcgen05.mma TS: A = P (TMEM), B = V (MN-major, smem)
+// K and V stream through separate 3-stage rings.  The running max is only
+// raised (and O rescaled in TMEM) when a row's max grows by more than 2^8;
+// otherwise exp2 is taken against the stale max, which stays exact because the
+// final normalisation uses the same reference.
 
 #include <math.h>
 
@@ -45,6 +48,7 @@ constexpr int kBN = 128;  // keys per block
 constexpr int kPageTok = 16;
 constexpr int kPagesPerBlock = kBN / kPageTok;
 constexpr int kThreads = 224;
+constexpr int kStages = 3;
 constexpr float kRescaleLog2 = 8.0f;
 
 struct PrefillParams {
@@ -66,31 +70,29 @@ struct PrefillParams {
 template <int D>
 struct PrefillCfg {
   static constexpr int HALVES = D / 64;
-  static constexpr int Q_HALF = kBM * 128;      // [128 rows][64 bf16]
-  static constexpr int KV_HALF = kBN * 128;     // [128 keys][64 bf16]
+  static constexpr int Q_HALF = kBM * 128;   // [128 rows][64 bf16]
+  static constexpr int KV_HALF = kBN * 128;  // [128 keys][64 bf16]
   static constexpr int Q_BYTES = HALVES * Q_HALF;
   static constexpr int KV_BYTES = HALVES * KV_HALF;
-  static constexpr int P_HALF = kBM * 128;      // [128 rows][64 keys]
-  static constexpr int P_BYTES = 2 * P_HALF;
-  static constexpr int KST = 2, VST = 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + VST * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int OFF_V = OFF_K + kStages * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + kStages * KV_BYTES;
   // At least 120 KB so a second CTA never shares the SM (each CTA holds all 512 TMEM columns).
   static constexpr int SMEM_BYTES = (1024 + OFF_BAR + 256) > 120 * 1024 ? (1024 + OFF_BAR + 256) : 120 * 1024;
   static constexpr uint32_t IDESC_S = umma_idesc_bf16(kBM, kBN, 0, 0);
   static constexpr uint32_t IDESC_PV = umma_idesc_bf16(kBM, D, 0, 1);
+  static constexpr uint32_t COL_O = 2 * kBN;        // O: columns [256, 256 + D)
+  static constexpr uint32_t COL_P = 2 * kBN + 128;  // P buffers: [384, 448) and [448, 512)
 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t o_full;
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2];   // MMA -> softmax: S_j complete, per S buffer
+  uint64_t p_full[2];   // softmax -> MMA: P_j stored in TMEM (4 warp arrivals), per S buffer
+  uint64_t pv_done[2];  // MMA -> softmax: PV_j complete, per S buffer
   uint32_t tmem_addr;
   int fail;
 };
@@ -132,15 +134,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
-      mbar_init(&bars->s_full[s], 1);
     }
-    mbar_init(&bars->p_full, 4);
-    mbar_init(&bars->o_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->p_full[s], 4);
+      mbar_init(&bars->pv_done[s], 1);
+    }
     bars->fail = 0;
     fence_barrier_init();
   }
@@ -156,7 +160,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem + Cfg::OFF_Q;
   uint8_t* sK = smem + Cfg::OFF_K;
   uint8_t* sV = smem + Cfg::OFF_V;
-  uint8_t* sP = smem + Cfg::OFF_P;
   const int32_t* btrow = p.bt + (int64_t)b * p.bt_stride;
 
   if (warp == 4 || warp == 5) {
@@ -176,8 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
       uint8_t* ring = is_k ? sK : sV;
       for (int j = 0; j < nb; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&empty[s], ((j >> 1) & 1) ^ 1)) {
+        const int s = j % kStages;
+        if (!mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1)) {
           report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, j);
           bars->fail = 1;
           break;
@@ -200,41 +203,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 6) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       auto issue_s = [&](int j) {
-        const int s = j & 1;
+        const int s = j % kStages, sb = j & 1;
         const uint32_t kb = k_base + s * Cfg::KV_BYTES;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint64_t a = umma_sdesc_sw128(q_base + (ks >> 2) * Cfg::Q_HALF + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = umma_sdesc_sw128(kb + (ks >> 2) * Cfg::KV_HALF + (ks & 3) * 32, 16, 1024);
-          umma_bf16_ss(tmem + s * kBN, a, bd, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + sb * kBN, a, bd, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->s_full[s]);
+        umma_commit(&bars->s_full[sb]);
         umma_commit(&bars->k_empty[s]);
       };
       bool ok = mbar_wait(&bars->q_full, 0);
       for (int j = 0; ok && j < min(nb, 2); ++j) {
-        ok = mbar_wait(&bars->k_full[j & 1], 0);
+        ok = mbar_wait(&bars->k_full[j % kStages], (j / kStages) & 1);
         tc_fence_after();
         if (ok) issue_s(j);
       }
       for (int j = 0; ok && j < nb; ++j) {
-        const int s = j & 1;
-        ok = mbar_wait(&bars->p_full, j & 1) && mbar_wait(&bars->v_full[s], (j >> 1) & 1);
+        const int s = j % kStages, sb = j & 1;
+        ok = mbar_wait(&bars->p_full[sb], (j >> 1) & 1) && mbar_wait(&bars->v_full[s], (j / kStages) & 1);
         tc_fence_after();
         if (!ok) break;
         const uint32_t vb = v_base + s * Cfg::KV_BYTES;
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint64_t a = umma_sdesc_sw128(p_base + (ks >> 2) * Cfg::P_HALF + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = umma_sdesc_sw128(vb + ks * (kPageTok * 128), Cfg::KV_HALF, 1024);
-          umma_bf16_ss(tmem + 2 * kBN, a, bd, Cfg::IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + Cfg::COL_O, tmem + Cfg::COL_P + sb * 64 + ks * 8, bd, Cfg::IDESC_PV,
+                       (j > 0 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(&bars->o_full);
+        umma_commit(&bars->pv_done[sb]);
         umma_commit(&bars->v_empty[s]);
         if (j + 2 < nb) {
-          ok = mbar_wait(&bars->k_full[s], ((j + 2) >> 1) & 1);
+          // S_{j+2} reuses S buffer sb, whose S_j the softmax warps have fully read (p_full)
+          ok = mbar_wait(&bars->k_full[(j + 2) % kStages], ((j + 2) / kStages) & 1);
           tc_fence_after();
           if (ok) issue_s(j + 2);
         }
@@ -253,21 +257,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     lim = min(lim, n - 1);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* prow0 = sP + r * 128;
+    const float sl2 = p.scale_log2;
     // Wait results are made warp-uniform: tcgen05.ld/st below are warp-collective.
     for (int j = 0; j < nb; ++j) {
       const int sb = j & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], (j >> 1) & 1));
       tc_fence_after();
       if (!ok) break;
+      // raw scores; the softmax scale is folded into one FFMA per element below
       float x[kBN];
+      {
+        uint32_t raw[kBN / 32][32];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(lane_base + sb * kBN + c * 32, raw);
-        tmem_wait_ld();
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32(lane_base + sb * kBN + c * 32, raw[c]);
+        tmem_wait_ld();  // one wait for all four loads
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(raw[e]) * p.scale_log2;
+        for (int c = 0; c < kBN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(raw[c][e]);
       }
       const int key0 = j * kBN;
       if (key0 + kBN - 1 > lim) {
@@ -275,55 +282,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < kBN; ++e)
           if (key0 + e > lim) x[e] = -INFINITY;
       }
-      float mx = -INFINITY;
+      // 8 independent partial maxima (short dependency chains), then a tree
+      float mp[8];
 #pragma unroll
-      for (int e = 0; e < kBN; ++e) mx = fmaxf(mx, x[e]);
+      for (int t = 0; t < 8; ++t) mp[t] = x[t];
+#pragma unroll
+      for (int e = 8; e < kBN; e += 8)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mp[t] = fmaxf(mp[t], x[e + t]);
+      float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      mx *= sl2;  // scale > 0, so max commutes with it
       float alpha = 1.f;
       if (mx > m + kRescaleLog2) {
-        alpha = (m == -INFINITY) ? 0.f : exp2f(m - mx);
+        alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - mx);
         m = mx;
       }
-      const float mref = (m == -INFINITY) ? 0.f : m;
-      float sum = 0.f;
+      const float neg_mref = (m == -INFINITY) ? 0.f : -m;
+      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int e = 0; e < kBN; e += 2) {
-        const float p0 = exp2f(x[e] - mref), p1 = exp2f(x[e + 1] - mref);
-        sum += p0 + p1;
+        const float p0 = ex2_approx(__fmaf_rn(x[e], sl2, neg_mref));
+        const float p1 = ex2_approx(__fmaf_rn(x[e + 1], sl2, neg_mref));
+        sp[(e >> 1) & 7] += p0 + p1;
         pk[e / 2] = pack_bf16(p0, p1);
       }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
-      if (j > 0) {
-        // P smem and O are still in use by PV_{j-1}
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full, (j - 1) & 1));
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O holds blocks < j once PV_{j-1} is complete; rescale it in TMEM
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1], ((j - 1) >> 1) & 1));
         tc_fence_after();
         if (!ok) break;
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t raw[32];
-            tmem_ld32(lane_base + 2 * kBN + c * 32, raw);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(lane_base + Cfg::COL_O + c * 32, raw);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * alpha);
-            tmem_st32(lane_base + 2 * kBN + c * 32, raw);
-          }
-          tmem_wait_st();
+          for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * alpha);
+          tmem_st32(lane_base + Cfg::COL_O + c * 32, raw);
         }
       }
-      // P row: keys [0, 64) in the first 128-byte-swizzled half, [64, 128) in the second
+      // P_j (bf16 pairs) into P buffer sb.  Its previous reader, PV_{j-2}, was
+      // issued before S_j and is covered by S_j's completion (s_full[sb]).
+      {
+        uint32_t lo[32], hi[32];
 #pragma unroll
-      for (int ch = 0; ch < kBN / 8; ++ch) {
-        const int half = ch >> 3, c16 = ch & 7;
-        uint4 v = make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(prow0 + half * Cfg::P_HALF + ((c16 ^ (r & 7)) << 4)) = v;
+        for (int e = 0; e < 32; ++e) {
+          lo[e] = pk[e];
+          hi[e] = pk[32 + e];
+        }
+        tmem_st32(lane_base + Cfg::COL_P + sb * 64, lo);
+        tmem_st32(lane_base + Cfg::COL_P + sb * 64 + 32, hi);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full);
+      if (lane == 0) mbar_arrive(&bars->p_full[sb]);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full, (nb - 1) & 1));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1));
     tc_fence_after();
     if (!ok) {
       report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 200);
@@ -337,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t raw[32];
-        tmem_ld32(lane_base + 2 * kBN + c * 32, raw);
+        tmem_ld32(lane_base + Cfg::COL_O + c * 32, raw);
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
