@@ -10,26 +10,30 @@
 // non-causal form serves block attention over a shared history (Wan,
 // videogen/src/lastkv/videogen/attention.py:9-32).
 //
-// Work unit: one CTA = 128 query rows x one KV head x one sequence, where the
-// rows pack TOK = 128 / GROUP query tokens times the GROUP query heads that
-// share the KV head (row r -> token r / GROUP, head r % GROUP), so every K/V
-// byte brought on chip serves the whole GQA group.
+// Work unit: one CTA = two 128-row query tiles (A, B) x one KV head x one
+// sequence.  Rows pack TOK = 128 / GROUP query tokens times the GROUP query
+// heads that share the KV head (row r -> token r / GROUP, head r % GROUP);
+// tile B holds the TOK tokens after tile A.  Every K/V block brought on chip
+// serves 256 rows (the whole GQA group of 2 TOK tokens).
 //
-// Warp roles (224 threads):
-//   warps 0-3  softmax + epilogue, one thread per row (TMEM lane = row)
-//   warp 4     TMA producer: Q tile once, then K blocks (128 keys = 8 pages)
-//   warp 5     TMA producer: V blocks
-//   warp 6     TMEM allocator and the single MMA-issuing thread
-// Per key block j (TMEM columns: S double-buffered in [0,128) / [128,256),
-// O in [256, 256 + D), bf16 P double-buffered in [384,448) / [448,512)):
-//   S_j = Q K_j^T              tcgen05.mma SS: A = Q, B = K (both K-major, smem)
-//   P_j = exp2(S_j*scale - m)  softmax warps, stored to TMEM with tcgen05.st
-//                              (two bf16 per 32-bit column)
-//   O  += P_j V_j              tcgen05.mma TS: A = P (TMEM), B = V (MN-major, smem)
-// K and V stream through separate 3-stage rings.  The running max is only
-// raised (and O rescaled in TMEM) when a row's max grows by more than 2^8;
-// otherwise exp2 is taken against the stale max, which stays exact because the
-// final normalisation uses the same reference.
+// Warp roles (352 threads):
+//   warps 0-3  softmax + epilogue of tile A, one thread per row (TMEM lane)
+//   warps 4-7  softmax + epilogue of tile B
+//   warp 8     TMA producer: Q tiles once, then K blocks (128 keys = 8 pages)
+//   warp 9     TMA producer: V blocks
+//   warp 10    TMEM allocator and the single MMA-issuing thread
+// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [256+D, 256+2D).
+// Per key block j the MMA thread issues, in order,
+//   PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
+// (S = Q K^T: A = Q, B = K, both K-major in smem; PV: A = P read from TMEM,
+// B = V MN-major in smem), so while one tile's softmax runs the tensor core
+// works on the other tile.  P (bf16, two per column) overwrites the first 64
+// columns of its own tile's S; the next S of that tile is issued after the PV
+// that reads P, and tcgen05.mma from one thread executes in issue order.
+// K and V stream through separate rings (3 and 2 stages).  The running max is
+// only raised (and O rescaled in TMEM) when a row's max grows by more than
+// 2^8; otherwise exp2 is taken against the stale max, which stays exact
+// because the final normalisation uses the same reference.
 
 #include <math.h>
 
@@ -44,11 +48,13 @@ namespace lkv {
 namespace {
 
 constexpr int kBM = 128;  // rows per tile
+constexpr int kTiles = 2;  // query tiles per CTA
 constexpr int kBN = 128;  // keys per block
 constexpr int kPageTok = 16;
 constexpr int kPagesPerBlock = kBN / kPageTok;
-constexpr int kThreads = 224;
-constexpr int kStages = 3;
+constexpr int kWarpK = 8, kWarpV = 9, kWarpMma = 10;
+constexpr int kThreads = 11 * 32;
+constexpr int kStagesK = 3, kStagesV = 2;
 constexpr float kRescaleLog2 = 8.0f;
 
 struct PrefillParams {
@@ -72,27 +78,29 @@ struct PrefillCfg {
   static constexpr int HALVES = D / 64;
   static constexpr int Q_HALF = kBM * 128;   // [128 rows][64 bf16]
   static constexpr int KV_HALF = kBN * 128;  // [128 keys][64 bf16]
-  static constexpr int Q_BYTES = HALVES * Q_HALF;
+  static constexpr int Q_BYTES = HALVES * Q_HALF;  // one tile
   static constexpr int KV_BYTES = HALVES * KV_HALF;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + kStages * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + kStages * KV_BYTES;
+  static constexpr int OFF_K = OFF_Q + kTiles * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + kStagesK * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + kStagesV * KV_BYTES;
+  static constexpr int BAR_BYTES = 512;
   // At least 120 KB so a second CTA never shares the SM (each CTA holds all 512 TMEM columns).
-  static constexpr int SMEM_BYTES = (1024 + OFF_BAR + 256) > 120 * 1024 ? (1024 + OFF_BAR + 256) : 120 * 1024;
+  static constexpr int SMEM_BYTES =
+      (1024 + OFF_BAR + BAR_BYTES) > 120 * 1024 ? (1024 + OFF_BAR + BAR_BYTES) : 120 * 1024;
   static constexpr uint32_t IDESC_S = umma_idesc_bf16(kBM, kBN, 0, 0);
   static constexpr uint32_t IDESC_PV = umma_idesc_bf16(kBM, D, 0, 1);
-  static constexpr uint32_t COL_O = 2 * kBN;        // O: columns [256, 256 + D)
-  static constexpr uint32_t COL_P = 2 * kBN + 128;  // P buffers: [384, 448) and [448, 512)
+  static constexpr uint32_t COL_S = 0;        // + tile * kBN
+  static constexpr uint32_t COL_O = 2 * kBN;  // + tile * D
 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[kStages], k_empty[kStages];
-  uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2];   // MMA -> softmax: S_j complete, per S buffer
-  uint64_t p_full[2];   // softmax -> MMA: P_j stored in TMEM (4 warp arrivals), per S buffer
-  uint64_t pv_done[2];  // MMA -> softmax: PV_j complete, per S buffer
+  uint64_t k_full[kStagesK], k_empty[kStagesK];
+  uint64_t v_full[kStagesV], v_empty[kStagesV];
+  uint64_t s_full[kTiles];   // MMA -> softmax: S_t(j) complete
+  uint64_t p_full[kTiles];   // softmax -> MMA: P_t(j) stored in TMEM (4 warp arrivals)
+  uint64_t pv_done[kTiles];  // MMA -> softmax: PV_t(j) complete
   uint32_t tmem_addr;
   int fail;
 };
@@ -102,25 +110,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_tcgen05_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
   using Cfg = PrefillCfg<D>;
-  constexpr int TOK = kBM / GROUP;
+  constexpr int TOK = kBM / GROUP;  // tokens per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + Cfg::OFF_BAR);
 
-  const int tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int cta_tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = p.cu_q[b];
   const int Lq = p.cu_q[b + 1] - q0;
-  const int t0 = tile * TOK;
+  const int t0 = cta_tile * kTiles * TOK;
   if (t0 >= Lq) return;
   const int n = p.seq_k[b];
-  const int t_end = min(t0 + TOK, Lq);
+  const int t_end = min(t0 + kTiles * TOK, Lq);
   int lim_max = p.causal ? n - Lq + t_end - 1 : n - 1;
   lim_max = min(lim_max, n - 1);
   const int nb = lim_max >= 0 ? lim_max / kBN + 1 : 0;
   if (nb == 0) {
     // no visible keys: zero output rows (and -inf LSE), as an empty softmax
-    for (int r = threadIdx.x; r < TOK * GROUP; r += kThreads) {
+    for (int r = threadIdx.x; r < kTiles * TOK * GROUP; r += kThreads) {
       const int tok = t0 + r / GROUP;
       if (tok >= Lq) continue;
       const int hq = hk * GROUP + r % GROUP;
@@ -134,21 +142,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kStagesK; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < kStagesV; ++s) {
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->p_full[s], 4);
-      mbar_init(&bars->pv_done[s], 1);
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], 4);
+      mbar_init(&bars->pv_done[t], 1);
     }
     bars->fail = 0;
     fence_barrier_init();
   }
-  if (warp == 6) {
+  if (warp == kWarpMma) {
     tmem_alloc(&bars->tmem_addr, 512);
     tmem_relinquish();
   }
@@ -162,25 +172,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + Cfg::OFF_V;
   const int32_t* btrow = p.bt + (int64_t)b * p.bt_stride;
 
-  if (warp == 4 || warp == 5) {
+  if (warp == kWarpK || warp == kWarpV) {
     // ------------------------------------------------------------ producers
     if (lane == 0) {
-      const bool is_k = warp == 4;
+      const bool is_k = warp == kWarpK;
+      const int stages = is_k ? kStagesK : kStagesV;
       const CUtensorMap* map = is_k ? &tmk : &tmv;
       tma_prefetch_desc(map);
       if (is_k) {
         tma_prefetch_desc(&tmq);
-        mbar_arrive_expect_tx(&bars->q_full, Cfg::Q_BYTES);
+        mbar_arrive_expect_tx(&bars->q_full, kTiles * Cfg::Q_BYTES);
 #pragma unroll
-        for (int h = 0; h < Cfg::HALVES; ++h)
-          tma_load_3d(sQ + h * Cfg::Q_HALF, &tmq, &bars->q_full, h * 64, hk * GROUP, q0 + t0);
+        for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+          for (int h = 0; h < Cfg::HALVES; ++h)
+            tma_load_3d(sQ + t * Cfg::Q_BYTES + h * Cfg::Q_HALF, &tmq, &bars->q_full, h * 64, hk * GROUP,
+                        q0 + t0 + t * TOK);
       }
       uint64_t* full = is_k ? bars->k_full : bars->v_full;
       uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
       uint8_t* ring = is_k ? sK : sV;
       for (int j = 0; j < nb; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1)) {
+        const int s = j % stages;
+        if (!mbar_wait(&empty[s], ((j / stages) & 1) ^ 1)) {
           report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, j);
           bars->fail = 1;
           break;
@@ -200,48 +214,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      auto issue_s = [&](int j) {
-        const int s = j % kStages, sb = j & 1;
-        const uint32_t kb = k_base + s * Cfg::KV_BYTES;
+      auto issue_s = [&](int t, int j) {
+        const uint32_t kb = k_base + (j % kStagesK) * Cfg::KV_BYTES;
+        const uint32_t qb = q_base + t * Cfg::Q_BYTES;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint64_t a = umma_sdesc_sw128(q_base + (ks >> 2) * Cfg::Q_HALF + (ks & 3) * 32, 16, 1024);
+          const uint64_t a = umma_sdesc_sw128(qb + (ks >> 2) * Cfg::Q_HALF + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = umma_sdesc_sw128(kb + (ks >> 2) * Cfg::KV_HALF + (ks & 3) * 32, 16, 1024);
-          umma_bf16_ss(tmem + sb * kBN, a, bd, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + Cfg::COL_S + t * kBN, a, bd, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->s_full[sb]);
-        umma_commit(&bars->k_empty[s]);
+        umma_commit(&bars->s_full[t]);
       };
-      bool ok = mbar_wait(&bars->q_full, 0);
-      for (int j = 0; ok && j < min(nb, 2); ++j) {
-        ok = mbar_wait(&bars->k_full[j % kStages], (j / kStages) & 1);
-        tc_fence_after();
-        if (ok) issue_s(j);
-      }
-      for (int j = 0; ok && j < nb; ++j) {
-        const int s = j % kStages, sb = j & 1;
-        ok = mbar_wait(&bars->p_full[sb], (j >> 1) & 1) && mbar_wait(&bars->v_full[s], (j / kStages) & 1);
-        tc_fence_after();
-        if (!ok) break;
-        const uint32_t vb = v_base + s * Cfg::KV_BYTES;
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = v_base + (j % kStagesV) * Cfg::KV_BYTES;
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
           const uint64_t bd = umma_sdesc_sw128(vb + ks * (kPageTok * 128), Cfg::KV_HALF, 1024);
-          umma_bf16_ts(tmem + Cfg::COL_O, tmem + Cfg::COL_P + sb * 64 + ks * 8, bd, Cfg::IDESC_PV,
+          umma_bf16_ts(tmem + Cfg::COL_O + t * D, tmem + Cfg::COL_S + t * kBN + ks * 8, bd, Cfg::IDESC_PV,
                        (j > 0 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(&bars->pv_done[sb]);
-        umma_commit(&bars->v_empty[s]);
-        if (j + 2 < nb) {
-          // S_{j+2} reuses S buffer sb, whose S_j the softmax warps have fully read (p_full)
-          ok = mbar_wait(&bars->k_full[(j + 2) % kStages], ((j + 2) / kStages) & 1);
+        umma_commit(&bars->pv_done[t]);
+      };
+      bool ok = mbar_wait(&bars->q_full, 0);
+      for (int j = 0; ok && j <= nb; ++j) {
+        // PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
+        if (j < nb) {
+          ok = mbar_wait(&bars->k_full[j % kStagesK], (j / kStagesK) & 1);
           tc_fence_after();
-          if (ok) issue_s(j + 2);
+          if (!ok) break;
         }
+        if (j > 0) {
+          ok = mbar_wait(&bars->v_full[(j - 1) % kStagesV], ((j - 1) / kStagesV) & 1);
+          if (!ok) break;
+        }
+        for (int t = 0; t < kTiles; ++t) {
+          if (j > 0) {
+            ok = mbar_wait(&bars->p_full[t], (j - 1) & 1);
+            tc_fence_after();
+            if (!ok) break;
+            issue_pv(t, j - 1);
+          }
+          if (j < nb) issue_s(t, j);
+        }
+        if (!ok) break;
+        if (j < nb) umma_commit(&bars->k_empty[j % kStagesK]);
+        if (j > 0) umma_commit(&bars->v_empty[(j - 1) % kStagesV]);
       }
       if (!ok) {
         report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 100);
@@ -250,9 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax (rows)
-    const int r = threadIdx.x;  // 0..127 = TMEM lane
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    const int tok = t0 + r / GROUP;
+    const int t = warp >> 2;                       // tile
+    const int r = (warp & 3) * 32 + lane;          // TMEM lane = row within the tile
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t col_s = Cfg::COL_S + t * kBN, col_o = Cfg::COL_O + t * D;
+    const int tok = t0 + t * TOK + r / GROUP;
     int lim = p.causal ? n - Lq + tok : n - 1;
     lim = min(lim, n - 1);
     float m = -INFINITY, l = 0.f;
@@ -260,8 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale_log2;
     // Wait results are made warp-uniform: tcgen05.ld/st below are warp-collective.
     for (int j = 0; j < nb; ++j) {
-      const int sb = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], (j >> 1) & 1));
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], j & 1));
       tc_fence_after();
       if (!ok) break;
       // raw scores; the softmax scale is folded into one FFMA per element below
@@ -269,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         uint32_t raw[kBN / 32][32];
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) tmem_ld32(lane_base + sb * kBN + c * 32, raw[c]);
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32(lane_base + col_s + c * 32, raw[c]);
         tmem_wait_ld();  // one wait for all four loads
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c)
@@ -285,11 +307,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 8 independent partial maxima (short dependency chains), then a tree
       float mp[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) mp[t] = x[t];
+      for (int u = 0; u < 8; ++u) mp[u] = x[u];
 #pragma unroll
       for (int e = 8; e < kBN; e += 8)
 #pragma unroll
-        for (int t = 0; t < 8; ++t) mp[t] = fmaxf(mp[t], x[e + t]);
+        for (int u = 0; u < 8; ++u) mp[u] = fmaxf(mp[u], x[e + u]);
       float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       mx *= sl2;  // scale > 0, so max commutes with it
       float alpha = 1.f;
@@ -310,22 +332,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        // O holds blocks < j once PV_{j-1} is complete; rescale it in TMEM
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1], ((j - 1) >> 1) & 1));
+        // O holds blocks < j once PV(j-1) is complete; rescale it in TMEM
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[t], (j - 1) & 1));
         tc_fence_after();
         if (!ok) break;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t raw[32];
-          tmem_ld32(lane_base + Cfg::COL_O + c * 32, raw);
+          tmem_ld32(lane_base + col_o + c * 32, raw);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * alpha);
-          tmem_st32(lane_base + Cfg::COL_O + c * 32, raw);
+          tmem_st32(lane_base + col_o + c * 32, raw);
         }
       }
-      // P_j (bf16 pairs) into P buffer sb.  Its previous reader, PV_{j-2}, was
-      // issued before S_j and is covered by S_j's completion (s_full[sb]).
+      // P(j) (bf16 pairs) over the first 64 columns of this tile's S, which is fully read.
       {
         uint32_t lo[32], hi[32];
 #pragma unroll
@@ -333,15 +354,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           lo[e] = pk[e];
           hi[e] = pk[32 + e];
         }
-        tmem_st32(lane_base + Cfg::COL_P + sb * 64, lo);
-        tmem_st32(lane_base + Cfg::COL_P + sb * 64 + 32, hi);
+        tmem_st32(lane_base + col_s, lo);
+        tmem_st32(lane_base + col_s + 32, hi);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[sb]);
+      if (lane == 0) mbar_arrive(&bars->p_full[t]);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[t], (nb - 1) & 1));
     tc_fence_after();
     if (!ok) {
       report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 200);
@@ -355,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t raw[32];
-        tmem_ld32(lane_base + Cfg::COL_O + c * 32, raw);
+        tmem_ld32(lane_base + col_o + c * 32, raw);
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
@@ -377,14 +398,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 6) tmem_dealloc(tmem, 512);
+  if (warp == kWarpMma) tmem_dealloc(tmem, 512);
 }
 
 template <int D, int GROUP>
 int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& prm,
                    int max_q, cudaStream_t stream) {
   using Cfg = PrefillCfg<D>;
-  constexpr int TOK = kBM / GROUP;
+  constexpr int TOK = kTiles * kBM / GROUP;  // query tokens per CTA
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
