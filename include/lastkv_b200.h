@@ -175,6 +175,8 @@ int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_par
  * q [T, *] row stride q_row, k/v likewise (bf16); positions int64 [T];
  * cos_sin bf16 [max_position, head_dim] = cos | sin halves (NeoX, full head);
  * q_weight / k_weight bf16 [head_dim]; inv_scale fp32 [num_kv_heads] or NULL;
+ * cos_sin == NULL skips RoPE (use_nope) and q_weight == k_weight == NULL skips
+ * the RMSNorm (use_qk_norm = False), as the reference's config switches allow;
  * ring_k/ring_v/src_k/src_v are flat token views [slots, num_kv_heads, head_dim]
  * of the page pool (slot = page * 16 + row).  Out-of-range positions or slots
  * are skipped and recorded in `error_word` (int32[4], may be NULL). */

@@ -63,36 +63,55 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
   if (h >= p.Hq + p.Hkv) return;
   const bool is_q = h < p.Hq;
   const int j = h - p.Hq;  // kv head
-  const int64_t pos = p.pos[t];
-  if (pos < 0 || pos >= p.max_pos) {
-    if (lane == 0) report_error(p.err, DEVERR_BAD_SLOT, 2, (int)pos);
-    return;
-  }
   const __nv_bfloat16* src = is_q ? p.q + (int64_t)t * p.q_row + (int64_t)h * D : p.k + (int64_t)t * p.k_row + (int64_t)j * D;
-  const __nv_bfloat16* cs = p.cos_sin + pos * p.cs_row;
   const int i0 = lane * E;
   float r1[E], r2[E];
-  float ss = 0.f;
+  if (p.cos_sin) {
+    const int64_t pos = p.pos[t];
+    if (pos < 0 || pos >= p.max_pos) {
+      if (lane == 0) report_error(p.err, DEVERR_BAD_SLOT, 2, (int)pos);
+      return;
+    }
+    const __nv_bfloat16* cs = p.cos_sin + pos * p.cs_row;
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float x = __bfloat162float(src[i0 + e]);
-    const float y = __bfloat162float(src[HALF + i0 + e]);
-    const float cc = __bfloat162float(cs[i0 + e]);
-    const float sn = __bfloat162float(cs[HALF + i0 + e]);
-    r1[e] = bf16r(__fmaf_rn(x, cc, -__fmul_rn(y, sn)));
-    r2[e] = bf16r(__fmaf_rn(y, cc, __fmul_rn(x, sn)));
-    ss = __fmaf_rn(r1[e], r1[e], ss);
-    ss = __fmaf_rn(r2[e], r2[e], ss);
+    for (int e = 0; e < E; ++e) {
+      const float x = __bfloat162float(src[i0 + e]);
+      const float y = __bfloat162float(src[HALF + i0 + e]);
+      const float cc = __bfloat162float(cs[i0 + e]);
+      const float sn = __bfloat162float(cs[HALF + i0 + e]);
+      r1[e] = bf16r(__fmaf_rn(x, cc, -__fmul_rn(y, sn)));
+      r2[e] = bf16r(__fmaf_rn(y, cc, __fmul_rn(x, sn)));
+    }
+  } else {  // use_nope: no rotary embedding
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      r1[e] = __bfloat162float(src[i0 + e]);
+      r2[e] = __bfloat162float(src[HALF + i0 + e]);
+    }
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float inv = rsqrtf(__fadd_rn(ss / (float)D, p.eps));
   const __nv_bfloat16* w = is_q ? p.qw : p.kw;
   __nv_bfloat16 o1[E], o2[E];
+  if (w) {
+    float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    o1[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r1[e], inv), __bfloat162float(w[i0 + e])));
-    o2[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r2[e], inv), __bfloat162float(w[HALF + i0 + e])));
+    for (int e = 0; e < E; ++e) {
+      ss = __fmaf_rn(r1[e], r1[e], ss);
+      ss = __fmaf_rn(r2[e], r2[e], ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(__fadd_rn(ss / (float)D, p.eps));
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      o1[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r1[e], inv), __bfloat162float(w[i0 + e])));
+      o2[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r2[e], inv), __bfloat162float(w[HALF + i0 + e])));
+    }
+  } else {  // use_qk_norm = False
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      o1[e] = __float2bfloat16_rn(r1[e]);
+      o2[e] = __float2bfloat16_rn(r2[e]);
+    }
   }
   auto store = [&](__nv_bfloat16* dst, const __nv_bfloat16* a, const __nv_bfloat16* b) {
 #pragma unroll
@@ -197,9 +216,9 @@ int rope_norm_append(const AppendArgs& a) {
   if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
   if (a.num_tokens < 0 || a.num_q_heads < 1 || a.num_kv_heads < 1) return LKV_ERR_INVALID_ARGUMENT;
   if (a.num_tokens == 0) return LKV_OK;
-  if (!a.q || !a.k || !a.v || !a.positions || !a.cos_sin || !a.q_weight || !a.k_weight || !a.q_out ||
-      !a.ring_slot || !a.ring_k || !a.ring_v)
-    return LKV_ERR_INVALID_ARGUMENT;
+  if (!a.q || !a.k || !a.v || !a.q_out || !a.ring_slot || !a.ring_k || !a.ring_v) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.cos_sin && !a.positions) return LKV_ERR_INVALID_ARGUMENT;
+  if ((a.q_weight == nullptr) != (a.k_weight == nullptr)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.src_slot && (!a.src_k || !a.src_v)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.num_tokens > 65535) return LKV_ERR_UNSUPPORTED;  // grid.y limit; callers split larger spans
   AppendParams p{};

@@ -1,0 +1,445 @@
+"""Drop-in LastKV language model whose attention runs on the B200 kernels.
+
+Mirrors the reference's HF implementation (llm/src/lastkv/llm/modeling.py)
+module for module and parameter name for parameter name, so a reference
+state dict loads strictly:
+
+* ``LastKVConfig``        - the config fields the path reads (configuration.py:13-48)
+* ``PagedLastKVCache``    - ``LastKVCache`` (modeling.py:37-67) backed by the merged
+                            paged pool: shared final-layer pages + per-layer 2C rings
+* ``LastKVAttention``     - ``LastKVAttention.forward(hidden, (cos, sin), cache)``
+                            (modeling.py:98-148): q/k/v projection, then one fused
+                            RoPE -> Q/K RMSNorm -> V/s -> paged-append kernel, then
+                            the split-KV decode kernel (one new token) or the tcgen05
+                            prefill kernel (a chunk), output scaled by s_l in-kernel
+* ``LastKVModel`` / ``LastKVForCausalLM`` - the chunk loop and commit
+                            (modeling.py:173-212): spans never cross a chunk
+                            boundary, and a completed chunk is blended into every
+                            layer ring by the blend kernel.
+
+Dense layers (projections, MLP, norms, embedding, LM head) are plain torch
+(cuBLAS); everything on the shared-KV path goes through ``lastkv_b200.ops``.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from . import ops
+from .contract import PAGE_SIZE, RMarinBackendContractError, require_chunk_size, require_heads
+
+
+@dataclass
+class LastKVConfig:
+    hidden_size: int
+    intermediate_size: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    num_hidden_layers: int
+    head_dim: int
+    vocab_size: int
+    chunk_size: int = 1024
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    rope_scaling: dict | None = None
+    max_position_embeddings: int = 8192
+    deep_kv_rescale: bool = True
+    deep_v_scale_init: object = 1.0
+    use_qk_norm: bool = True
+    use_nope: bool = False
+    attention_bias: bool = False
+    tie_word_embeddings: bool = False
+    initializer_range: float = 0.02
+    extra: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        require_chunk_size(self.chunk_size)
+        require_heads(self.num_attention_heads, self.num_key_value_heads, self.head_dim)
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "LastKVConfig":
+        known = {f for f in cls.__dataclass_fields__ if f != "extra"}
+        kw = {k: v for k, v in d.items() if k in known}
+        return cls(**kw, extra={k: v for k, v in d.items() if k not in known})
+
+
+def _llama3_inv_freq(inv_freq: torch.Tensor, scaling: dict) -> torch.Tensor:
+    """Llama-3.1 frequency scaling (the published rule: keep high frequencies,
+    divide low ones by ``factor``, interpolate smoothly in between)."""
+    factor = scaling["factor"]
+    low, high = scaling.get("low_freq_factor", 1.0), scaling.get("high_freq_factor", 4.0)
+    old_len = scaling.get("original_max_position_embeddings", 8192)
+    low_wl, high_wl = old_len / low, old_len / high
+    wavelen = 2 * math.pi / inv_freq
+    scaled = torch.where(wavelen > low_wl, inv_freq / factor, inv_freq)
+    smooth = (old_len / wavelen - low) / (high - low)
+    mid = (1 - smooth) * scaled / factor + smooth * scaled
+    is_mid = (wavelen >= high_wl) & (wavelen <= low_wl)
+    return torch.where(is_mid, mid, scaled)
+
+
+class RotaryEmbedding(nn.Module):
+    """NeoX rotary frequencies; returns (cos, sin) [1, L, D] like the HF module."""
+
+    def __init__(self, config: LastKVConfig, device=None):
+        super().__init__()
+        d = config.head_dim
+        inv = 1.0 / (config.rope_theta ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
+        if config.rope_scaling and config.rope_scaling.get("rope_type", config.rope_scaling.get("type")) == "llama3":
+            inv = _llama3_inv_freq(inv, config.rope_scaling)
+        self.register_buffer("inv_freq", inv.to(device) if device else inv, persistent=False)
+
+    @torch.no_grad()
+    def forward(self, x, position_ids):
+        freqs = position_ids[..., None].float() * self.inv_freq.to(x.device)[None, None, :]
+        emb = torch.cat((freqs, freqs), dim=-1)
+        return emb.cos().to(x.dtype), emb.sin().to(x.dtype)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim, eps):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.variance_epsilon = eps
+
+    def forward(self, x):
+        dt = x.dtype
+        h = x.float()
+        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.variance_epsilon)
+        return self.weight * h.to(dt)
+
+
+class MLP(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.gate_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
+        self.up_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
+
+    def forward(self, x):
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+# ----------------------------------------------------------------------- cache
+
+
+class PagedLastKVCache:
+    """``LastKVCache`` on the merged paged pool, for ``batch`` unpadded sequences.
+
+    Layout (batching.py:1999-2016): pages ``[0, src)`` hold each sequence's shared
+    final-layer history (raw K, raw V), ``pages_per_seq`` per sequence (the
+    page order may be shuffled); layer ``l`` owns ``2C/16`` ring pages per
+    sequence at ``ring_base[l] + b * ring_pages`` holding K and V / s_l.
+    ``seen_tokens``, ``get_seq_length`` and ``reorder_cache`` keep the
+    reference's meaning (modeling.py:56-67).
+    """
+
+    def __init__(self, config: LastKVConfig, batch: int, max_tokens: int, device=None, *, page_order=None):
+        self.num_layers = config.num_hidden_layers
+        self.chunk_size = config.chunk_size
+        self.batch = batch
+        self.max_tokens = max_tokens
+        self.hkv, self.d = config.num_key_value_heads, config.head_dim
+        self.seen_tokens = 0
+        self.committed = 0
+        device = torch.device(device or "cuda")
+        self.device = device
+        C = self.chunk_size
+        self.pages_per_seq = -(-max_tokens // PAGE_SIZE)
+        self.ring_pages = 2 * C // PAGE_SIZE
+        self.ring_tokens = 2 * C
+        self.src_pages = batch * self.pages_per_seq
+        self.ring_stride = self.ring_pages * batch + 1
+        self.num_pages = self.src_pages + self.num_layers * self.ring_stride
+        shape = (self.num_pages, PAGE_SIZE, self.hkv, self.d)
+        self.pool_k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.pool_v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        order = np.arange(self.src_pages) if page_order is None else np.asarray(page_order)
+        if sorted(order.tolist()) != list(range(self.src_pages)):
+            raise RMarinBackendContractError("page_order must permute the shared pages")
+        self.src_table = order.reshape(batch, self.pages_per_seq).astype(np.int32)
+        self.src_table_dev = torch.from_numpy(self.src_table).to(device)
+        self.ring_base = self.src_pages + np.arange(self.num_layers) * self.ring_stride
+        self.ring_base_dev = torch.from_numpy(self.ring_base.astype(np.int32)).to(device)
+        self.error_word = torch.zeros(4, dtype=torch.int32, device=device)
+        self.workspace = ops.Workspace.for_decode(batch, config.num_attention_heads, self.d,
+                                                  self.pages_per_seq + self.ring_pages, device=device)
+        self._meta = None
+
+    # -- reference API
+    def get_seq_length(self, layer_idx=0):
+        return self.seen_tokens
+
+    def reorder_cache(self, beam_idx):
+        """Reorder sequences (beam search): gather shared pages and rings by beam index."""
+        idx = beam_idx.to("cpu").long().numpy()
+        src_old = self.src_table[idx].reshape(-1)
+        src_new = self.src_table.reshape(-1)
+        ring_old = (idx[:, None] * self.ring_pages + np.arange(self.ring_pages)[None]).reshape(-1)
+        ring_new = (np.arange(self.batch)[:, None] * self.ring_pages + np.arange(self.ring_pages)[None]).reshape(-1)
+        old = [src_old] + [self.ring_base[l] + ring_old for l in range(self.num_layers)]
+        new = [src_new] + [self.ring_base[l] + ring_new for l in range(self.num_layers)]
+        o = torch.from_numpy(np.concatenate(old)).to(self.device)
+        n = torch.from_numpy(np.concatenate(new)).to(self.device)
+        for pool in (self.pool_k, self.pool_v):
+            pool[n] = pool.index_select(0, o)
+        self._meta = None
+
+    # -- per-span metadata (shared by all layers of one chunk piece)
+    def plan_host(self, n_new: int) -> dict:
+        """Host part of the span plan (fastpath.py:427-454 / 373-424) as numpy arrays."""
+        C, P = self.chunk_size, PAGE_SIZE
+        start = self.seen_tokens
+        last = start + n_new - 1
+        if last >= self.max_tokens:
+            raise RMarinBackendContractError(f"cache capacity {self.max_tokens} exceeded")
+        if (start // C) != (last // C):
+            raise RMarinBackendContractError("a span may not cross a chunk boundary")
+        cur = (last // C) * C
+        rec = max(0, cur - C)
+        nsrc = rec // P
+        window = last + 1 - rec
+        npages = -(-window // P)
+        first = (rec // P) % self.ring_pages
+        B = self.batch
+        W = nsrc + npages
+        bt = np.zeros((B, W), np.int32)
+        for b in range(B):
+            bt[b, :nsrc] = self.src_table[b, :nsrc]
+            bt[b, nsrc:] = b * self.ring_pages + (first + np.arange(npages)) % self.ring_pages
+        pos = start + np.arange(n_new)
+        ring_tok = (np.arange(B)[:, None] * self.ring_tokens + (pos % self.ring_tokens)[None, :]).reshape(-1)
+        src_tok = (self.src_table[:, pos // P] * P + (pos % P)[None, :]).reshape(-1)
+        return {"bt": bt, "nsrc": nsrc, "W": W, "seq_k": last + 1, "ring_tok": ring_tok.astype(np.int64),
+                "src_tok": src_tok.astype(np.int64)}
+
+    def plan(self, n_new: int):
+        h = self.plan_host(n_new)
+        B, dev = self.batch, self.device
+        bt_d = torch.from_numpy(h["bt"]).to(dev)
+        nsrc_d = torch.full((B,), h["nsrc"], dtype=torch.int32, device=dev)
+        meta = {
+            "n": n_new, "W": h["W"],
+            "bt_all": ops.build_layer_block_tables(bt_d, nsrc_d, self.ring_base_dev),
+            "seq_k": torch.full((B,), h["seq_k"], dtype=torch.int32, device=dev),
+            "cu_q": torch.arange(0, (B + 1) * n_new, n_new, dtype=torch.int32, device=dev),
+            "local_pos": torch.arange(n_new, device=dev, dtype=torch.int64).repeat(B),
+            "ring_tok": torch.from_numpy(h["ring_tok"]).to(dev),
+            "src_slot": torch.from_numpy(h["src_tok"]).to(dev),
+        }
+        self._meta = meta
+        return meta
+
+    def advance(self, n_new: int):
+        self.seen_tokens += n_new
+        self._meta = None
+
+    def commit(self, alpha: torch.Tensor):
+        """Blend the chunk that just completed into every layer ring (modeling.py:203-207)."""
+        C, P = self.chunk_size, PAGE_SIZE
+        end = self.seen_tokens
+        if end % C or end == self.committed:
+            return
+        if end != self.committed + C:
+            raise RMarinBackendContractError("boundary commits must be contiguous and exactly one chunk")
+        pages = np.arange((end - C) // P, end // P)
+        raw = self.src_table[:, pages]
+        ring_first = ((end - C) % self.ring_tokens) // P
+        ring = (self.ring_base[0] + np.arange(self.batch)[:, None] * self.ring_pages
+                + ring_first + np.arange(C // P)[None, :])
+        ops.blend_chunk(self.pool_k, self.pool_v, torch.from_numpy(raw.astype(np.int32)).to(self.device),
+                        torch.from_numpy(ring.astype(np.int32)).to(self.device), self.ring_stride, alpha,
+                        error_word=self.error_word)
+        self.committed = end
+
+    def check_errors(self):
+        e = self.error_word.cpu().tolist()
+        w = self.workspace.error()
+        if e[0] or w[0]:
+            raise RMarinBackendContractError(f"device error word set: append/blend {e}, decode {w}")
+
+
+# ----------------------------------------------------------------------- attention
+
+
+class LastKVAttention(nn.Module):
+    """Same parameters and call signature as the reference (modeling.py:70-148)."""
+
+    def __init__(self, config: LastKVConfig, layer_idx: int):
+        super().__init__()
+        self.config = config
+        self.layer_idx = layer_idx
+        self.head_dim = config.head_dim
+        self.num_heads = config.num_attention_heads
+        self.num_key_value_heads = config.num_key_value_heads
+        h, d = config.hidden_size, config.head_dim
+        self.q_proj = nn.Linear(h, self.num_heads * d, bias=config.attention_bias)
+        self.k_proj = nn.Linear(h, self.num_key_value_heads * d, bias=config.attention_bias)
+        self.v_proj = nn.Linear(h, self.num_key_value_heads * d, bias=config.attention_bias)
+        self.o_proj = nn.Linear(self.num_heads * d, h, bias=config.attention_bias)
+        self.prev_chunk_alphas = nn.Parameter(torch.zeros(self.num_key_value_heads))
+        if config.deep_kv_rescale:
+            init = config.deep_v_scale_init
+            value = init[layer_idx] if isinstance(init, (list, tuple)) else init
+            values = value if isinstance(value, (list, tuple)) else [value] * self.num_key_value_heads
+            if len(values) != self.num_key_value_heads:
+                raise ValueError("deep_v_scale_init must match the number of KV heads")
+            self.deep_v_scale = nn.Parameter(torch.tensor(values, dtype=torch.float32))
+        if config.use_qk_norm:
+            self.q_norm = RMSNorm(d, config.rms_norm_eps)
+            self.k_norm = RMSNorm(d, config.rms_norm_eps)
+
+    def value_scale(self) -> torch.Tensor:
+        """s_l per KV head as the pool sees it: bf16-exact values (batching.py:1070-1080)."""
+        if not self.config.deep_kv_rescale:
+            return torch.ones(self.num_key_value_heads, device=self.q_proj.weight.device)
+        return self.deep_v_scale.detach().to(torch.bfloat16).float()
+
+    def blend_alpha(self) -> torch.Tensor:
+        """sigmoid of the bf16 logits, rounded to bf16 (batching.py:1067-1079)."""
+        return self.prev_chunk_alphas.detach().to(torch.bfloat16).sigmoid().float()
+
+    def forward(self, hidden_states, position_embeddings, cache: PagedLastKVCache):
+        B, L, _ = hidden_states.shape
+        D, Hq, Hkv = self.head_dim, self.num_heads, self.num_key_value_heads
+        meta = cache._meta if cache._meta is not None and cache._meta["n"] == L else cache.plan(L)
+        q = self.q_proj(hidden_states).reshape(B * L, Hq * D)
+        k = self.k_proj(hidden_states).reshape(B * L, Hkv * D)
+        v = self.v_proj(hidden_states).reshape(B * L, Hkv * D)
+        if q.dtype != torch.bfloat16:
+            q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+        cs = None
+        if not self.config.use_nope:
+            cos, sin = position_embeddings
+            cs = torch.cat((cos[0, :, : D // 2], sin[0, :, : D // 2]), dim=-1).to(torch.bfloat16).contiguous()
+        s = self.value_scale()
+        inv = (1.0 / s).contiguous()
+        top = self.layer_idx == cache.num_layers - 1
+        flat_k = cache.pool_k.view(-1, Hkv, D)
+        flat_v = cache.pool_v.view(-1, Hkv, D)
+        ring_slot = meta["ring_tok"] + int(cache.ring_base[self.layer_idx]) * PAGE_SIZE
+        qn = getattr(self, "q_norm", None)
+        kn = getattr(self, "k_norm", None)
+        q_out = ops.rope_norm_append(
+            q, k, v, meta["local_pos"], cs,
+            qn.weight.detach().to(torch.bfloat16) if qn is not None else None,
+            kn.weight.detach().to(torch.bfloat16) if kn is not None else None,
+            self.config.rms_norm_eps, inv, ring_slot, flat_k, flat_v,
+            meta["src_slot"] if top else None, flat_k if top else None, flat_v if top else None,
+            error_word=cache.error_word)
+        out_scale = s.repeat_interleave(Hq // Hkv).contiguous()
+        bt = meta["bt_all"][self.layer_idx]
+        if L == 1:
+            out = ops.decode_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], out_scale=out_scale,
+                                   workspace=cache.workspace, max_pages=meta["W"])
+        else:
+            out = ops.prefill_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], meta["cu_q"], L,
+                                    out_scale=out_scale, error_word=cache.error_word, max_pages=meta["W"])
+        out = out.view(B, L, Hq * D).to(hidden_states.dtype)
+        return self.o_proj(out)
+
+
+class LastKVDecoderLayer(nn.Module):
+    def __init__(self, config, layer_idx):
+        super().__init__()
+        self.self_attn = LastKVAttention(config, layer_idx)
+        self.mlp = MLP(config)
+        self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+
+    def forward(self, hidden_states, position_embeddings, cache):
+        hidden_states = hidden_states + self.self_attn(self.input_layernorm(hidden_states), position_embeddings, cache)
+        return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+
+
+class LastKVModel(nn.Module):
+    def __init__(self, config: LastKVConfig):
+        super().__init__()
+        self.config = config
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList(LastKVDecoderLayer(config, i) for i in range(config.num_hidden_layers))
+        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.rotary_emb = RotaryEmbedding(config)
+
+    def forward(self, input_ids, cache: PagedLastKVCache):
+        """Chunk loop of modeling.py:194-208: split at chunk boundaries, commit after all layers."""
+        hidden = self.embed_tokens(input_ids)
+        B, length, _ = hidden.shape
+        if not length:
+            raise ValueError("At least one new token is required")
+        if cache.chunk_size != self.config.chunk_size or cache.num_layers != len(self.layers):
+            raise ValueError("Cache architecture does not match this model")
+        C = self.config.chunk_size
+        outputs = []
+        start = 0
+        while start < length:
+            take = min(length - start, C - cache.seen_tokens % C)
+            chunk = hidden[:, start:start + take]
+            pos = torch.arange(cache.seen_tokens, cache.seen_tokens + take, device=hidden.device)[None]
+            position_embeddings = self.rotary_emb(chunk, pos)
+            cache.plan(take)
+            for layer in self.layers:
+                chunk = layer(chunk, position_embeddings, cache)
+            outputs.append(chunk)
+            cache.advance(take)
+            if cache.seen_tokens % C == 0:
+                cache.commit(self.blend_alpha())
+            start += take
+        return self.norm(torch.cat(outputs, dim=1))
+
+    def blend_alpha(self) -> torch.Tensor:
+        cached = getattr(self, "_alpha", None)
+        if cached is None:
+            cached = torch.stack([l.self_attn.blend_alpha() for l in self.layers]).contiguous()
+            self._alpha = cached
+        return cached
+
+
+class LastKVForCausalLM(nn.Module):
+    """``CustomRecurrentMarinAKV254ReuseKVForCausalLM`` (modeling.py:215-293) on the B200 path."""
+
+    def __init__(self, config: LastKVConfig):
+        super().__init__()
+        self.config = config
+        self.model = LastKVModel(config)
+        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+
+    def new_cache(self, batch: int, max_tokens: int, **kw) -> PagedLastKVCache:
+        return PagedLastKVCache(self.config, batch, max_tokens, device=self.lm_head.weight.device, **kw)
+
+    def forward(self, input_ids, past_key_values: PagedLastKVCache, logits_to_keep: int = 0):
+        if not isinstance(past_key_values, PagedLastKVCache):
+            raise TypeError("Use a PagedLastKVCache created by this model")
+        hidden = self.model(input_ids, past_key_values)
+        if logits_to_keep:
+            hidden = hidden[:, -logits_to_keep:]
+        return self.lm_head(hidden), past_key_values
+
+    @torch.no_grad()
+    def generate_greedy(self, prompt, max_new_tokens: int, cache: PagedLastKVCache | None = None):
+        cache = cache or self.new_cache(prompt.shape[0], prompt.shape[1] + max_new_tokens)
+        logits, _ = self(prompt, cache, logits_to_keep=1)
+        out = [prompt]
+        nxt = logits[:, -1].float().argmax(-1, keepdim=True)
+        for _ in range(max_new_tokens):
+            out.append(nxt)
+            if len(out) - 1 == max_new_tokens:
+                break
+            logits, _ = self(nxt, cache, logits_to_keep=1)
+            nxt = logits[:, -1].float().argmax(-1, keepdim=True)
+        return torch.cat(out, dim=1)
+
+    def load_reference_state_dict(self, state: dict, strict: bool = True):
+        """Load the reference's tensor names (strict, as modeling.py:243-249 requires)."""
+        missing, unexpected = self.load_state_dict(state, strict=False)
+        if strict and (missing or unexpected):
+            raise ValueError(f"Checkpoint is not a strict LastKV model match: missing={missing}, "
+                             f"unexpected={unexpected}")
+        self.model._alpha = None
+        return self

@@ -178,20 +178,26 @@ def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_s
     [slots, Hkv, D] of the pools.  Returns q_out [T, Hq, D].
     """
     T = q.shape[0]
-    D = cos_sin.shape[-1]
+    D = ring_k.shape[-1]
     Hq, Hkv = q.shape[-1] // D, k.shape[-1] // D
     require_heads(Hq, Hkv, D)
     for name, t in (("q", q), ("k", k), ("v", v)):
         _require(t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1, f"{name} must be bf16 [T, H*D] rows")
-    _require(positions.dtype == torch.int64 and ring_slot.dtype == torch.int64, "positions/slots must be int64")
-    _require(cos_sin.dtype == torch.bfloat16 and cos_sin.stride(1) == 1, "cos_sin must be bf16 [max_pos, D]")
-    _require(q_weight.dtype == torch.bfloat16 and k_weight.dtype == torch.bfloat16, "norm weights must be bf16")
+    _require(ring_slot.dtype == torch.int64, "slots must be int64")
+    if cos_sin is not None:  # None: use_nope (no rotary)
+        _require(positions.dtype == torch.int64, "positions must be int64")
+        _require(cos_sin.dtype == torch.bfloat16 and cos_sin.stride(1) == 1 and cos_sin.shape[-1] == D,
+                 "cos_sin must be bf16 [max_pos, D]")
+    _require((q_weight is None) == (k_weight is None), "q/k norm weights come together (None: use_qk_norm=False)")
+    if q_weight is not None:
+        _require(q_weight.dtype == torch.bfloat16 and k_weight.dtype == torch.bfloat16, "norm weights must be bf16")
     if q_out is None:
         q_out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
     top = src_slot is not None
     st = _capi.lib().lkv_rope_norm_append(
-        q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), positions.data_ptr(),
-        cos_sin.data_ptr(), cos_sin.stride(0), cos_sin.shape[0], q_weight.data_ptr(), k_weight.data_ptr(),
+        q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), _ptr(positions),
+        _ptr(cos_sin), cos_sin.stride(0) if cos_sin is not None else 0,
+        cos_sin.shape[0] if cos_sin is not None else 0, _ptr(q_weight), _ptr(k_weight),
         float(eps), _ptr(inv_scale), q_out.data_ptr(), q_out.stride(0), ring_slot.data_ptr(),
         ring_k.data_ptr(), ring_v.data_ptr(), ring_k.shape[0],
         _ptr(src_slot), _ptr(src_k) if top else None, _ptr(src_v) if top else None,

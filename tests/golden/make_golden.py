@@ -208,8 +208,11 @@ def main():
     state = {f"w_{k}": v.detach().numpy().astype(np.float32) for k, v in model.state_dict().items()}
     with torch.inference_mode():
         gen = model.generate(tokens[:1, :20], max_new_tokens=24, do_sample=False, use_cache=True)
+        # the logits that chose each generated token (teacher-forced replay of the output)
+        gen_logits = model(gen[:, :-1], use_cache=False).logits[:, 19:].float().numpy()
     data = {"tokens": tokens.numpy(), "segments": np.array(segments), "logits_incremental": logits,
             "generate_prompt": tokens[:1, :20].numpy(), "generate_out": gen.numpy(),
+            "generate_logits": gen_logits,
             "hidden_size": np.int64(model.config.hidden_size),
             "intermediate_size": np.int64(model.config.intermediate_size),
             "vocab_size": np.int64(model.config.vocab_size)}
