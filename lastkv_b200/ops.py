@@ -230,6 +230,10 @@ def build_layer_block_tables(block_table, nsrc, ring_base, out=None):
     L = ring_base.numel()
     if out is None:
         out = torch.empty((L, B, W), dtype=torch.int32, device=block_table.device)
+    _require(out.shape == (L, B, W) and out.is_contiguous() and out.dtype == torch.int32,
+             "out must be a contiguous int32 [L, B, W] tensor")
+    _require(nsrc.dtype == torch.int32 and ring_base.dtype == torch.int32 and block_table.dtype == torch.int32,
+             "block tables, nsrc and ring_base must be int32")
     st = _capi.lib().lkv_build_layer_block_tables(block_table.data_ptr(), block_table.stride(0), nsrc.data_ptr(),
                                                   ring_base.data_ptr(), L, B, W, out.data_ptr(), _stream())
     _capi.check(st, "lkv_build_layer_block_tables")

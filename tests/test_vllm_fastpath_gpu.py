@@ -1,0 +1,112 @@
+"""Serving fast path (prepare + run_layer) on the B200 kernels.
+
+1. The reference's recorded calls: pre-RoPE projections in, attention outputs
+   compared with the reference's SDPA outputs (chunked prefill across two
+   boundaries, then decode), batch 2.
+2. A random multi-step schedule mixing prefill spans and decode steps at
+   different positions per sequence, with boundary commits, checked step by
+   step against the oracle's merged pool driven with the same inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lastkv_oracle as O
+from tests.conftest import golden_calls
+from tests.gpu_helpers import assert_close_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _fast(layers, slots, max_tokens, chunk, hkv, hq, d, order=None, max_tokens_step=256):
+    from lastkv_b200.vllm_backend import SharedKVFastPath, SharedKVPool
+
+    pool = SharedKVPool(num_layers=layers, num_slots=slots, max_sequence_tokens=max_tokens, chunk_size=chunk,
+                        num_kv_heads=hkv, head_dim=d, device="cuda", page_order=order)
+    return pool, SharedKVFastPath(pool, max_batch=8, max_tokens=max_tokens_step, num_q_heads=hq)
+
+
+def test_run_layer_reproduces_reference_calls(small_d128):
+    from lastkv_b200.vllm_backend import Span, rope_cos_sin_cache
+
+    data = small_d128
+    L, C = int(data["num_layers"]), int(data["chunk"])
+    hq, hkv, d = int(data["num_heads"]), int(data["num_kv_heads"]), int(data["head_dim"])
+    B, T = data["tokens"].shape
+    order = np.random.default_rng(2).permutation(B * (-(-T // 16)))
+    pool, fast = _fast(L, B, T, C, hkv, hq, d, order)
+    pool.bind_parameters(torch.from_numpy(data["alpha_logits"]), torch.from_numpy(data["v_scale"]), hq)
+    fast.register_layers([(torch.from_numpy(data["q_norm_w"][l]).cuda(), torch.from_numpy(data["k_norm_w"][l]).cuda())
+                          for l in range(L)], rope_cos_sin_cache(T, d, float(data["rope_theta"])), float(data["eps"]))
+    n_checked = 0
+    for rec in golden_calls(data):
+        layer, start, lq = rec["layer"], rec["start"], rec["lq"]
+        if layer == 0:
+            assert fast.prepare([Span(b, start, lq) for b in range(B)])
+        q = torch.from_numpy(rec["q_proj"].reshape(B * lq, hq * d)).cuda().bfloat16()
+        k = torch.from_numpy(rec["k_proj"].reshape(B * lq, hkv * d)).cuda().bfloat16()
+        v = torch.from_numpy(rec["v_proj"].reshape(B * lq, hkv * d)).cuda().bfloat16()
+        out = torch.empty((B * lq, hq, d), dtype=torch.bfloat16, device="cuda")
+        fast.run_layer(layer, q, k, v, out)
+        exp = rec["out"].transpose(0, 2, 1, 3).reshape(B * lq, hq, d)
+        assert_close_bf16(out.float().cpu().numpy(), exp, what=f"layer {layer} @ {start} x {lq}")
+        n_checked += 1
+    fast.check_errors()
+    assert n_checked == int(data["calln"])
+
+
+def test_mixed_prefill_decode_schedule_matches_oracle():
+    from lastkv_b200.vllm_backend import Span, chunk_aligned_new_tokens, rope_cos_sin_cache
+
+    rng = np.random.default_rng(7)
+    L, slots, C, hkv, hq, d = 3, 3, 32, 2, 8, 128
+    max_tok = 160
+    order = rng.permutation(slots * (max_tok // 16))
+    pool, fast = _fast(L, slots, max_tok, C, hkv, hq, d, order)
+    alpha_logits = rng.standard_normal((L, hkv)).astype(np.float32)
+    v_scale = rng.uniform(0.4, 1.6, (L, hkv)).astype(np.float32)
+    pool.bind_parameters(torch.from_numpy(alpha_logits), torch.from_numpy(v_scale), hq)
+    fast.register_layers([(None, None)] * L, None, 1e-6)  # use_nope / no qk-norm: inputs are final q/k
+    lay = O.PoolLayout(num_layers=L, chunk=C, page=16, num_slots=slots, src_pages=pool.src_pages)
+    state = O.PagedLastKV(layout=lay, hkv=hkv, d=d, batch=slots, alpha=O.alpha_from_logits(alpha_logits),
+                          v_scale=O.bf16_round(v_scale), bf16=True,
+                          src_page_lists=[list(pool.src_table[s]) for s in range(slots)])
+    # per-slot request lengths; each step schedules chunk-aligned spans (prefill) or one token (decode)
+    target = [150, 70, 100]
+    done = [0, 0, 0]
+    prompt = [100, 40, 64]
+    step = 0
+    while any(done[s] < target[s] for s in range(slots)):
+        spans = []
+        for s in range(slots):
+            if done[s] >= target[s]:
+                continue
+            want = prompt[s] - done[s] if done[s] < prompt[s] else 1
+            n = chunk_aligned_new_tokens(done[s], min(want, int(rng.integers(1, 40))), C)
+            spans.append(Span(s, done[s], n))
+        # the oracle commits the previous boundary at the same point the fast path does
+        for sp in spans:
+            state.commit_if_boundary(sp.slot, sp.num_computed_tokens)
+        fast.prepare(spans)
+        T = sum(sp.num_query_tokens for sp in spans)
+        for layer in range(L):
+            q = O.bf16_round(rng.standard_normal((T, hq, d)))
+            k = O.bf16_round(rng.standard_normal((T, hkv, d)))
+            v = O.bf16_round(rng.standard_normal((T, hkv, d)))
+            out = torch.empty((T, hq, d), dtype=torch.bfloat16, device="cuda")
+            fast.run_layer(layer, torch.from_numpy(q).cuda().bfloat16(), torch.from_numpy(k).cuda().bfloat16(),
+                           torch.from_numpy(v).cuda().bfloat16(), out)
+            got = out.float().cpu().numpy()
+            t = 0
+            for sp in spans:
+                n = sp.num_query_tokens
+                state.append(layer, sp.slot, k[t:t + n], v[t:t + n], sp.num_computed_tokens)
+                exp = state.attend(layer, sp.slot, q[t:t + n], sp.num_computed_tokens, scale=d ** -0.5)
+                assert_close_bf16(got[t:t + n], exp, what=f"step {step} layer {layer} slot {sp.slot}")
+                t += n
+        for sp in spans:
+            done[sp.slot] += sp.num_query_tokens
+        step += 1
+    fast.check_errors()
+    assert step > 10
