@@ -80,6 +80,21 @@ def test_decode_partial_then_merge_equals_full():
                       what="merge")
 
 
+def test_context_parallel_layer_single_rank_equals_decode():
+    """ContextParallelDecode's kernel path (partial decode -> merge kernel) on one rank."""
+    from lastkv_b200 import ops
+    from lastkv_b200.context_parallel import ContextParallelDecode
+
+    B, Hq, Hkv, D = 4, 32, 8, 128
+    t, _ = make_paged_case(13, B, Hq, Hkv, D, [9000, 100, 4097, 1])
+    scale = torch.rand(Hq, device="cuda") + 0.5
+    cp = ContextParallelDecode()
+    a = cp.layer(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], out_scale=scale)
+    b = ops.decode_paged(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], out_scale=scale)
+    assert_close_bf16(a.float().cpu().numpy().reshape(B, Hq, D), b.float().cpu().numpy(), max_abs=1.6e-2,
+                      rel_l2=6e-3, what="cp single rank")
+
+
 def test_decode_empty_sequence_and_nan_tail():
     from lastkv_b200 import ops
 
