@@ -222,6 +222,32 @@ def main():
     np.savez_compressed(os.path.join(args.out, "small_d128.npz"), **data)
     print("small_d128:", len(calls), "calls")
 
+    # --- config1: the 124M architecture, 512-token prompt + 128 greedy steps --
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from seeded_weights import CONFIG1, nontrivial_alpha, nontrivial_scale, seeded_state
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    prompt = torch.randint(0, CONFIG1["vocab_size"], (1, 512), generator=torch.Generator().manual_seed(0))
+    out = {"prompt": prompt.numpy()}
+    for tag, chunk, nontrivial in (("c4096", 4096, False), ("c128", 128, True)):
+        config = Config(**CONFIG1, chunk_size=chunk, max_position_embeddings=4096, bos_token_id=1,
+                        eos_token_id=None, pad_token_id=0, attn_implementation="sdpa")
+        with torch.device("meta"):
+            shapes = {k: tuple(v.shape) for k, v in Model(config).state_dict().items()}
+        state = seeded_state(shapes, seed=1, alpha_fn=nontrivial_alpha if nontrivial else None,
+                             scale_fn=nontrivial_scale if nontrivial else None)
+        model = Model(config).eval()
+        missing, unexpected = model.load_state_dict({k: torch.from_numpy(v) for k, v in state.items()}, strict=True)
+        with torch.inference_mode():
+            gen = model.generate(prompt, max_new_tokens=128, do_sample=False, use_cache=True)
+            logits = model(gen[:, :-1], use_cache=False).logits[0, 511:].float()
+        top_v, top_i = logits.topk(8, dim=-1)
+        out[f"{tag}_tokens"] = gen.numpy()
+        out[f"{tag}_top_v"] = top_v.numpy()
+        out[f"{tag}_top_i"] = top_i.numpy()
+        print(f"config1 {tag}: first tokens {gen[0, 512:520].tolist()}")
+    np.savez_compressed(os.path.join(args.out, "config1_124m.npz"), **out)
+
 
 if __name__ == "__main__":
     main()
