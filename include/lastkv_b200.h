@@ -180,6 +180,9 @@ int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_par
  * ring_k/ring_v/src_k/src_v are flat token views [slots, num_kv_heads, head_dim]
  * of the page pool (slot = page * 16 + row).  Out-of-range positions or slots
  * are skipped and recorded in `error_word` (int32[4], may be NULL). */
+#define LKV_ROPE_INTERLEAVED 1 /* rotary pairs (2i, 2i+1) (GPT-J / Wan) instead of (i, i + D/2) */
+#define LKV_ROPE_TABLE_FP32 2  /* cos_sin is fp32 (e.g. per-token 3-D tables) instead of bf16 */
+
 int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_row,
                          const void* v, int64_t v_row, const int64_t* positions,
                          const void* cos_sin, int64_t cos_sin_row, int64_t max_position,
@@ -188,7 +191,23 @@ int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_
                          const int64_t* ring_slot, void* ring_k, void* ring_v, int64_t ring_slots,
                          const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots,
                          int num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
-                         int32_t* error_word, void* stream);
+                         int flags, int32_t* error_word, void* stream);
+
+/* ------------------------------------------------------------------ gather / blend
+ * Token-level commit for histories whose segments do not start on page
+ * boundaries (the Wan block cache: per-layer first-frame prefix, previous
+ * block blended with the shared final-layer history,
+ * videogen/src/lastkv/videogen/model.py:173-195, 217-272, 716-729).  For every
+ * token i (flat pool slots = page * 16 + row), on K and V:
+ *   src_b[i] <  0 : dst = a          (copy)
+ *   src_a[i] <  0 : dst = b          (copy)
+ *   otherwise     : dst = bf16(bf16(x*a) + bf16(bf16(1-x)*b)),  x = alpha[alpha_row[i], head]
+ * with a = source (shared final layer) and b = the layer's own K/V.  dst slots
+ * must not overlap any source slot of the same call. */
+int lkv_gather_blend(void* pool_k, void* pool_v, int64_t num_slots, const int64_t* dst_slot,
+                     const int64_t* src_a_slot, const int64_t* src_b_slot, const int32_t* alpha_row,
+                     const float* alpha, int num_tokens, int num_kv_heads, int head_dim,
+                     int32_t* error_word, void* stream);
 
 /* ------------------------------------------------------------------ blend
  * Chunk-boundary commit; replaces blend_chunk_ / _commit_previous_boundary

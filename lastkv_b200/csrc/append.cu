@@ -30,8 +30,10 @@ struct AppendParams {
   const __nv_bfloat16* v;
   int64_t v_row;
   const int64_t* pos;
-  const __nv_bfloat16* cos_sin;
+  const void* cos_sin;  // bf16 or fp32 [max_pos, D] = cos | sin halves
   int64_t cs_row;
+  int interleaved;  // RoPE pairs (2i, 2i+1) instead of (i, i + D/2)
+  int cs_fp32;
   int64_t max_pos;
   const __nv_bfloat16* qw;
   const __nv_bfloat16* kw;
@@ -65,6 +67,9 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
   const int j = h - p.Hq;  // kv head
   const __nv_bfloat16* src = is_q ? p.q + (int64_t)t * p.q_row + (int64_t)h * D : p.k + (int64_t)t * p.k_row + (int64_t)j * D;
   const int i0 = lane * E;
+  // element indices of the two members of rotary pair (i0 + e): NeoX halves or interleaved
+  auto ix1 = [&](int e) { return p.interleaved ? 2 * (i0 + e) : i0 + e; };
+  auto ix2 = [&](int e) { return p.interleaved ? 2 * (i0 + e) + 1 : HALF + i0 + e; };
   float r1[E], r2[E];
   if (p.cos_sin) {
     const int64_t pos = p.pos[t];
@@ -72,21 +77,28 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
       if (lane == 0) report_error(p.err, DEVERR_BAD_SLOT, 2, (int)pos);
       return;
     }
-    const __nv_bfloat16* cs = p.cos_sin + pos * p.cs_row;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      const float x = __bfloat162float(src[i0 + e]);
-      const float y = __bfloat162float(src[HALF + i0 + e]);
-      const float cc = __bfloat162float(cs[i0 + e]);
-      const float sn = __bfloat162float(cs[HALF + i0 + e]);
+      const float x = __bfloat162float(src[ix1(e)]);
+      const float y = __bfloat162float(src[ix2(e)]);
+      float cc, sn;
+      if (p.cs_fp32) {
+        const float* cs = static_cast<const float*>(p.cos_sin) + pos * p.cs_row;
+        cc = cs[i0 + e];
+        sn = cs[HALF + i0 + e];
+      } else {
+        const __nv_bfloat16* cs = static_cast<const __nv_bfloat16*>(p.cos_sin) + pos * p.cs_row;
+        cc = __bfloat162float(cs[i0 + e]);
+        sn = __bfloat162float(cs[HALF + i0 + e]);
+      }
       r1[e] = bf16r(__fmaf_rn(x, cc, -__fmul_rn(y, sn)));
       r2[e] = bf16r(__fmaf_rn(y, cc, __fmul_rn(x, sn)));
     }
   } else {  // use_nope: no rotary embedding
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      r1[e] = __bfloat162float(src[i0 + e]);
-      r2[e] = __bfloat162float(src[HALF + i0 + e]);
+      r1[e] = __bfloat162float(src[ix1(e)]);
+      r2[e] = __bfloat162float(src[ix2(e)]);
     }
   }
   const __nv_bfloat16* w = is_q ? p.qw : p.kw;
@@ -103,8 +115,8 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
     const float inv = rsqrtf(__fadd_rn(ss / (float)D, p.eps));
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      o1[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r1[e], inv), __bfloat162float(w[i0 + e])));
-      o2[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r2[e], inv), __bfloat162float(w[HALF + i0 + e])));
+      o1[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r1[e], inv), __bfloat162float(w[ix1(e)])));
+      o2[e] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r2[e], inv), __bfloat162float(w[ix2(e)])));
     }
   } else {  // use_qk_norm = False
 #pragma unroll
@@ -116,8 +128,8 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
   auto store = [&](__nv_bfloat16* dst, const __nv_bfloat16* a, const __nv_bfloat16* b) {
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      dst[i0 + e] = a[e];
-      dst[HALF + i0 + e] = b[e];
+      dst[ix1(e)] = a[e];
+      dst[ix2(e)] = b[e];
     }
   };
   if (is_q) {
@@ -132,8 +144,8 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
   const float is = p.inv_scale ? p.inv_scale[j] : 1.f;
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    va[e] = vsrc[i0 + e];
-    vb[e] = vsrc[HALF + i0 + e];
+    va[e] = vsrc[ix1(e)];
+    vb[e] = vsrc[ix2(e)];
     vsa[e] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(va[e]), is));
     vsb[e] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(vb[e]), is));
   }
@@ -200,6 +212,88 @@ __global__ void __launch_bounds__(256) blend_chunk_kernel(const BlendParams p) {
   }
 }
 
+struct GatherBlendParams {
+  __nv_bfloat16* pool_k;
+  __nv_bfloat16* pool_v;
+  int64_t num_slots;
+  const int64_t* dst;
+  const int64_t* src_a;
+  const int64_t* src_b;
+  const int32_t* alpha_row;
+  const float* alpha;
+  int Hkv, D;
+  int* err;
+};
+
+// One CTA per token: copy or blend the token's Hkv x D row of K and of V.
+__global__ void __launch_bounds__(128) gather_blend_kernel(const GatherBlendParams p) {
+  const int i = blockIdx.x;
+  const int64_t dst = p.dst[i], a = p.src_a[i], b = p.src_b[i];
+  const bool ok = dst >= 0 && dst < p.num_slots && a < p.num_slots && b < p.num_slots && (a >= 0 || b >= 0);
+  if (!ok) {
+    if (threadIdx.x == 0) report_error(p.err, DEVERR_BAD_SLOT, 5, i);
+    return;
+  }
+  const int row = p.Hkv * p.D;
+  const int vecs = row / 8;
+#pragma unroll 1
+  for (int which = 0; which < 2; ++which) {
+    __nv_bfloat16* pool = which ? p.pool_v : p.pool_k;
+    uint4* d = reinterpret_cast<uint4*>(pool + dst * row);
+    const uint4* sa = a >= 0 ? reinterpret_cast<const uint4*>(pool + a * row) : nullptr;
+    const uint4* sb = b >= 0 ? reinterpret_cast<const uint4*>(pool + b * row) : nullptr;
+    for (int vi = threadIdx.x; vi < vecs; vi += blockDim.x) {
+      if (!sb) {
+        d[vi] = sa[vi];
+        continue;
+      }
+      if (!sa) {
+        d[vi] = sb[vi];
+        continue;
+      }
+      const int head = vi * 8 / p.D;
+      const float al = p.alpha[(int64_t)p.alpha_row[i] * p.Hkv + head];
+      const float ia = bf16r(__fsub_rn(1.f, al));
+      uint4 av = sa[vi], bv = sb[vi];
+      uint32_t* x = reinterpret_cast<uint32_t*>(&av);
+      uint32_t* y = reinterpret_cast<uint32_t*>(&bv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float t1l = bf16r(__fmul_rn(al, bf16_lo(x[e]))), t1h = bf16r(__fmul_rn(al, bf16_hi(x[e])));
+        const float t3l = bf16r(__fmul_rn(ia, bf16_lo(y[e]))), t3h = bf16r(__fmul_rn(ia, bf16_hi(y[e])));
+        y[e] = pack_bf16(__fadd_rn(t1l, t3l), __fadd_rn(t1h, t3h));
+      }
+      d[vi] = bv;
+    }
+  }
+}
+
+int gather_blend(void* pool_k, void* pool_v, int64_t num_slots, const int64_t* dst, const int64_t* src_a,
+                 const int64_t* src_b, const int32_t* alpha_row, const float* alpha, int num_tokens,
+                 int num_kv_heads, int head_dim, int32_t* error_word, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (num_tokens < 0 || num_kv_heads < 1) return LKV_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return LKV_OK;
+  if (!pool_k || !pool_v || !dst || !src_a || !src_b || !alpha_row || !alpha) return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(pool_k) & 15) || (reinterpret_cast<uintptr_t>(pool_v) & 15))
+    return LKV_ERR_INVALID_ARGUMENT;
+  if (num_tokens > 2147483647) return LKV_ERR_UNSUPPORTED;
+  GatherBlendParams p{};
+  p.pool_k = static_cast<__nv_bfloat16*>(pool_k);
+  p.pool_v = static_cast<__nv_bfloat16*>(pool_v);
+  p.num_slots = num_slots;
+  p.dst = dst;
+  p.src_a = src_a;
+  p.src_b = src_b;
+  p.alpha_row = alpha_row;
+  p.alpha = alpha;
+  p.Hkv = num_kv_heads;
+  p.D = head_dim;
+  p.err = error_word;
+  gather_blend_kernel<<<num_tokens, 128, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
 __global__ void build_block_tables_kernel(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc,
                                           const int32_t* ring_base, int L, int B, int W, int32_t* bt_all) {
   const int64_t total = (int64_t)L * B * W;
@@ -229,8 +323,10 @@ int rope_norm_append(const AppendArgs& a) {
   p.v = static_cast<const __nv_bfloat16*>(a.v);
   p.v_row = a.v_row;
   p.pos = a.positions;
-  p.cos_sin = static_cast<const __nv_bfloat16*>(a.cos_sin);
+  p.cos_sin = a.cos_sin;
   p.cs_row = a.cos_sin_row;
+  p.interleaved = (a.flags & LKV_ROPE_INTERLEAVED) ? 1 : 0;
+  p.cs_fp32 = (a.flags & LKV_ROPE_TABLE_FP32) ? 1 : 0;
   p.max_pos = a.max_position;
   p.qw = static_cast<const __nv_bfloat16*>(a.q_weight);
   p.kw = static_cast<const __nv_bfloat16*>(a.k_weight);

@@ -168,7 +168,8 @@ int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_
                          const void* q_weight, const void* k_weight, float eps, const float* inv_scale, void* q_out,
                          int64_t q_out_row, const int64_t* ring_slot, void* ring_k, void* ring_v, int64_t ring_slots,
                          const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots, int num_tokens,
-                         int num_q_heads, int num_kv_heads, int head_dim, int32_t* error_word, void* stream) {
+                         int num_q_heads, int num_kv_heads, int head_dim, int flags, int32_t* error_word,
+                         void* stream) {
   lkv::AppendArgs a{};
   a.q = q;
   a.q_row = q_row;
@@ -198,9 +199,18 @@ int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_
   a.num_q_heads = num_q_heads;
   a.num_kv_heads = num_kv_heads;
   a.head_dim = head_dim;
+  a.flags = flags;
   a.error_word = error_word;
   a.stream = stream;
   return lkv::rope_norm_append(a);
+}
+
+int lkv_gather_blend(void* pool_k, void* pool_v, int64_t num_slots, const int64_t* dst_slot,
+                     const int64_t* src_a_slot, const int64_t* src_b_slot, const int32_t* alpha_row,
+                     const float* alpha, int num_tokens, int num_kv_heads, int head_dim, int32_t* error_word,
+                     void* stream) {
+  return lkv::gather_blend(pool_k, pool_v, num_slots, dst_slot, src_a_slot, src_b_slot, alpha_row, alpha,
+                           num_tokens, num_kv_heads, head_dim, error_word, static_cast<cudaStream_t>(stream));
 }
 
 int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages, const int32_t* raw_pages,

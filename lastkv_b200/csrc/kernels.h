@@ -92,10 +92,15 @@ struct AppendArgs {
   void* src_v;
   int64_t src_slots;
   int num_tokens, num_q_heads, num_kv_heads, head_dim;
+  int flags;  // LKV_ROPE_INTERLEAVED | LKV_ROPE_TABLE_FP32
   int32_t* error_word;
   void* stream;
 };
 int rope_norm_append(const AppendArgs& a);
+
+int gather_blend(void* pool_k, void* pool_v, int64_t num_slots, const int64_t* dst, const int64_t* src_a,
+                 const int64_t* src_b, const int32_t* alpha_row, const float* alpha, int num_tokens,
+                 int num_kv_heads, int head_dim, int32_t* error_word, cudaStream_t stream);
 
 struct BlendArgs {
   void* pool_k;

@@ -170,12 +170,13 @@ def merge_partials(o_parts, lse_parts, *, out_scale=None, out=None, lse_out=None
 
 
 def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_scale, ring_slot, ring_k, ring_v,
-                     src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None):
+                     src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None, interleaved=False):
     """Fused RoPE -> Q/K RMSNorm -> V/s -> paged append for one layer.
 
     q [T, Hq*D], k/v [T, Hkv*D] bf16 (row-strided views allowed); positions
-    int64 [T]; cos_sin bf16 [max_pos, D]; ring_* / src_* flat token views
-    [slots, Hkv, D] of the pools.  Returns q_out [T, Hq, D].
+    int64 [T]; cos_sin bf16 or fp32 [max_pos, D] (cos | sin halves) or None;
+    ``interleaved`` rotates pairs (2i, 2i+1) instead of (i, i + D/2); ring_* /
+    src_* flat token views [slots, Hkv, D] of the pools.  Returns q_out [T, Hq, D].
     """
     T = q.shape[0]
     D = ring_k.shape[-1]
@@ -186,8 +187,9 @@ def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_s
     _require(ring_slot.dtype == torch.int64, "slots must be int64")
     if cos_sin is not None:  # None: use_nope (no rotary)
         _require(positions.dtype == torch.int64, "positions must be int64")
-        _require(cos_sin.dtype == torch.bfloat16 and cos_sin.stride(1) == 1 and cos_sin.shape[-1] == D,
-                 "cos_sin must be bf16 [max_pos, D]")
+        _require(cos_sin.dtype in (torch.bfloat16, torch.float32) and cos_sin.stride(1) == 1
+                 and cos_sin.shape[-1] == D, "cos_sin must be bf16 or fp32 [max_pos, D]")
+    flags = (1 if interleaved else 0) | (2 if cos_sin is not None and cos_sin.dtype == torch.float32 else 0)
     _require((q_weight is None) == (k_weight is None), "q/k norm weights come together (None: use_qk_norm=False)")
     if q_weight is not None:
         _require(q_weight.dtype == torch.bfloat16 and k_weight.dtype == torch.bfloat16, "norm weights must be bf16")
@@ -201,9 +203,28 @@ def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_s
         float(eps), _ptr(inv_scale), q_out.data_ptr(), q_out.stride(0), ring_slot.data_ptr(),
         ring_k.data_ptr(), ring_v.data_ptr(), ring_k.shape[0],
         _ptr(src_slot), _ptr(src_k) if top else None, _ptr(src_v) if top else None,
-        src_k.shape[0] if top else 0, T, Hq, Hkv, D, _ptr(error_word), _stream())
+        src_k.shape[0] if top else 0, T, Hq, Hkv, D, flags, _ptr(error_word), _stream())
     _capi.check(st, "lkv_rope_norm_append")
     return q_out
+
+
+def gather_blend(pool_k, pool_v, dst, src_a, src_b, alpha_row, alpha, *, error_word=None):
+    """Token-level copy / blend on the flat pool (see lkv_gather_blend).
+
+    dst, src_a, src_b int64 [N] flat token slots (-1 in src_a or src_b means
+    copy the other); alpha_row int32 [N] row of alpha fp32 [R, Hkv].
+    """
+    _check_pool(pool_k, pool_v)
+    N = dst.numel()
+    for name, t in (("dst", dst), ("src_a", src_a), ("src_b", src_b)):
+        _require(t.dtype == torch.int64 and t.numel() == N and t.is_contiguous(), f"{name} must be int64 [N]")
+    _require(alpha_row.dtype == torch.int32 and alpha_row.numel() == N, "alpha_row must be int32 [N]")
+    _require(alpha.dtype == torch.float32 and alpha.is_contiguous(), "alpha must be fp32 [rows, Hkv]")
+    st = _capi.lib().lkv_gather_blend(pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0] * pool_k.shape[1],
+                                      dst.data_ptr(), src_a.data_ptr(), src_b.data_ptr(), alpha_row.data_ptr(),
+                                      alpha.data_ptr(), N, pool_k.shape[2], pool_k.shape[3], _ptr(error_word),
+                                      _stream())
+    _capi.check(st, "lkv_gather_blend")
 
 
 def blend_chunk(pool_k, pool_v, raw_pages, ring_pages, ring_layer_stride: int, alpha, *, error_word=None):

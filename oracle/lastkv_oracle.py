@@ -468,6 +468,92 @@ def chunk_aligned_new_tokens(num_computed: int, num_new: int, chunk: int) -> int
 
 
 # --------------------------------------------------------------------------
+# Wan causal block attention over a shared final-layer history
+# --------------------------------------------------------------------------
+
+
+def wan_rope_angles(frames: int, fh: int, fw: int, start_frame: int, head_dim: int, theta: float = 10000.0):
+    """Angles [T, D/2] of Wan's causal 3-D RoPE for a block of ``frames`` frames.
+
+    Restates ``rope_params`` (videogen/src/lastkv/videogen/layers.py:24-31), the
+    frequency table split (model.py:568; layers.py:135-136) and
+    ``causal_rope_apply`` (layers.py:126-154): complex pair i of a token at
+    (frame f, row h, col w) rotates by f*inv_t[i] (i < c - 2(c//3)), then
+    h*inv_h, then w*inv_w, with each table over its own sub-dimension.
+    """
+    d = head_dim
+    dims = [d - 4 * (d // 6), 2 * (d // 6), 2 * (d // 6)]
+    inv = [1.0 / theta ** (np.arange(0, dd, 2, dtype=np.float64) / dd) for dd in dims]
+    f, h, w = np.meshgrid(np.arange(frames) + start_frame, np.arange(fh), np.arange(fw), indexing="ij")
+    return np.concatenate([f.reshape(-1, 1) * inv[0][None], h.reshape(-1, 1) * inv[1][None],
+                           w.reshape(-1, 1) * inv[2][None]], axis=1)
+
+
+def rope_interleaved(x, angles) -> np.ndarray:
+    """Rotate pairs (2i, 2i+1) of x [T, H, D] by angles [T, D/2] in float64 (layers.py:141-150)."""
+    x = np.asarray(x, dtype=np.float64)
+    c = np.cos(angles)[:, None, :]
+    s = np.sin(angles)[:, None, :]
+    out = np.empty_like(x)
+    out[..., 0::2] = x[..., 0::2] * c - x[..., 1::2] * s
+    out[..., 1::2] = x[..., 0::2] * s + x[..., 1::2] * c
+    return out
+
+
+class WanHistory:
+    """Per-layer history of one sequence, composed as the reference composes it.
+
+    ``history(layer, start)`` restates ``_compose_history_kv`` (model.py:217-272)
+    with ``history_kv`` (cache.py:58-65) and ``_blend_first_local_kv_segment``
+    (model.py:173-195): [per-layer prefix | shared final-layer K/V | previous
+    block = a*shared + (1-a)*layer-local, first-frame tokens kept local].
+    ``commit(start, kvs)`` restates ``_update_caches_akv`` (model.py:716-729).
+    Arrays are [T, H, D]; ``alpha`` [L, H] are the sigmoid'ed block weights.
+    """
+
+    def __init__(self, num_layers: int, prefix_tokens: int, block_tokens: int, alpha):
+        self.L, self.P, self.BT = num_layers, prefix_tokens, block_tokens
+        self.alpha = np.asarray(alpha, dtype=np.float64)
+        self.prefix = [None] * num_layers
+        self.shared = None
+        self.curr = [None] * num_layers
+
+    def history(self, layer: int, start: int):
+        if start <= 0:
+            return None
+        P = self.P
+        sk, sv = self.shared
+        pk, pv = self.prefix[layer]
+        keep = min(start, P)
+        deep_k = np.concatenate([pk[:keep], sk[keep:start]]) if start > keep else pk[:start]
+        deep_v = np.concatenate([pv[:keep], sv[keep:start]]) if start > keep else pv[:start]
+        prev_start = start - min(self.BT, start)
+        ck, cv = self.curr[layer]
+        a = self.alpha[layer][None, :, None]
+        bk = a * deep_k[prev_start:start] + (1 - a) * ck
+        bv = a * deep_v[prev_start:start] + (1 - a) * cv
+        keep_n = min(max(P - prev_start, 0), start - prev_start)
+        if keep_n:
+            bk[:keep_n], bv[:keep_n] = ck[:keep_n], cv[:keep_n]
+        return (np.concatenate([deep_k[:prev_start], bk]), np.concatenate([deep_v[:prev_start], bv]))
+
+    def commit(self, start: int, kvs):
+        top_k, top_v = kvs[-1]
+        end = start + top_k.shape[0]
+        if self.shared is None:
+            self.shared = (top_k.copy(), top_v.copy())
+        else:
+            self.shared = (np.concatenate([self.shared[0], top_k]), np.concatenate([self.shared[1], top_v]))
+        for layer, (k, v) in enumerate(kvs):
+            if start < self.P:
+                n = min(end, self.P) - start
+                pk = k[:n] if self.prefix[layer] is None else np.concatenate([self.prefix[layer][0], k[:n]])
+                pv = v[:n] if self.prefix[layer] is None else np.concatenate([self.prefix[layer][1], v[:n]])
+                self.prefix[layer] = (pk, pv)
+            self.curr[layer] = (k.copy(), v.copy())
+
+
+# --------------------------------------------------------------------------
 # CPU baseline: the reference's own per-layer computation (torch, CPU)
 # --------------------------------------------------------------------------
 

@@ -248,6 +248,97 @@ def main():
         print(f"config1 {tag}: first tokens {gen[0, 512:520].tolist()}")
     np.savez_compressed(os.path.join(args.out, "config1_124m.npz"), **out)
 
+    wan_golden(args.reference, args.out, torch)
+
+
+def _diffusers_stub() -> str:
+    """A temporary package exposing the three diffusers names videogen/model.py imports."""
+    import tempfile
+
+    root = tempfile.mkdtemp(prefix="diffusers_stub_")
+    pkg = os.path.join(root, "diffusers")
+    os.makedirs(os.path.join(pkg, "models"))
+    open(os.path.join(pkg, "__init__.py"), "w").close()
+    open(os.path.join(pkg, "models", "__init__.py"), "w").close()
+    with open(os.path.join(pkg, "configuration_utils.py"), "w") as f:
+        f.write("class ConfigMixin:\n    pass\n\n\ndef register_to_config(fn):\n    return fn\n")
+    with open(os.path.join(pkg, "models", "modeling_utils.py"), "w") as f:
+        f.write("import torch\n\n\nclass ModelMixin(torch.nn.Module):\n    pass\n")
+    return root
+
+
+def wan_golden(reference, out_dir, torch):
+    """Record the reference Wan block attention (videogen/src/lastkv/videogen/model.py:217-390)
+    over six 3-frame blocks of a tiny model: 2 heads x 128, 8 tokens per frame (2 x 4 grid),
+    one-frame local prefix; none of the segment boundaries is a multiple of 16."""
+    sys.path.insert(0, _diffusers_stub())
+    sys.path.insert(0, os.path.join(reference, "videogen", "src"))
+    from lastkv.videogen import model as wm
+    from lastkv.videogen.cache import allocate_caches
+
+    torch.manual_seed(123)
+    cfg = dict(model_type="t2v", patch_size=(1, 2, 2), dim=256, ffn_dim=64, num_heads=2, num_layers=3, text_dim=8,
+               text_len=5, freq_dim=16, in_dim=2, out_dim=2, qk_norm=True, cross_attn_norm=True,
+               akv_mode="reusekv", v_gap=95, num_frame_per_block=3, force_first_local_kv_tokens=8, eps=1e-6)
+    model = wm.AKV2541ReuseKVCausalWanModel(**cfg).eval()
+    with torch.no_grad():
+        model.prev_block_alphas.normal_()
+        for blk in model.blocks:
+            blk.self_attn.norm_q.weight.copy_(torch.linspace(0.6, 1.4, 256))
+            blk.self_attn.norm_k.weight.copy_(torch.linspace(1.3, 0.7, 256))
+    fh, fw, fpb, blocks = 2, 4, 3, 6
+    frame_tok = fh * fw
+    block_tok = frame_tok * fpb
+    caches = allocate_caches(model, 1, block_tok * blocks, block_tok, torch.float32, "cpu", shared=True)
+    model._ensure_current_history_caches(caches)
+    grid = torch.tensor([[fpb, fh, fw]])
+    rec, calls = {}, []
+    orig_attention = wm.attention
+
+    def capture(q, k, v, *a, **kw):
+        out = orig_attention(q, k, v, *a, **kw)
+        rec.update(roped_q=q.detach().clone(), full_k=k.detach().clone(), full_v=v.detach().clone(),
+                   out=out.detach().clone())
+        return out
+
+    wm.attention = capture
+    try:
+        hooks = []
+        for blk in model.blocks:
+            at = blk.self_attn
+            hooks.append(at.norm_q.register_forward_hook(lambda m, a, o: rec.__setitem__("qn", o.detach().clone())))
+            hooks.append(at.norm_k.register_forward_hook(lambda m, a, o: rec.__setitem__("kn", o.detach().clone())))
+            hooks.append(at.v.register_forward_hook(lambda m, a, o: rec.__setitem__("v", o.detach().clone())))
+        g = torch.Generator().manual_seed(9)
+        with torch.no_grad():
+            for n in range(blocks):
+                start = n * block_tok
+                kvs = []
+                for layer, blk in enumerate(model.blocks):
+                    model._set_prev_block_alpha(caches[layer], layer, torch.float32, "cpu")
+                    x = torch.randn(1, block_tok, 256, generator=g)
+                    _, kv = blk.self_attn(x, grid, model.freqs, kv_cache=caches[layer], current_start=start,
+                                          num_frame_per_block=fpb, return_current_kv=True)
+                    kvs.append(kv)
+                    calls.append(dict(layer=layer, start=start, **{k: v.numpy() for k, v in rec.items()}))
+                model._update_caches_akv(caches, kvs, None, grid, start_frame=start // frame_tok,
+                                         current_start=start)
+        for h in hooks:
+            h.remove()
+    finally:
+        wm.attention = orig_attention
+    data = {"calln": np.int64(len(calls)), "num_heads": np.int64(2), "head_dim": np.int64(128),
+            "frame_h": np.int64(fh), "frame_w": np.int64(fw), "frames_per_block": np.int64(fpb),
+            "prefix_tokens": np.int64(8), "num_layers": np.int64(3),
+            "prev_block_alphas": model.prev_block_alphas.detach().numpy().astype(np.float32)}
+    for i, c in enumerate(calls):
+        p = f"call{i}_"
+        data[p + "meta"] = np.array([c["layer"], c["start"], block_tok, c["full_k"].shape[1]], dtype=np.int64)
+        for k in ("qn", "kn", "v", "roped_q", "out"):
+            data[p + k] = c[k].astype(np.float32)
+    np.savez_compressed(os.path.join(out_dir, "wan_block_attn.npz"), **data)
+    print("wan:", len(calls), "calls; key lengths", sorted({int(c["full_k"].shape[1]) for c in calls}))
+
 
 if __name__ == "__main__":
     main()
