@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--case", default="config2", choices=["config2", "small"],
                     help="small: 8 sequences x 2 layers, for ncu captures")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "cp128k"],
+                    help="cp128k: config 4, 128K-context decode sharded over the ranks")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
@@ -287,6 +289,77 @@ def measure_prefill(device, reps: int = 5, batch: int | None = None):
             "peak_tflops": peak, "peak_source": src, "kernel": "prefill_tcgen05_kernel"}
 
 
+WAN = dict(batch=2, heads=12, head_dim=128, frame_h=30, frame_w=52, frames_per_block=3, max_frames=21,
+           prefix_tokens=1560)
+
+
+def measure_wan(device, reps: int = 5, batch: int | None = None):
+    """Wan-1.3B causal block attention (config 5): the last 3-frame block (4680 queries) against the
+    full 21-frame history (32760 keys), per layer: fused 3-D-RoPE append + non-causal tcgen05 prefill."""
+    import torch
+
+    from lastkv_b200 import ops
+    from lastkv_b200.wan import WanSharedKVCache, wan_block_attention
+
+    W = dict(WAN)
+    if batch:
+        W["batch"] = batch
+    B, H, D = W["batch"], W["heads"], W["head_dim"]
+    cache = WanSharedKVCache(num_layers=1, batch=B, num_heads=H, head_dim=D, frame_h=W["frame_h"],
+                             frame_w=W["frame_w"], frames_per_block=W["frames_per_block"],
+                             max_frames=W["max_frames"], prefix_tokens=W["prefix_tokens"], device=device)
+    BT = cache.block
+    gen = torch.Generator(device=device).manual_seed(5)
+    alpha = torch.rand((1, H), generator=gen, device=device)
+    blocks = W["max_frames"] // W["frames_per_block"]
+
+    def rnd():
+        x = torch.randn((B, BT, H * D), generator=gen, device=device, dtype=torch.float32)
+        return (x / x.pow(2).mean(-1, keepdim=True).sqrt()).to(torch.bfloat16)
+
+    q, k, v = rnd(), rnd(), rnd()
+    for n in range(blocks - 1):  # build the history block by block
+        cache.begin_block(n)
+        wan_block_attention(q, k, v, cache, 0)
+        cache.commit_block(alpha)
+    m = cache.begin_block(blocks - 1)
+    S = (blocks - 1) * BT
+    flops = 4 * H * D * BT * (S + BT) * B
+    wan_block_attention(q, k, v, cache, 0)
+    qa = torch.randn((B * BT, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    out = torch.empty_like(qa)
+
+    def attn_only():
+        ops.prefill_paged(qa, cache.pool_k, cache.pool_v, m["bt"][0], m["seq_k"], m["cu_q"], BT, causal=False,
+                          out=out, error_word=cache.error_word, max_pages=m["W"])
+
+    attn_only()
+    torch.cuda.synchronize()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record()
+    for _ in range(reps):
+        attn_only()
+    e[1].record()
+    for _ in range(reps):
+        wan_block_attention(q, k, v, cache, 0)
+    e[2].record()
+    torch.cuda.synchronize()
+    cache.check_errors()
+    attn_ms = e[0].elapsed_time(e[1]) / reps
+    layer_ms = e[1].elapsed_time(e[2]) / reps
+    try:
+        peak = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["bf16_tflops"])
+        src = "measured (burst)"
+    except (OSError, KeyError, ValueError):
+        peak, src = 1590.0, "fallback"
+    tf = flops / (attn_ms * 1e-3) / 1e12
+    return {"workload": f"Wan-1.3B block attention: batch {B}, 12 heads x 128, 4680-token block vs "
+                        f"{S + BT} keys ([1560 prefix | shared | blended prev block | block]), non-causal",
+            "flops_per_layer": flops, "attn_ms": attn_ms, "tflops": tf, "frac": tf / peak,
+            "layer_ms_incl_rope_append": layer_ms, "peak_tflops": peak, "peak_source": src,
+            "kernel": "prefill_tcgen05_kernel<128, 1> (non-causal)"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -414,6 +487,7 @@ def run_ours(args):
     if not args.no_prefill:
         # the small case (profiler captures) runs the same spans with 2 sequences
         line["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
+        line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = cpu_layer_step_sample(args.cpu_seconds, batch=8)
         med = statistics.median(times)
@@ -453,12 +527,97 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+CP = dict(batch=4, q_heads=32, kv_heads=8, head_dim=128, context=131072, window=2048, layers=32)
+
+
+def run_cp(args):
+    """Config 4: 128K-context decode, sequence-sharded over the ranks (context parallel).
+
+    Each rank holds a contiguous 1/G slice of every sequence's shared pages (the
+    last rank also the 2048-token ring window); per layer the partial decode
+    kernel runs on the slice, the (o, lse) partials are all-gathered over NCCL
+    and merged exactly.  Prints one JSON line (rank 0).
+    """
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from lastkv_b200 import _capi, ops
+    from lastkv_b200.context_parallel import ContextParallelDecode, plan_shard
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    _capi.load()
+    B, Hq, H, D, N, Wt, L = (CP[k] for k in ("batch", "q_heads", "kv_heads", "head_dim", "context", "window",
+                                             "layers"))
+    nsrc = (N - Wt) // 16
+    sp = plan_shard(nsrc, Wt, 16, world, rank)
+    pages_mine = (sp.p1 - sp.p0) + sp.ring_pages
+    gen = torch.Generator(device=device).manual_seed(300 + rank)
+    pool_k = torch.randn((B * pages_mine + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    pool_v = torch.randn((B * pages_mine + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    bt = torch.randperm(B * pages_mine, generator=gen, device=device).to(torch.int32).view(B, pages_mine)
+    seq_k = torch.full((B,), sp.seq_k, dtype=torch.int32, device=device)
+    q = torch.randn((L, B, Hq, D), generator=gen, device=device, dtype=torch.bfloat16)
+    out = torch.empty((L, B, Hq, D), dtype=torch.bfloat16, device=device)
+    scale = torch.ones(Hq, device=device)
+    ws = ops.Workspace.for_decode(B, Hq, D, pages_mine, device=device)
+    cp = ContextParallelDecode()
+
+    def step():
+        for l in range(L):
+            cp.layer(q[l], pool_k, pool_v, bt, seq_k, out_scale=scale, out=out[l], workspace=ws,
+                     max_pages=pages_mine)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    layer_ms = ms / (args.steps * L)
+    bytes_layer = 2 * B * H * N * D * 2
+    line = {"metric": "context-parallel decode tokens/s (attention only, 32 layers, 128K context)",
+            "value": B * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cp128k", "batch": B, "context_tokens": N, "ring_window": Wt, "q_heads": Hq,
+                       "kv_heads": H, "head_dim": D, "layers_per_step": L,
+                       "parallelism": f"cp{world} (shared pages sharded, NCCL all-gather + LSE merge)"},
+            "layer_ms": layer_ms, "attn_bytes_per_layer_total": bytes_layer,
+            "hbm_gbs_per_gpu": bytes_layer / world / (layer_ms * 1e-3) / 1e9,
+            "combine_bytes_per_rank_per_layer": B * Hq * (D + 1) * 4}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.case == "small":
         CFG.update(SMALL)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cp128k":
+        run_cp(args)
     else:
         run_ours(args)
 
