@@ -153,14 +153,18 @@ int lkv_prefill_paged(const void* q, int64_t q_stride_tok,
  * Exact log-sum-exp merge of `num_parts` attention partials over disjoint key
  * sets (flashinfer cascade.merge_state / vLLM merge_attn_states, used at
  * flashinfer_executor.py:185-231 and fastpath.py:719):
- *   o_parts   fp32 [num_parts, rows, head_dim]   (normalised partial outputs)
- *   lse_parts fp32 [num_parts, rows]             (natural log, -inf = empty)
+ *   o_parts   fp32, part p at o_parts + p * o_part_stride: [rows, head_dim]
+ *             (normalised partial outputs)
+ *   lse_parts fp32, part p at lse_parts + p * lse_part_stride: [rows]
+ *             (natural log, -inf = empty)
  *   out       bf16 [rows, head_dim] = out_scale[row % num_q_heads] * merged
  *   lse_out   fp32 [rows] (optional)
- * rows = tokens * num_q_heads.  out_scale is optional. */
+ * rows = tokens * num_q_heads; strides in elements, 0 = packed (rows * head_dim,
+ * rows), so one all-gathered buffer of [o | lse] parts can be merged in place.
+ * out_scale is optional. */
 int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows,
-                       int head_dim, int num_q_heads, const float* out_scale,
-                       void* out, float* lse_out, void* stream);
+                       int head_dim, int num_q_heads, int64_t o_part_stride, int64_t lse_part_stride,
+                       const float* out_scale, void* out, float* lse_out, void* stream);
 
 /* ------------------------------------------------------------------ append
  * Fused cache-append epilogue of one layer; replaces _fused_qkv_kernel

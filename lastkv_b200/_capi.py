@@ -39,7 +39,7 @@ _SIGNATURES = {
     "lkv_decode_plan": (I32, [I32, I32, I32, I32, I32, SZ, I32, P, P]),
     "lkv_decode_paged_noalloc": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, P, P,
                                        I32, I32, I32, I32, I32, F32, P, P]),
-    "lkv_merge_partials": (I32, [P, P, I32, I64, I32, I32, P, P, P, P]),
+    "lkv_merge_partials": (I32, [P, P, I32, I64, I32, I32, I64, I64, P, P, P, P]),
     "lkv_rope_norm_append": (I32, [P, I64, P, I64, P, I64, P, P, I64, I64, P, P, F32, P, P, I64,
                                    P, P, P, I64, P, P, P, I64, I32, I32, I32, I32, I32, P, P]),
     "lkv_gather_blend": (I32, [P, P, I64, P, P, P, P, P, I32, I32, I32, P, P]),

@@ -53,7 +53,14 @@ def plan_shard(nsrc_pages: int, window_tokens: int, page: int, world: int, rank:
 
 
 class ContextParallelDecode:
-    """Sequence-sharded decode for one process group (NCCL on GPUs, gloo for host tests)."""
+    """Sequence-sharded decode for one process group (NCCL on GPUs, gloo for host tests).
+
+    With the default kernels each rank writes its partial (o, lse) into one
+    packed send buffer [B*Hq*D | B*Hq] so a single all-gather per layer moves
+    it, and the merge kernel reads the gathered parts in place.  ``partial_fn``
+    and ``merge_fn`` can be injected (host tests) and then use separate
+    o / lse tensors.
+    """
 
     def __init__(self, group=None, *, partial_fn=None, merge_fn=None):
         import torch.distributed as dist
@@ -62,6 +69,7 @@ class ContextParallelDecode:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.injected = partial_fn is not None or merge_fn is not None
         self.partial_fn = partial_fn or self._partial_kernel
         self.merge_fn = merge_fn or self._merge_kernel
         self._bufs = {}
@@ -75,24 +83,40 @@ class ContextParallelDecode:
     def _merge_kernel(o_all, lse_all, out_scale, out):
         return ops.merge_partials(o_all, lse_all, out_scale=out_scale, out=out)
 
-    def _gather_buffers(self, shape_o, shape_l, device):
-        """Concatenated [world * B, ...] receive buffers (the form every backend accepts)."""
-        key = (tuple(shape_o), str(device))
+    def _buffers(self, key, make):
         if key not in self._bufs:
-            self._bufs[key] = (torch.empty((self.world * shape_o[0], *shape_o[1:]), dtype=torch.float32,
-                                           device=device),
-                               torch.empty((self.world * shape_l[0], *shape_l[1:]), dtype=torch.float32,
-                                           device=device))
+            self._bufs[key] = make()
         return self._bufs[key]
 
     def layer(self, q, pool_k, pool_v, block_table, seq_k, *, out_scale=None, out=None, workspace=None,
               max_pages=None):
         """One layer: local partial over this rank's keys, all-gather, exact merge."""
+        if self.injected:
+            return self._layer_generic(q, pool_k, pool_v, block_table, seq_k, out_scale, out, workspace, max_pages)
+        B, Hq, D = q.shape
+        n = -(-(B * Hq * (D + 1)) // 4) * 4  # o | lse | pad to a multiple of 4 floats (float4 reads)
+        send, recv = self._buffers(("packed", n, str(q.device)), lambda: (
+            torch.empty(n, dtype=torch.float32, device=q.device),
+            torch.empty(self.world * n, dtype=torch.float32, device=q.device)))
+        o_view = send[: B * Hq * D].view(B, Hq, D)
+        l_view = send[B * Hq * D: B * Hq * (D + 1)].view(B, Hq)
+        ops.decode_paged(q, pool_k, pool_v, block_table, seq_k, workspace=workspace, max_pages=max_pages,
+                         partial=True, partial_out=(o_view, l_view))
+        if self.world == 1:
+            parts = send.view(1, n)
+        else:
+            self.dist.all_gather_into_tensor(recv, send, group=self.group)
+            parts = recv.view(self.world, n)
+        return ops.merge_partials_packed(parts, B, Hq, D, out_scale=out_scale, out=out)
+
+    def _layer_generic(self, q, pool_k, pool_v, block_table, seq_k, out_scale, out, workspace, max_pages):
         o, lse = self.partial_fn(q, pool_k, pool_v, block_table, seq_k, workspace, max_pages)
         if self.world == 1:
             o_all, lse_all = o.unsqueeze(0), lse.unsqueeze(0)
         else:
-            o_flat, lse_flat = self._gather_buffers(o.shape, lse.shape, o.device)
+            o_flat, lse_flat = self._buffers(("split", tuple(o.shape), str(o.device)), lambda: (
+                torch.empty((self.world * o.shape[0], *o.shape[1:]), dtype=torch.float32, device=o.device),
+                torch.empty((self.world * lse.shape[0], *lse.shape[1:]), dtype=torch.float32, device=o.device)))
             self.dist.all_gather_into_tensor(o_flat, o.contiguous(), group=self.group)
             self.dist.all_gather_into_tensor(lse_flat, lse.contiguous(), group=self.group)
             o_all = o_flat.view(self.world, *o.shape)

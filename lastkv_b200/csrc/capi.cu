@@ -158,9 +158,10 @@ int lkv_decode_plan(int batch, int num_q_heads, int num_kv_heads, int head_dim, 
 }
 
 int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim,
-                       int num_q_heads, const float* out_scale, void* out, float* lse_out, void* stream) {
-  return lkv::merge_partials(o_parts, lse_parts, num_parts, rows, head_dim, num_q_heads, out_scale, out, lse_out,
-                             static_cast<cudaStream_t>(stream));
+                       int num_q_heads, int64_t o_part_stride, int64_t lse_part_stride, const float* out_scale,
+                       void* out, float* lse_out, void* stream) {
+  return lkv::merge_partials(o_parts, lse_parts, num_parts, rows, head_dim, num_q_heads, o_part_stride,
+                             lse_part_stride, out_scale, out, lse_out, static_cast<cudaStream_t>(stream));
 }
 
 int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_row, const void* v, int64_t v_row,

@@ -299,13 +299,15 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 // ------------------------------------------------------------------ merge
 // One warp per output row (token, head): merge `parts` normalised partials.
 // part_o: [rows, S, D] with row stride S*D when split_major == 0 (decode
-// splits), or [S, rows, D] when split_major == 1 (context-parallel ranks).
+// splits), or part s at part_o + s * o_part_stride ([rows, D] each) when
+// split_major == 1 (context-parallel ranks; lse likewise with lse_part_stride).
 struct MergeParams {
   const float* part_o;
   const float* part_lse;
   int S;
   int64_t rows;
   int split_major;
+  int64_t o_part_stride, lse_part_stride;  // elements, split_major == 1
   int lse_log2;  // 1: part_lse in log2 units, 0: natural log
   int Hq;
   const float* out_scale;
@@ -324,12 +326,11 @@ __global__ void __launch_bounds__(128) merge_partials_kernel(const MergeParams p
   if (row >= p.rows) return;
   const float to2 = p.lse_log2 ? 1.f : 1.4426950408889634f;
   auto lse_at = [&](int s) -> float {
-    const int64_t i = p.split_major ? (int64_t)s * p.rows + row : row * p.S + s;
+    const int64_t i = p.split_major ? (int64_t)s * p.lse_part_stride + row : row * p.S + s;
     return p.part_lse[i] * to2;
   };
   auto o_at = [&](int s) -> const float* {
-    const int64_t i = p.split_major ? (int64_t)s * p.rows + row : row * p.S + s;
-    return p.part_o + i * D;
+    return p.split_major ? p.part_o + (int64_t)s * p.o_part_stride + row * D : p.part_o + (row * p.S + s) * D;
   };
   float M = -INFINITY;
   for (int s = lane; s < p.S; s += 32) M = fmaxf(M, lse_at(s));
@@ -598,11 +599,16 @@ int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspa
 }
 
 int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim, int hq,
-                   const float* out_scale, void* out, float* lse_out, cudaStream_t stream) {
+                   int64_t o_part_stride, int64_t lse_part_stride, const float* out_scale, void* out,
+                   float* lse_out, cudaStream_t stream) {
   if (head_dim != 64 && head_dim != 128) return LKV_ERR_UNSUPPORTED;
   if (num_parts < 1 || rows < 0 || hq < 1 || rows % hq) return LKV_ERR_INVALID_ARGUMENT;
   if (rows == 0) return LKV_OK;
   if (!o_parts || !lse_parts || !out) return LKV_ERR_INVALID_ARGUMENT;
+  if (o_part_stride == 0) o_part_stride = rows * head_dim;
+  if (lse_part_stride == 0) lse_part_stride = rows;
+  if (o_part_stride < rows * head_dim || lse_part_stride < rows || (o_part_stride & 3))
+    return LKV_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(o_parts) & 15) || (reinterpret_cast<uintptr_t>(out) & 3))
     return LKV_ERR_INVALID_ARGUMENT;
   MergeParams mp{};
@@ -611,6 +617,8 @@ int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, 
   mp.S = num_parts;
   mp.rows = rows;
   mp.split_major = 1;
+  mp.o_part_stride = o_part_stride;
+  mp.lse_part_stride = lse_part_stride;
   mp.lse_log2 = 0;
   mp.Hq = hq;
   mp.out_scale = out_scale;

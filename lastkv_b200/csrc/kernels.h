@@ -64,7 +64,8 @@ int decode_paged(const DecodeArgs& a);
 int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspace_bytes, int partial, int* splits,
                 int* launches);
 int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim, int hq,
-                   const float* out_scale, void* out, float* lse_out, cudaStream_t stream);
+                   int64_t o_part_stride, int64_t lse_part_stride, const float* out_scale, void* out,
+                   float* lse_out, cudaStream_t stream);
 
 struct AppendArgs {
   const void* q;

@@ -67,7 +67,7 @@ class Workspace:
 
 def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, out=None, lse=None,
                  out_scale=None, workspace: Workspace | None = None, max_pages: int | None = None,
-                 partial: bool = False):
+                 partial: bool = False, partial_out=None):
     """One query token per sequence against its paged history.
 
     q [B, Hq, D] bf16 (row-strided views allowed); block_table int32 [B, W];
@@ -92,8 +92,13 @@ def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, o
         workspace = Workspace.for_decode(B, Hq, D, W, device=q.device)
     po = pl = None
     if partial:
-        po = torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
-        pl = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+        if partial_out is not None:  # caller views (e.g. the two halves of one send buffer)
+            po, pl = partial_out
+            _require(po.dtype == torch.float32 and po.is_contiguous() and po.numel() == B * Hq * D, "partial o")
+            _require(pl.dtype == torch.float32 and pl.is_contiguous() and pl.numel() == B * Hq, "partial lse")
+        else:
+            po = torch.empty((B, Hq, D), dtype=torch.float32, device=q.device)
+            pl = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
     elif out is None:
         out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
     if out is not None:
@@ -163,8 +168,24 @@ def merge_partials(o_parts, lse_parts, *, out_scale=None, out=None, lse_out=None
     if out is None:
         out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=o_parts.device)
     _require(out.is_contiguous() and out.dtype == torch.bfloat16, "out must be contiguous bf16")
-    st = _capi.lib().lkv_merge_partials(o_parts.data_ptr(), lse_parts.data_ptr(), P_, T * Hq, D, Hq,
+    st = _capi.lib().lkv_merge_partials(o_parts.data_ptr(), lse_parts.data_ptr(), P_, T * Hq, D, Hq, 0, 0,
                                         _ptr(out_scale), out.data_ptr(), _ptr(lse_out), _stream())
+    _capi.check(st, "lkv_merge_partials")
+    return out
+
+
+def merge_partials_packed(parts, T: int, Hq: int, D: int, *, out_scale=None, out=None, lse_out=None):
+    """LSE-merge parts packed as [P, T*Hq*D (o) | T*Hq (lse) | pad] fp32 rows (one all-gather buffer)."""
+    P_ = parts.shape[0]
+    rows = T * Hq
+    stride = parts.shape[1]  # o [rows*D], lse [rows], padding to a multiple of 4 floats
+    _require(parts.dtype == torch.float32 and parts.is_contiguous() and stride >= rows * (D + 1)
+             and stride % 4 == 0, "parts must be contiguous fp32 [P, >= rows * (D + 1)], stride % 4 == 0")
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=parts.device)
+    _require(out.is_contiguous() and out.dtype == torch.bfloat16, "out must be contiguous bf16")
+    st = _capi.lib().lkv_merge_partials(parts.data_ptr(), parts.data_ptr() + rows * D * 4, P_, rows, D, Hq, stride,
+                                        stride, _ptr(out_scale), out.data_ptr(), _ptr(lse_out), _stream())
     _capi.check(st, "lkv_merge_partials")
     return out
 
