@@ -57,16 +57,19 @@ def traffic_per_launch() -> int:
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100; e2e8b: 256 - warmup)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--case", default="config2", choices=["config2", "small"],
                     help="small: 8 sequences x 2 layers, for ncu captures")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "cp128k"],
-                    help="cp128k: config 4, 128K-context decode sharded over the ranks")
+    ap.add_argument("--workload", default="decode", choices=["decode", "cp128k", "e2e8b"],
+                    help="cp128k: config 4, 128K-context decode sharded over the ranks; "
+                         "e2e8b: config 3, the 8B-architecture model end to end")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
+    ap.add_argument("--e2e-layers", type=int, default=None,
+                    help="e2e8b with fewer layers (same per-layer shapes), for profiler captures; never a bench line")
     return ap.parse_args()
 
 
@@ -610,14 +613,184 @@ def run_cp(args):
         dist.destroy_process_group()
 
 
+E2E8B = dict(layers=32, hidden=4096, q_heads=32, kv_heads=8, head_dim=128, ffn=14336, vocab=128256, chunk=1024,
+             batch=8, prompt=8192, prefill_call=2048, decode_tokens=256)
+# A 4-layer, 2-sequence, 2048-token version for quick checks and profiler captures; never a bench line.
+E2E8B_SMALL = dict(layers=4, batch=2, prompt=2048)
+
+
+def e2e8b_config():
+    from lastkv_b200.hf import LastKVConfig
+
+    c = E2E8B
+    return LastKVConfig(hidden_size=c["hidden"], intermediate_size=c["ffn"], num_attention_heads=c["q_heads"],
+                        num_key_value_heads=c["kv_heads"], num_hidden_layers=c["layers"], head_dim=c["head_dim"],
+                        vocab_size=c["vocab"], chunk_size=c["chunk"], rms_norm_eps=1e-5, rope_theta=500000.0,
+                        rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                      "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+                        max_position_embeddings=131072)
+
+
+def run_e2e8b(args):
+    """Config 3: the 8B-architecture model end to end, batch 8 per GPU (weak scaling).
+
+    Random-init bf16 weights (built on the meta device, materialised on the
+    GPU, then seeded N(0, 0.02); blend logits ~ N(0, 1), value scales ~ U(0.1, 2)).
+    Prefill: 8192 random-token prompts in 2048-token calls (each split at the
+    1024-token chunk boundaries, as the reference's chunk loop does), timed
+    once after one warm-up call on a scratch cache.  Decode: every step is one
+    replay of the CUDA graph of the whole model step (fused append + split-KV
+    decode per layer, cuBLAS dense layers, argmax) with the host plan copied in
+    from pinned memory and the new ids copied out to pinned memory; warm-up +
+    timed steps = the config's 256 decode tokens by default.  Ranks run
+    independent replicas (no collective on the data path).
+    """
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from lastkv_b200 import _capi, ops
+    from lastkv_b200.hf import LastKVForCausalLM
+    from lastkv_b200.runner import GraphDecodeRunner, init_random_
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    _capi.load()
+    _capi.check(_capi.lib().lkv_check_device(local), "lkv_check_device")
+    c = E2E8B
+    B, P, call, L = c["batch"], c["prompt"], c["prefill_call"], c["layers"]
+    Hkv, D = c["kv_heads"], c["head_dim"]
+    cfg = e2e8b_config()
+    with torch.device("meta"):
+        model = LastKVForCausalLM(cfg)
+    model = model.to(torch.bfloat16).to_empty(device=device).eval()
+    init_random_(model, seed=1234)
+    model.model._alpha = None
+    model.fuse_projections_()
+    weight_bytes = sum(p.numel() * p.element_size() for n, p in model.named_parameters() if "embed_tokens" not in n)
+    gen = torch.Generator(device=device).manual_seed(77 + rank)
+    prompt = torch.randint(0, c["vocab"], (B, P), generator=gen, device=device)
+    total_tokens = P + args.warmup + args.steps
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.no_grad():
+        scratch = model.new_cache(B, call)
+        model(prompt[:, :call], scratch, logits_to_keep=1)  # cuBLAS / kernel warm-up, same shapes
+        del scratch
+        cache = model.new_cache(B, total_tokens + 1)
+        runner = GraphDecodeRunner(model, cache)
+        torch.cuda.synchronize()
+        barrier()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        runner.prefill(prompt, call)
+        p1.record(stream)
+        torch.cuda.synchronize()
+        prefill_ms = p0.elapsed_time(p1)
+
+        runner.capture()
+        for _ in range(args.warmup):
+            runner.step()
+        host_ids = torch.empty((max(args.steps, 1), B), dtype=torch.int64, pin_memory=True)
+        torch.cuda.synchronize()
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        clocks = ClockSampler(uuid)
+        clocks.start()
+        barrier()
+        torch.cuda.synchronize()
+        first_pos = cache.seen_tokens
+        w0 = time.perf_counter()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for i in range(args.steps):
+            ids = runner.step()
+            host_ids[i].copy_(ids.view(-1), non_blocking=True)
+        d1.record(stream)
+        torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - w0) * 1e3
+        barrier()
+        clk = clocks.stop()
+    cache.check_errors()
+    decode_ms = d0.elapsed_time(d1)
+    if not bool(((host_ids[: args.steps] >= 0) & (host_ids[: args.steps] < c["vocab"])).all()):
+        raise RuntimeError("decoded ids out of range")
+    vals = torch.tensor([decode_ms, wall_ms, prefill_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    decode_ms, wall_ms, prefill_ms = vals.tolist()
+
+    # HBM bytes one step must move: every weight but the embedding table once, plus
+    # every layer's keys and values (token p attends to p + 1 keys per sequence)
+    kv_bytes = sum(L * B * (first_pos + i + 1) * Hkv * D * 2 * 2 for i in range(args.steps))
+    step_bytes = weight_bytes + kv_bytes / max(args.steps, 1)
+    ms_step = decode_ms / max(args.steps, 1)
+    try:
+        peak, peak_src = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        peak, peak_src = 6650.0, "fallback"
+    achieved = step_bytes / (ms_step * 1e-3) / 1e9
+    splits, per_call = ops.decode_plan(B, c["q_heads"], Hkv, D, cache.pages_per_seq + cache.ring_pages,
+                                       cache.workspace)
+    launches_per_step = 1 + L * (1 + per_call)  # block tables + per layer (append + decode [+ merge])
+    tokens = B * args.steps * world
+    h2d = sum(t.numel() * t.element_size() for k, t in runner._h[0].items()
+                                            if k != "done")
+    line = {
+        "metric": "end-to-end decode tokens/s (8B architecture, batch 8 per GPU, CUDA-graph steps)",
+        "value": tokens / (decode_ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompt ids)",
+        "config": {"workload": "e2e8b", "layers": L, "d_model": c["hidden"], "q_heads": c["q_heads"],
+                   "kv_heads": Hkv, "head_dim": D, "ffn": c["ffn"], "vocab": c["vocab"], "chunk": c["chunk"],
+                   "batch_per_gpu": B, "global_batch": B * world, "prompt_tokens": P,
+                   "prefill_call_tokens": call, "decode_positions": [first_pos, first_pos + args.steps],
+                   "l2": "16 GB of weights per step (larger than L2); no flush",
+                   "parallelism": f"dp{world} (independent replicas, no collective)"},
+        "e2e": {"value": tokens / (wall_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": B * 8,
+                "timing": "host wall clock around the step loop (plan H2D + graph replay + ids D2H), max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "kernel": "whole decode step (weights + shared-KV reads)",
+                     "algorithmic_bytes_per_step": int(step_bytes), "weight_bytes": int(weight_bytes),
+                     "kv_bytes_per_step": int(kv_bytes / max(args.steps, 1)), "traffic": None},
+        "prefill": {"tokens_per_s": B * P * world / (prefill_ms * 1e-3), "ms": prefill_ms,
+                    "tokens_per_gpu": B * P},
+        "clocks": clk,
+        "gpu_launches": int(args.steps * launches_per_step),
+        "kv_splits": splits,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del runner
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.steps is None:
+        args.steps = max(E2E8B["decode_tokens"] - args.warmup, 1) if args.workload == "e2e8b" else 100
     if args.case == "small":
         CFG.update(SMALL)
+        E2E8B.update(E2E8B_SMALL)
+    if args.e2e_layers:
+        E2E8B["layers"] = args.e2e_layers
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "cp128k":
         run_cp(args)
+    elif args.workload == "e2e8b":
+        run_e2e8b(args)
     else:
         run_ours(args)
 

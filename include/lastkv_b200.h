@@ -237,6 +237,26 @@ int lkv_build_layer_block_tables(const int32_t* block_table, int64_t block_table
                                  const int32_t* nsrc, const int32_t* ring_base,
                                  int num_layers, int batch, int width, int32_t* bt_all, void* stream);
 
+/* ------------------------------------------------------------------ dense epilogues
+ * The decoder layer's residual-add + RMSNorm and SiLU-and-mul in one launch
+ * each, with the eager modules' bf16 rounding points (modeling.py decoder
+ * layer; the vLLM model's fused_add_rms_norm / silu_and_mul pair,
+ * vllm/src/lastkv/vllm/vllm_model.py:756-789).  All tensors bf16 rows, row
+ * strides in elements (multiples of 8), 16-byte aligned.
+ *
+ * lkv_rmsnorm: if residual != NULL, h = bf16(x + residual) is written to
+ * residual_out (may alias residual or x), else h = x; then
+ *   out = bf16(weight * bf16(h * rsqrt(mean(h^2) + eps)))   (fp32 accumulation)
+ * hidden <= 8192, a multiple of 8.
+ *
+ * lkv_silu_mul: gate_up rows hold [gate (ffn) | up (ffn)];
+ *   out = bf16(bf16(silu(gate)) * up). */
+int lkv_rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual_row,
+                void* residual_out, int64_t residual_out_row, const void* weight,
+                void* out, int64_t out_row, int rows, int hidden, float eps, void* stream);
+int lkv_silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row,
+                 int64_t rows, int ffn, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

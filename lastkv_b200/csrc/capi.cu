@@ -277,4 +277,16 @@ int lkv_build_layer_block_tables(const int32_t* block_table, int64_t block_table
                                        bt_all, static_cast<cudaStream_t>(stream));
 }
 
+int lkv_rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual_row, void* residual_out,
+                int64_t residual_out_row, const void* weight, void* out, int64_t out_row, int rows, int hidden,
+                float eps, void* stream) {
+  return lkv::rmsnorm(x, x_row, residual, residual_row, residual_out, residual_out_row, weight, out, out_row, rows,
+                      hidden, eps, static_cast<cudaStream_t>(stream));
+}
+
+int lkv_silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
+                 void* stream) {
+  return lkv::silu_mul(gate_up, gate_up_row, out, out_row, rows, ffn, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -120,4 +120,10 @@ int blend_chunk(const BlendArgs& a);
 int build_layer_block_tables(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc, const int32_t* ring_base,
                              int num_layers, int batch, int width, int32_t* bt_all, cudaStream_t stream);
 
+int rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual_row, void* residual_out,
+            int64_t residual_out_row, const void* weight, void* out, int64_t out_row, int rows, int hidden, float eps,
+            cudaStream_t stream);
+int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
+             cudaStream_t stream);
+
 }  // namespace lkv

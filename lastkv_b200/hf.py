@@ -89,11 +89,23 @@ class RotaryEmbedding(nn.Module):
 
     def __init__(self, config: LastKVConfig, device=None):
         super().__init__()
-        d = config.head_dim
-        inv = 1.0 / (config.rope_theta ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
+        self.config = config
+        self.register_buffer("inv_freq", self._frequencies(device or "cpu"), persistent=False)
+
+    def _frequencies(self, device) -> torch.Tensor:
+        """fp32 frequencies, computed on the host (as the reference's module is built) and moved."""
+        config, d = self.config, self.config.head_dim
+        inv = 1.0 / (config.rope_theta ** (torch.arange(0, d, 2, dtype=torch.int64, device="cpu").float() / d))
         if config.rope_scaling and config.rope_scaling.get("rope_type", config.rope_scaling.get("type")) == "llama3":
             inv = _llama3_inv_freq(inv, config.rope_scaling)
-        self.register_buffer("inv_freq", inv.to(device) if device else inv, persistent=False)
+        return inv.to(device)
+
+    def _apply(self, fn, recurse=True):
+        # dtype casts of the model and meta-device materialisation leave the
+        # frequencies fp32 and exact: recompute them on the buffer's new device
+        super()._apply(fn, recurse)
+        self.inv_freq = self._frequencies(self.inv_freq.device)
+        return self
 
     @torch.no_grad()
     def forward(self, x, position_ids):
@@ -114,6 +126,53 @@ class RMSNorm(nn.Module):
         h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.variance_epsilon)
         return self.weight * h.to(dt)
 
+    def fused(self, x, residual=None):
+        """``(h, norm(h))`` with ``h = x + residual`` (or ``x``): one kernel for bf16 CUDA rows."""
+        H = x.shape[-1]
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16 and H % 8 == 0 \
+                and H <= 8192:
+            w = self.weight.detach()
+            if residual is None:
+                return x, ops.rmsnorm(x, w, self.variance_epsilon)
+            return ops.rmsnorm(x, w, self.variance_epsilon, residual)
+        h = x if residual is None else x + residual
+        return h, self(h)
+
+
+def _fuse_linears(linears) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Concatenate the weights (and biases) of ``linears`` along the output dim and
+    re-point each module's parameters at its slice, so one GEMM computes all of
+    them and state-dict loads still write through the original names."""
+    w = torch.cat([lin.weight.detach() for lin in linears], 0)
+    has_bias = linears[0].bias is not None
+    b = torch.cat([lin.bias.detach() for lin in linears], 0) if has_bias else None
+    start = 0
+    for lin in linears:
+        n = lin.out_features
+        rg = lin.weight.requires_grad
+        lin.weight = nn.Parameter(w[start:start + n], requires_grad=rg)
+        if has_bias:
+            lin.bias = nn.Parameter(b[start:start + n], requires_grad=lin.bias.requires_grad)
+        start += n
+    return w, b
+
+
+def _fused_ok(fused, linears) -> bool:
+    """The fused buffers still back every module's parameters (a later .to() or
+    parameter replacement breaks the aliasing; then the modules run separately)."""
+    if fused is None:
+        return False
+    w, b = fused
+    start = 0
+    for lin in linears:
+        n = lin.out_features
+        if lin.weight.data_ptr() != w[start:start + n].data_ptr() or lin.weight.dtype != w.dtype:
+            return False
+        if b is not None and (lin.bias is None or lin.bias.data_ptr() != b[start:start + n].data_ptr()):
+            return False
+        start += n
+    return True
+
 
 class MLP(nn.Module):
     def __init__(self, config):
@@ -121,8 +180,16 @@ class MLP(nn.Module):
         self.gate_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
         self.up_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
         self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
+        self._gate_up = None
+
+    def fuse_(self):
+        """One [gate | up] GEMM + the SiLU-and-mul kernel instead of two GEMMs and two elementwise ops."""
+        self._gate_up = _fuse_linears([self.gate_proj, self.up_proj])
+        return self
 
     def forward(self, x):
+        if x.is_cuda and x.dtype == torch.bfloat16 and _fused_ok(self._gate_up, [self.gate_proj, self.up_proj]):
+            return self.down_proj(ops.silu_mul(F.linear(x, self._gate_up[0])))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -222,10 +289,15 @@ class PagedLastKVCache:
     def plan(self, n_new: int):
         h = self.plan_host(n_new)
         B, dev = self.batch, self.device
-        bt_d = torch.from_numpy(h["bt"]).to(dev)
+        # block tables are padded to the maximum width, so the decode kernel's
+        # split plan is the same at every position (and in captured graphs)
+        w_max = self.pages_per_seq + self.ring_pages
+        bt = np.zeros((B, w_max), np.int32)
+        bt[:, : h["W"]] = h["bt"]
+        bt_d = torch.from_numpy(bt).to(dev)
         nsrc_d = torch.full((B,), h["nsrc"], dtype=torch.int32, device=dev)
         meta = {
-            "n": n_new, "W": h["W"],
+            "n": n_new, "W": w_max,
             "bt_all": ops.build_layer_block_tables(bt_d, nsrc_d, self.ring_base_dev),
             "seq_k": torch.full((B,), h["seq_k"], dtype=torch.int32, device=dev),
             "cu_q": torch.arange(0, (B + 1) * n_new, n_new, dtype=torch.int32, device=dev),
@@ -294,6 +366,30 @@ class LastKVAttention(nn.Module):
         if config.use_qk_norm:
             self.q_norm = RMSNorm(d, config.rms_norm_eps)
             self.k_norm = RMSNorm(d, config.rms_norm_eps)
+        self._qkv = None
+        self._consts = (None, None)
+
+    def fuse_qkv_(self):
+        """One [q | k | v] GEMM per call; the three projections become views of its weight."""
+        self._qkv = _fuse_linears([self.q_proj, self.k_proj, self.v_proj])
+        return self
+
+    def _layer_constants(self):
+        """(s, 1/s, s per query head, q-norm weight, k-norm weight) for the kernels, rebuilt
+        only when a parameter they derive from changes (in-place loads bump the version)."""
+        params = [p for p in (getattr(self, "deep_v_scale", None),
+                              getattr(getattr(self, "q_norm", None), "weight", None),
+                              getattr(getattr(self, "k_norm", None), "weight", None)) if p is not None]
+        key = tuple((p.data_ptr(), p._version, p.dtype) for p in params) + (str(self.q_proj.weight.device),)
+        if self._consts[0] != key:
+            s = self.value_scale()
+            qn = getattr(self, "q_norm", None)
+            kn = getattr(self, "k_norm", None)
+            self._consts = (key, (s, (1.0 / s).contiguous(),
+                                  s.repeat_interleave(self.num_heads // self.num_key_value_heads).contiguous(),
+                                  qn.weight.detach().to(torch.bfloat16).contiguous() if qn is not None else None,
+                                  kn.weight.detach().to(torch.bfloat16).contiguous() if kn is not None else None))
+        return self._consts[1]
 
     def value_scale(self) -> torch.Tensor:
         """s_l per KV head as the pool sees it: bf16-exact values (batching.py:1070-1080)."""
@@ -309,31 +405,36 @@ class LastKVAttention(nn.Module):
         B, L, _ = hidden_states.shape
         D, Hq, Hkv = self.head_dim, self.num_heads, self.num_key_value_heads
         meta = cache._meta if cache._meta is not None and cache._meta["n"] == L else cache.plan(L)
-        q = self.q_proj(hidden_states).reshape(B * L, Hq * D)
-        k = self.k_proj(hidden_states).reshape(B * L, Hkv * D)
-        v = self.v_proj(hidden_states).reshape(B * L, Hkv * D)
+        if _fused_ok(self._qkv, [self.q_proj, self.k_proj, self.v_proj]):
+            qkv = F.linear(hidden_states, *self._qkv).reshape(B * L, (Hq + 2 * Hkv) * D)
+            q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+        else:
+            q = self.q_proj(hidden_states).reshape(B * L, Hq * D)
+            k = self.k_proj(hidden_states).reshape(B * L, Hkv * D)
+            v = self.v_proj(hidden_states).reshape(B * L, Hkv * D)
         if q.dtype != torch.bfloat16:
             q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
         cs = None
         if not self.config.use_nope:
             cos, sin = position_embeddings
-            cs = torch.cat((cos[0, :, : D // 2], sin[0, :, : D // 2]), dim=-1).to(torch.bfloat16).contiguous()
-        s = self.value_scale()
-        inv = (1.0 / s).contiguous()
+            # the (cos | sin) table is the same for every layer of a span: build it once
+            if meta.get("cs_of") is not cos:
+                meta["cs"] = torch.cat((cos[0, :, : D // 2], sin[0, :, : D // 2]), dim=-1).to(
+                    torch.bfloat16).contiguous()
+                meta["cs_of"] = cos
+            cs = meta["cs"]
+        s, inv, out_scale, q_w, k_w = self._layer_constants()
         top = self.layer_idx == cache.num_layers - 1
         flat_k = cache.pool_k.view(-1, Hkv, D)
         flat_v = cache.pool_v.view(-1, Hkv, D)
-        ring_slot = meta["ring_tok"] + int(cache.ring_base[self.layer_idx]) * PAGE_SIZE
-        qn = getattr(self, "q_norm", None)
-        kn = getattr(self, "k_norm", None)
+        if "ring_slot_all" not in meta:  # every layer's ring slots of the span, one launch
+            meta["ring_slot_all"] = meta["ring_tok"][None, :] + cache.ring_base_dev.to(torch.int64)[:, None] * PAGE_SIZE
+        ring_slot = meta["ring_slot_all"][self.layer_idx]
         q_out = ops.rope_norm_append(
-            q, k, v, meta["local_pos"], cs,
-            qn.weight.detach().to(torch.bfloat16) if qn is not None else None,
-            kn.weight.detach().to(torch.bfloat16) if kn is not None else None,
+            q, k, v, meta["local_pos"], cs, q_w, k_w,
             self.config.rms_norm_eps, inv, ring_slot, flat_k, flat_v,
             meta["src_slot"] if top else None, flat_k if top else None, flat_v if top else None,
             error_word=cache.error_word)
-        out_scale = s.repeat_interleave(Hq // Hkv).contiguous()
         bt = meta["bt_all"][self.layer_idx]
         if L == 1:
             out = ops.decode_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], out_scale=out_scale,
@@ -354,8 +455,24 @@ class LastKVDecoderLayer(nn.Module):
         self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, hidden_states, position_embeddings, cache):
-        hidden_states = hidden_states + self.self_attn(self.input_layernorm(hidden_states), position_embeddings, cache)
-        return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+        h, delta = self.forward_residual(hidden_states, None, position_embeddings, cache)
+        return h + delta
+
+    def forward_residual(self, residual, delta, position_embeddings, cache):
+        """``(residual stream, pending delta) -> (residual stream, MLP output)``.
+
+        The same arithmetic as ``forward`` (h = h + attn(norm(h)); h + mlp(norm(h))),
+        with each residual add done inside the following RMSNorm kernel; the MLP
+        output is returned un-added so the next layer's norm can absorb it.
+        """
+        h, x = self.input_layernorm.fused(residual, delta)
+        h, x = self.post_attention_layernorm.fused(h, self.self_attn(x, position_embeddings, cache))
+        return h, self.mlp(x)
+
+    def fuse_projections_(self):
+        self.self_attn.fuse_qkv_()
+        self.mlp.fuse_()
+        return self
 
 
 class LastKVModel(nn.Module):
@@ -384,14 +501,19 @@ class LastKVModel(nn.Module):
             pos = torch.arange(cache.seen_tokens, cache.seen_tokens + take, device=hidden.device)[None]
             position_embeddings = self.rotary_emb(chunk, pos)
             cache.plan(take)
-            for layer in self.layers:
-                chunk = layer(chunk, position_embeddings, cache)
-            outputs.append(chunk)
+            outputs.append(self.run_layers(chunk, position_embeddings, cache))
             cache.advance(take)
             if cache.seen_tokens % C == 0:
                 cache.commit(self.blend_alpha())
             start += take
-        return self.norm(torch.cat(outputs, dim=1))
+        return outputs[0] if len(outputs) == 1 else torch.cat(outputs, dim=1)
+
+    def run_layers(self, hidden, position_embeddings, cache):
+        """All decoder layers and the final norm over one planned span."""
+        residual, delta = hidden, None
+        for layer in self.layers:
+            residual, delta = layer.forward_residual(residual, delta, position_embeddings, cache)
+        return self.norm.fused(residual, delta)[1]
 
     def blend_alpha(self) -> torch.Tensor:
         cached = getattr(self, "_alpha", None)
@@ -409,6 +531,13 @@ class LastKVForCausalLM(nn.Module):
         self.config = config
         self.model = LastKVModel(config)
         self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+
+    def fuse_projections_(self):
+        """Fuse each layer's q/k/v and gate/up projections into one GEMM each (inference).
+        Parameter names and state-dict loading are unchanged; call after moving the model."""
+        for layer in self.model.layers:
+            layer.fuse_projections_()
+        return self
 
     def new_cache(self, batch: int, max_tokens: int, **kw) -> PagedLastKVCache:
         return PagedLastKVCache(self.config, batch, max_tokens, device=self.lm_head.weight.device, **kw)

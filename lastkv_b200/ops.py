@@ -282,5 +282,58 @@ def build_layer_block_tables(block_table, nsrc, ring_base, out=None):
     return out
 
 
+def _rows2d(t, name):
+    _require(t.dtype == torch.bfloat16 and t.is_cuda and t.stride(-1) == 1, f"{name} must be CUDA bf16 with unit stride")
+    return t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
+
+
+def rmsnorm(x, weight, eps: float, residual=None, *, out=None, residual_out=None):
+    """RMSNorm over the last dim, optionally after the residual add h = x + residual.
+
+    Returns ``out`` (the normalised rows), or ``(h, out)`` when ``residual`` is
+    given; ``h`` is written to ``residual_out`` (default: a new tensor).  The
+    rounding points are those of the eager decoder layer (see lkv_rmsnorm).
+    """
+    shape = x.shape
+    H = shape[-1]
+    x2 = _rows2d(x, "x")
+    _require(weight.dtype == torch.bfloat16 and weight.is_contiguous() and weight.numel() == H,
+             "weight must be contiguous bf16 [hidden]")
+    rows = x2.shape[0]
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+    _require(out.is_contiguous() and out.shape == shape, "out must be contiguous and match x")
+    o2 = _rows2d(out, "out")
+    r2 = ro2 = None
+    if residual is not None:
+        _require(residual.shape == shape, "residual must match x")
+        r2 = _rows2d(residual, "residual")
+        if residual_out is None:
+            residual_out = torch.empty(shape, dtype=torch.bfloat16, device=x.device)
+        _require(residual_out.is_contiguous() and residual_out.shape == shape,
+                 "residual_out must be contiguous and match x")
+        ro2 = _rows2d(residual_out, "residual_out")
+    st = _capi.lib().lkv_rmsnorm(x2.data_ptr(), x2.stride(0), _ptr(r2), r2.stride(0) if r2 is not None else 0,
+                                 _ptr(ro2), ro2.stride(0) if ro2 is not None else 0, weight.data_ptr(),
+                                 o2.data_ptr(), o2.stride(0), rows, H, float(eps), _stream())
+    _capi.check(st, "lkv_rmsnorm")
+    return out if residual is None else (residual_out, out)
+
+
+def silu_mul(gate_up, *, out=None):
+    """bf16(bf16(silu(gate)) * up) for rows [gate | up] of width 2F; returns [..., F]."""
+    F2 = gate_up.shape[-1]
+    _require(F2 % 2 == 0, "gate_up must hold [gate | up]")
+    g2 = _rows2d(gate_up, "gate_up")
+    if out is None:
+        out = torch.empty((*gate_up.shape[:-1], F2 // 2), dtype=torch.bfloat16, device=gate_up.device)
+    _require(out.is_contiguous() and out.shape == (*gate_up.shape[:-1], F2 // 2), "out must be contiguous [..., F]")
+    o2 = _rows2d(out, "out")
+    st = _capi.lib().lkv_silu_mul(g2.data_ptr(), g2.stride(0), o2.data_ptr(), o2.stride(0), g2.shape[0], F2 // 2,
+                                  _stream())
+    _capi.check(st, "lkv_silu_mul")
+    return out
+
+
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)

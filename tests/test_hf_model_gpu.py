@@ -18,7 +18,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def build_small(data, page_order=None):
+def build_small(data, page_order=None, fused=False):
     from lastkv_b200.hf import LastKVConfig, LastKVForCausalLM
 
     cfg = LastKVConfig(hidden_size=int(data["hidden_size"]), intermediate_size=int(data["intermediate_size"]),
@@ -29,12 +29,16 @@ def build_small(data, page_order=None):
                        deep_v_scale_init=data["v_scale"].tolist())
     model = LastKVForCausalLM(cfg)
     model.load_reference_state_dict({k[2:]: torch.from_numpy(v) for k, v in data.items() if k.startswith("w_")})
-    return model.cuda().to(torch.bfloat16).eval()
+    model = model.cuda().to(torch.bfloat16).eval()
+    return model.fuse_projections_() if fused else model
 
 
-def test_incremental_logits_match_reference(small_d128):
+@pytest.mark.parametrize("fused", [False, True], ids=["modules", "fused_projections"])
+def test_incremental_logits_match_reference(small_d128, fused):
+    """Both the module-per-projection path and the fused q|k|v, gate|up GEMMs with the
+    RMSNorm / SiLU-and-mul kernels meet the same tolerance."""
     data = small_d128
-    model = build_small(data)
+    model = build_small(data, fused=fused)
     tokens = torch.from_numpy(data["tokens"]).cuda()
     B, T = tokens.shape
     per = -(-T // 16)
@@ -57,12 +61,13 @@ def test_incremental_logits_match_reference(small_d128):
     assert rel <= 2e-2 and err <= 5e-2 * span
 
 
-def test_greedy_generation_matches_reference(small_d128):
+@pytest.mark.parametrize("fused", [False, True], ids=["modules", "fused_projections"])
+def test_greedy_generation_matches_reference(small_d128, fused):
     """Teacher-forced on the reference's greedy continuation: every step picks the
     reference's token unless the reference's own top-2 margin is within twice this
     model's logit error at that step (a bf16-vs-fp32 near-tie)."""
     data = small_d128
-    model = build_small(data)
+    model = build_small(data, fused=fused)
     prompt = torch.from_numpy(data["generate_prompt"]).cuda()
     ref = data["generate_out"]
     n_new = ref.shape[1] - prompt.shape[1]
@@ -102,3 +107,26 @@ def test_cache_reorder_matches_fresh_run(small_d128):
         model(tokens[order, :21], c2)
         b, _ = model(tokens[order, 21:40], c2)
     torch.testing.assert_close(a.float(), b.float(), rtol=0, atol=0)
+
+
+def test_fused_parameters_alias_and_reload(small_d128):
+    """After fusing, the projections are views of the fused weights: a strict reference
+    state-dict load writes through them, and the fused path still matches the modules."""
+    data = small_d128
+    state = {k[2:]: torch.from_numpy(v) for k, v in data.items() if k.startswith("w_")}
+    fused = build_small(data, fused=True)
+    attn = fused.model.layers[0].self_attn
+    w, _ = attn._qkv
+    assert attn.q_proj.weight.data_ptr() == w.data_ptr()
+    with torch.no_grad():
+        w.zero_()
+    fused.load_reference_state_dict(state)  # reloads through the views
+    plain = build_small(data)
+    tokens = torch.from_numpy(data["tokens"]).cuda()
+    with torch.no_grad():
+        a, _ = fused(tokens[:, :21], fused.new_cache(2, 32))
+        b, _ = plain(tokens[:, :21], plain.new_cache(2, 32))
+    a, b = a.float().cpu().numpy(), b.float().cpu().numpy()
+    rel = np.linalg.norm(a - b) / np.linalg.norm(b)
+    print(f"fused vs modules: rel_l2={rel:.3e}")
+    assert rel <= 1e-2
