@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace lkv {
 
@@ -57,6 +58,8 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 
 template <int D>
 __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParams p) {
+  pdl_launch_dependents();
+  pdl_wait();  // q/k/v come from the projection GEMM
   constexpr int HALF = D / 2;
   constexpr int E = HALF / 32;  // rotary pairs per lane (2 for D=128, 1 for D=64)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -348,11 +351,9 @@ int rope_norm_append(const AppendArgs& a) {
   p.err = a.error_word;
   dim3 grid((a.num_q_heads + a.num_kv_heads + 7) / 8, a.num_tokens);
   cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
-  if (a.head_dim == 128)
-    rope_norm_append_kernel<128><<<grid, 256, 0, stream>>>(p);
-  else
-    rope_norm_append_kernel<64><<<grid, 256, 0, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+  const cudaError_t e = a.head_dim == 128 ? launch_pdl(rope_norm_append_kernel<128>, grid, dim3(256), 0, stream, p)
+                                          : launch_pdl(rope_norm_append_kernel<64>, grid, dim3(256), 0, stream, p);
+  return e == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
 }
 
 int blend_chunk(const BlendArgs& a) {

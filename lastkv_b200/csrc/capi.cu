@@ -4,12 +4,14 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
 
 #include "kernels.h"
 #include "lastkv_b200.h"
+#include "launch.cuh"
 
 namespace lkv {
 
@@ -33,6 +35,14 @@ EncodeTiledFn encode_fn() {
 }
 
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LKV_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 // 4-D map over the pool [num_pages, 16, Hkv, D] (innermost first: D, Hkv, 16,
 // pages), copying one (page, kv head, 64-wide half of D) tile of 16 rows x
@@ -68,6 +78,26 @@ int make_query_tensor_map(CUtensorMap* map, const void* q, int64_t total_q, int6
   cuuint32_t box[3] = {64, (cuuint32_t)group, (cuuint32_t)(128 / group)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LKV_OK : LKV_ERR_TENSOR_MAP;
+}
+
+// 2-D map over a row-major bf16 matrix [rows, cols] (row stride in elements),
+// copying (box_rows x 64 columns) tiles of 128-byte rows, 128-byte swizzled: a
+// K-major UMMA operand tile.  Reads past the matrix fill zeros.
+int make_matrix_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride,
+                           int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LKV_ERR_TENSOR_MAP;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || rows < 1 || cols < 1 || rows > (int64_t)0x7fffffff ||
+      cols > (int64_t)0x7fffffff || row_stride < cols || (row_stride * 2) % 16 || box_rows < 1 || box_rows > 256)
+    return LKV_ERR_INVALID_ARGUMENT;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LKV_OK : LKV_ERR_TENSOR_MAP;
@@ -287,6 +317,21 @@ int lkv_rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t resi
 int lkv_silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
                  void* stream) {
   return lkv::silu_mul(gate_up, gate_up_row, out, out_row, rows, ffn, static_cast<cudaStream_t>(stream));
+}
+
+int lkv_decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* splits, int* ctas_per_sm) {
+  return lkv::decode_gemm_plan(n_rows, k, mode, tiles, splits, ctas_per_sm);
+}
+
+size_t lkv_decode_gemm_workspace_bytes(int64_t n_rows, int64_t k, int mode) {
+  return lkv::decode_gemm_workspace_bytes(n_rows, k, mode);
+}
+
+int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row, int m,
+                    int64_t n_rows, int64_t k, int mode, void* workspace, size_t workspace_bytes,
+                    int32_t* error_word, int* splits, void* stream) {
+  return lkv::decode_gemm(x, x_row, w, w_row, y, y_row, m, n_rows, k, mode, workspace, workspace_bytes, error_word,
+                          static_cast<cudaStream_t>(stream), splits);
 }
 
 }  // extern "C"

@@ -29,6 +29,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace lkv {
 
@@ -94,6 +95,8 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  pdl_wait();  // q, the appended keys and the tables come from the previous kernels
 
   const int n = max(0, p.seq_k[b]);
   const int npages = min((n + PAGE - 1) / PAGE, p.W);
@@ -321,6 +324,8 @@ struct MergeParams {
 template <int D>
 __global__ void __launch_bounds__(128) merge_partials_kernel(const MergeParams p) {
   constexpr int PER = D / 32;
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 4 + warp;
   if (row >= p.rows) return;
@@ -441,8 +446,9 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
   prm.S = S;
   prm.final_out = (S == 1 && !partial_mode) ? 1 : 0;
   dim3 grid(S, prm.Hkv, prm.B);
-  decode_splitkv_kernel<D, GROUP, kNW, STAGES><<<grid, (kNW + 1) * 32, Cfg::SMEM_BYTES, stream>>>(tmk, tmv, prm);
-  if (cudaGetLastError() != cudaSuccess) return LKV_ERR_CUDA;
+  if (launch_pdl(decode_splitkv_kernel<D, GROUP, kNW, STAGES>, grid, dim3((kNW + 1) * 32), Cfg::SMEM_BYTES, stream,
+                 tmk, tmv, prm) != cudaSuccess)
+    return LKV_ERR_CUDA;
   if (prm.final_out) return LKV_OK;
   MergeParams mp{};
   mp.part_o = prm.part_o;
@@ -460,8 +466,10 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
     mp.out_f32 = part_o_user;
     mp.out_lse_f32 = part_lse_user;
   }
-  merge_partials_kernel<D><<<(unsigned)((rows + 3) / 4), 128, 0, stream>>>(mp);
-  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+  return launch_pdl(merge_partials_kernel<D>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, stream, mp) ==
+                 cudaSuccess
+             ? LKV_OK
+             : LKV_ERR_CUDA;
 }
 
 }  // namespace
@@ -626,11 +634,9 @@ int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, 
   mp.out_stride_tok = (int64_t)hq * head_dim;
   mp.lse_out = lse_out;
   const unsigned blocks = (unsigned)((rows + 3) / 4);
-  if (head_dim == 128)
-    merge_partials_kernel<128><<<blocks, 128, 0, stream>>>(mp);
-  else
-    merge_partials_kernel<64><<<blocks, 128, 0, stream>>>(mp);
-  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+  const cudaError_t e = head_dim == 128 ? launch_pdl(merge_partials_kernel<128>, dim3(blocks), dim3(128), 0, stream, mp)
+                                         : launch_pdl(merge_partials_kernel<64>, dim3(blocks), dim3(128), 0, stream, mp);
+  return e == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
 }
 
 }  // namespace lkv

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace lkv {
 
@@ -62,6 +63,8 @@ struct RmsParams {
 };
 
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const RmsParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int nvec = p.hidden / 8;
   const uint4* x = reinterpret_cast<const uint4*>(p.x + row * p.x_row);
@@ -112,6 +115,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const RmsParams p
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gate_up, int64_t gu_row,
                                                        __nv_bfloat16* __restrict__ out, int64_t out_row,
                                                        int64_t rows, int ffn) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int nv = ffn / 8;
   const int64_t total = rows * nv;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -154,8 +159,8 @@ int rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual
               out_row,
               hidden,
               eps};
-  rmsnorm_kernel<<<rows, kNormThreads, 0, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+  return launch_pdl(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, stream, p) == cudaSuccess ? LKV_OK
+                                                                                                  : LKV_ERR_CUDA;
 }
 
 int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
@@ -167,9 +172,11 @@ int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_ro
     return LKV_ERR_INVALID_ARGUMENT;
   const int64_t total = rows * (ffn / 8);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
-  silu_mul_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gate_up), gate_up_row,
-                                              static_cast<__nv_bfloat16*>(out), out_row, rows, ffn);
-  return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+  return launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, stream,
+                    static_cast<const __nv_bfloat16*>(gate_up), gate_up_row, static_cast<__nv_bfloat16*>(out),
+                    out_row, rows, ffn) == cudaSuccess
+             ? LKV_OK
+             : LKV_ERR_CUDA;
 }
 
 }  // namespace lkv

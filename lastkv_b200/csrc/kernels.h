@@ -13,6 +13,8 @@ namespace lkv {
 constexpr size_t kWorkspaceHeader = 256;
 
 int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, int num_kv_heads, int head_dim);
+int make_matrix_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride,
+                           int box_rows);
 int make_query_tensor_map(CUtensorMap* map, const void* q, int64_t total_q, int64_t q_stride_tok, int num_q_heads,
                           int head_dim, int group);
 
@@ -125,5 +127,11 @@ int rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual
             cudaStream_t stream);
 int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
              cudaStream_t stream);
+
+size_t decode_gemm_workspace_bytes(int64_t n_rows, int64_t k, int mode);
+int decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* splits, int* ctas_per_sm);
+int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row, int m,
+                int64_t n_rows, int64_t k, int mode, void* workspace, size_t workspace_bytes, int32_t* error_word,
+                cudaStream_t stream, int* splits_out);
 
 }  // namespace lkv

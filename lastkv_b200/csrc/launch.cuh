@@ -1,0 +1,43 @@
+// Kernel launches with programmatic dependent launch (PDL).
+//
+// A kernel launched through launch_pdl() may start while the previous kernel
+// in the stream is still draining; it must execute pdl_wait() (griddepcontrol
+// .wait, which returns once the previous grid has completed and its writes are
+// visible) before it reads anything that kernel produced and before any global
+// write.  Work that touches neither - barrier set-up, TMEM allocation, tensor
+// map prefetch, streaming weights into shared memory - overlaps the previous
+// kernel's tail.  Kernels call pdl_launch_dependents() early so the next one can
+// be scheduled; the next grid starts only after every CTA of this one has
+// called it (or exited), so it never takes resources this grid still needs.
+// Setting LKV_PDL=0 in the environment launches without the attribute (plain
+// stream order; the device-side calls are then no-ops).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace lkv {
+
+bool pdl_enabled();
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace lkv

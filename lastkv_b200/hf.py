@@ -174,6 +174,17 @@ def _fused_ok(fused, linears) -> bool:
     return True
 
 
+def _decode_gate_up(x, weight):
+    """``silu(x @ gate.T) * (x @ up.T)`` on the tcgen05 decode GEMM (weight = [gate | up])
+    for at most 16 bf16 rows - one weight stream with the SiLU-and-mul in its epilogue;
+    None when the shapes are not decode-sized.  The other projections stay on cuBLAS,
+    which streams the narrower weights of a decode step faster than this kernel's
+    split-K launches."""
+    if ops.decode_gemm_supported(x, weight):
+        return ops.decode_gemm(x, weight, silu_mul=True)
+    return None
+
+
 class MLP(nn.Module):
     def __init__(self, config):
         super().__init__()
@@ -189,7 +200,11 @@ class MLP(nn.Module):
 
     def forward(self, x):
         if x.is_cuda and x.dtype == torch.bfloat16 and _fused_ok(self._gate_up, [self.gate_proj, self.up_proj]):
-            return self.down_proj(ops.silu_mul(F.linear(x, self._gate_up[0])))
+            w = self._gate_up[0]
+            h = _decode_gate_up(x, w)
+            if h is None:
+                h = ops.silu_mul(F.linear(x, w))
+            return self.down_proj(h)
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -405,7 +420,8 @@ class LastKVAttention(nn.Module):
         B, L, _ = hidden_states.shape
         D, Hq, Hkv = self.head_dim, self.num_heads, self.num_key_value_heads
         meta = cache._meta if cache._meta is not None and cache._meta["n"] == L else cache.plan(L)
-        if _fused_ok(self._qkv, [self.q_proj, self.k_proj, self.v_proj]):
+        fast = _fused_ok(self._qkv, [self.q_proj, self.k_proj, self.v_proj])
+        if fast:
             qkv = F.linear(hidden_states, *self._qkv).reshape(B * L, (Hq + 2 * Hkv) * D)
             q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
         else:
@@ -533,8 +549,11 @@ class LastKVForCausalLM(nn.Module):
         self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
 
     def fuse_projections_(self):
-        """Fuse each layer's q/k/v and gate/up projections into one GEMM each (inference).
-        Parameter names and state-dict loading are unchanged; call after moving the model."""
+        """Inference fast path: each layer's q/k/v and gate/up projections become one
+        GEMM each, and decode-sized gate/up calls (<= 16 rows) run on the tcgen05
+        decode GEMM with the SiLU-and-mul in its epilogue.  Parameter names and
+        state-dict loading are unchanged; call after moving the model (a later move
+        falls back to the module path)."""
         for layer in self.model.layers:
             layer.fuse_projections_()
         return self

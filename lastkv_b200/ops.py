@@ -335,5 +335,74 @@ def silu_mul(gate_up, *, out=None):
     return out
 
 
+GEMM_PLAIN, GEMM_SILU_MUL = 0, 1
+DECODE_GEMM_MAX_ROWS = 16
+_GEMM_WS: dict = {}
+
+
+def _gemm_workspace(device, nbytes: int) -> torch.Tensor:
+    """One zero-initialised workspace per device, grown (outside graph capture) to the largest shape seen."""
+    key = (device.type, device.index)
+    ws = _GEMM_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        _require(not torch.cuda.is_current_stream_capturing(),
+                 "decode_gemm: run each shape once before CUDA-graph capture (its workspace is sized then)")
+        ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
+        _GEMM_WS[key] = ws
+    return ws
+
+
+def decode_gemm_supported(x, weight) -> bool:
+    """Whether ``decode_gemm(x, weight)`` takes these tensors (else use F.linear)."""
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and weight.dim() == 2):
+        return False
+    K = x.shape[-1]
+    rows = x.numel() // K if K else 0
+    return (1 <= rows <= DECODE_GEMM_MAX_ROWS and weight.shape[1] == K and K % 8 == 0 and x.stride(-1) == 1
+            and weight.stride(1) == 1 and weight.stride(0) % 8 == 0 and weight.data_ptr() % 16 == 0
+            and x.data_ptr() % 16 == 0 and (x.dim() == 2 or x.is_contiguous()) and x.stride(0) % 8 == 0)
+
+
+def decode_gemm_plan(n_rows: int, k: int, silu_mul: bool = False) -> dict:
+    """{tiles, splits, ctas_per_sm} of the decode GEMM launch for a weight [n_rows, k] on this device."""
+    import ctypes
+
+    t, s, o = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _capi.check(_capi.lib().lkv_decode_gemm_plan(n_rows, k, GEMM_SILU_MUL if silu_mul else GEMM_PLAIN,
+                                                 ctypes.byref(t), ctypes.byref(s), ctypes.byref(o)),
+                "lkv_decode_gemm_plan")
+    return {"tiles": t.value, "splits": s.value, "ctas_per_sm": o.value}
+
+
+def decode_gemm(x, weight, *, silu_mul: bool = False, out=None, error_word=None):
+    """``x @ weight.T`` for 1..16 rows of x (decode) on tcgen05, bf16 out.
+
+    ``silu_mul``: weight holds [gate (F rows) | up (F rows)] and the result is
+    ``silu(x @ gate.T) * (x @ up.T)`` [..., F] with the eager rounding points.
+    Capturable in CUDA graphs once the shape has run eagerly.
+    """
+    K = x.shape[-1]
+    x2 = _rows2d(x, "x")
+    M = x2.shape[0]
+    _require(1 <= M <= DECODE_GEMM_MAX_ROWS, f"decode_gemm takes 1..{DECODE_GEMM_MAX_ROWS} rows")
+    _require(weight.dtype == torch.bfloat16 and weight.dim() == 2 and weight.stride(1) == 1 and weight.shape[1] == K,
+             "weight must be bf16 [N, K] rows")
+    N = weight.shape[0]
+    mode = GEMM_SILU_MUL if silu_mul else GEMM_PLAIN
+    n_out = N // 2 if silu_mul else N
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n_out), dtype=torch.bfloat16, device=x.device)
+    _require(out.is_contiguous() and out.shape == (*x.shape[:-1], n_out) and out.dtype == torch.bfloat16,
+             "out must be contiguous bf16 [..., N]")
+    lib = _capi.lib()
+    nbytes = lib.lkv_decode_gemm_workspace_bytes(N, K, mode)
+    _require(nbytes > 0, "decode_gemm: unsupported shape")
+    ws = _gemm_workspace(x.device, nbytes)
+    st = lib.lkv_decode_gemm(x2.data_ptr(), x2.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(), n_out,
+                             M, N, K, mode, ws.data_ptr(), ws.numel(), _ptr(error_word), None, _stream())
+    _capi.check(st, "lkv_decode_gemm")
+    return out
+
+
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
