@@ -264,23 +264,20 @@ int lkv_silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t ou
  * reference's q/k/v, o, gate/up and down projections, modeling.py decoder
  * layer; vLLM's QKVParallelLinear / MergedColumnParallelLinear in its model).
  * tcgen05 with the weight rows as the MMA's M side; fp32 accumulation; split-K
- * partials are added in a fixed order (deterministic).
+ * partials are reduced inside a thread-block cluster in a fixed order
+ * (deterministic).  No workspace; one launch; capturable in CUDA graphs.
  *   LKV_GEMM_PLAIN:     y[m, n] = bf16(acc), n < n_rows.
  *   LKV_GEMM_SILU_MUL:  w = [gate (F rows) | up (F rows)], n_rows = 2F;
  *                       y[m, j] = bf16(bf16(silu(bf16(gate))) * bf16(up)), j < F.
- * x and w: 16-byte aligned, row strides (elements) multiples of 8.  workspace:
- * at least lkv_decode_gemm_workspace_bytes(n_rows, k, mode) bytes, 256-byte
- * aligned, ZERO-FILLED before first use (it holds per-tile counters that every
- * launch leaves at zero) and used by one stream at a time.  *splits (optional)
- * receives the split-K factor (launches: 1).  Capturable in CUDA graphs. */
+ * x and w: 16-byte aligned, row strides (elements) multiples of 8; y row stride
+ * >= the output width.  *splits (optional) receives the split-K factor. */
 #define LKV_GEMM_PLAIN 0
 #define LKV_GEMM_SILU_MUL 1
-size_t lkv_decode_gemm_workspace_bytes(int64_t n_rows, int64_t k, int mode);
 /* The launch this device will use: weight tiles, split-K factor, CTAs per SM. */
 int lkv_decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* splits, int* ctas_per_sm);
 int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row,
-                    int m, int64_t n_rows, int64_t k, int mode, void* workspace, size_t workspace_bytes,
-                    int32_t* error_word, int* splits, void* stream);
+                    int m, int64_t n_rows, int64_t k, int mode, int32_t* error_word, int* splits,
+                    void* stream);
 
 #ifdef __cplusplus
 }

@@ -47,9 +47,8 @@ _SIGNATURES = {
     "lkv_build_layer_block_tables": (I32, [P, I64, P, P, I32, I32, I32, P, P]),
     "lkv_rmsnorm": (I32, [P, I64, P, I64, P, I64, P, P, I64, I32, I32, F32, P]),
     "lkv_silu_mul": (I32, [P, I64, P, I64, I64, I32, P]),
-    "lkv_decode_gemm_workspace_bytes": (SZ, [I64, I64, I32]),
     "lkv_decode_gemm_plan": (I32, [I64, I64, I32, P, P, P]),
-    "lkv_decode_gemm": (I32, [P, I64, P, I64, P, I64, I32, I64, I64, I32, P, SZ, P, P, P]),
+    "lkv_decode_gemm": (I32, [P, I64, P, I64, P, I64, I32, I64, I64, I32, P, P, P]),
     "lkv_prefill_paged": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
                                 I32, I32, I32, I32, I32, I32, I32, I32, F32, P, P]),
 }

@@ -323,14 +323,9 @@ int lkv_decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* s
   return lkv::decode_gemm_plan(n_rows, k, mode, tiles, splits, ctas_per_sm);
 }
 
-size_t lkv_decode_gemm_workspace_bytes(int64_t n_rows, int64_t k, int mode) {
-  return lkv::decode_gemm_workspace_bytes(n_rows, k, mode);
-}
-
 int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row, int m,
-                    int64_t n_rows, int64_t k, int mode, void* workspace, size_t workspace_bytes,
-                    int32_t* error_word, int* splits, void* stream) {
-  return lkv::decode_gemm(x, x_row, w, w_row, y, y_row, m, n_rows, k, mode, workspace, workspace_bytes, error_word,
+                    int64_t n_rows, int64_t k, int mode, int32_t* error_word, int* splits, void* stream) {
+  return lkv::decode_gemm(x, x_row, w, w_row, y, y_row, m, n_rows, k, mode, error_word,
                           static_cast<cudaStream_t>(stream), splits);
 }
 

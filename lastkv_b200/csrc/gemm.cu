@@ -1,5 +1,5 @@
 // Decode-shaped weight GEMM on tcgen05 (sm_100a): y[m, n] = sum_k x[m, k] * w[n, k]
-// for m < 16 rows of activations (one decode token per sequence) against a
+// for m <= 16 rows of activations (one decode token per sequence) against a
 // bf16 weight matrix w [n_rows, k] (the nn.Linear layout).
 //
 // At decode batch sizes the GEMM is a weight stream: every weight byte is read
@@ -9,13 +9,17 @@
 // Both operands are TMA-loaded, 128-byte swizzled and K-major, 64 columns of k
 // (one 128-byte row) per pipeline stage; the weight loads carry an evict-first
 // L2 hint.  One thread produces, one thread issues tcgen05.mma, then all four
-// warps read their 32 TMEM lanes each for the epilogue.
+// warps read their 32 TMEM lanes each for the epilogue.  Launched with PDL: the
+// first stages' weights stream in while the previous kernel drains; the
+// activation loads and every global write wait for it (griddepcontrol.wait).
 //
-// Split-K: when tiles alone do not fill the GPU, each tile's k range is split
-// over `splits` CTAs that write fp32 partials; the last CTA to arrive (a ticket
-// counter per tile, reset by that CTA) adds them in split order - so results do
-// not depend on arrival order - and runs the epilogue.  Nothing waits on
-// another CTA.
+// Split-K inside a thread-block cluster: when the tiles alone do not fill the
+// GPU, the k range of each tile is split over the CTAs of one cluster (<= 8,
+// co-scheduled by the hardware).  Each CTA leaves its fp32 partial tile in its
+// own shared memory; after a cluster barrier every CTA reduces a slice of the
+// tile's rows from all partials over distributed shared memory, adding them in
+// split order (results do not depend on timing), and a second barrier keeps
+// the partials alive until all CTAs are done.  No global scratch, no atomics.
 //
 // Epilogues (the rounding points of the eager torch modules):
 //   LKV_GEMM_PLAIN     y = bf16(acc)                                 (nn.Linear)
@@ -39,9 +43,9 @@ namespace {
 constexpr int kRows = 128;    // weight rows per tile (UMMA M)
 constexpr int kBatch = 16;    // activation rows (UMMA N), zero-padded
 constexpr int kKB = 64;       // k per stage: one 128-byte swizzled row
-constexpr int kStages = 5;  // 93 KB: two CTAs share an SM
+constexpr int kStages = 5;    // 93 KB: two CTAs share an SM
 constexpr int kThreads = 128;
-constexpr int kMaxSplits = 16;
+constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr int kWStage = kRows * 128;
 constexpr int kXStage = kBatch * 128;
 constexpr int kStageBytes = kWStage + kXStage;
@@ -53,13 +57,11 @@ constexpr int kKernelId = 7;
 struct GemmParams {
   __nv_bfloat16* y;
   int64_t y_row;
-  float* partial;
-  unsigned int* tickets;
   int m;          // activation rows (1..16)
   int n_out;      // output columns
   int half_rows;  // SILU_MUL: F (the up rows start there)
   int kb_total;
-  int splits;
+  int splits;     // = cluster size along y
   int mode;
   int* err;
 };
@@ -69,10 +71,54 @@ struct GemmBars {
   uint64_t empty[kStages];
   uint64_t acc;
   uint32_t tmem;
-  int last;
 };
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();  // the barrier is .aligned: every warp arrives converged
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Sum over the cluster's partials (split order) of element `e` of the [kBatch][kRows] partial tile.
+__device__ __forceinline__ float cluster_sum(uint32_t part, int splits, int e) {
+  float v[kMaxSplits];
+#pragma unroll
+  for (int s = 0; s < kMaxSplits; ++s) v[s] = s < splits ? dsmem_ld(dsmem_map(part, s) + e * 4) : 0.f;
+  float sum = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxSplits; ++s)
+    if (s < splits) sum += v[s];
+  return sum;
+}
+
+__device__ __forceinline__ float silu_mul_round(float g_acc, float u_acc) {
+  const float g = bf16_round(g_acc);
+  const float s = bf16_round(g / (1.0f + expf(-g)));
+  return s * bf16_round(u_acc);
+}
 
 __global__ void __launch_bounds__(kThreads, 2)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
@@ -96,7 +142,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->acc, 1);
-    bars->last = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -122,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_load_2d_hint(smem + i * kStageBytes + kWStage / 2, &tmw, &bars->full[i], (kb0 + i) * kKB, r_hi, pol);
     }
     pdl_wait();
-    for (int i = 0; i < pre; ++i) tma_load_2d(smem + i * kStageBytes + kWStage, &tmx, &bars->full[i], (kb0 + i) * kKB, 0);
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(smem + i * kStageBytes + kWStage, &tmx, &bars->full[i], (kb0 + i) * kKB, 0);
     for (int i = pre; i < nkb; ++i) {
       const int s = i % kStages;
       if (!mbar_wait(&bars->empty[s], ((i / kStages) & 1) ^ 1)) {
@@ -170,55 +216,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int j = 0; j < kBatch; ++j) acc[j] = __uint_as_float(v[j]);
   }
-  pdl_wait();  // before any global write (the workspace and y may still be read by the previous kernel)
+  pdl_wait();  // before any global write (y may still be read by the previous kernel)
 
-  bool write = true;
-  if (p.splits > 1) {
-    float* mine = p.partial + (size_t)(tile * p.splits + split) * kBatch * kRows;
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j)
-      if (j < p.m) mine[j * kRows + r] = acc[j];
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const unsigned prev = atomicAdd(&p.tickets[tile], 1u);
-      bars->last = prev == (unsigned)(p.splits - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    write = bars->last != 0;
-    if (write) {
-      __threadfence();
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        float sum = 0.f;
-        if (j < p.m)
-          for (int sp = 0; sp < p.splits; ++sp)
-            sum += __ldcg(p.partial + ((size_t)(tile * p.splits + sp) * kBatch + j) * kRows + r);
-        acc[j] = sum;
-      }
-      if (threadIdx.x == 0) p.tickets[tile] = 0u;  // every CTA of this tile has arrived
-    }
-  }
-
-  if (write) {  // CTA-uniform
+  // The stage ring is idle once the accumulator is complete (every TMA load was
+  // consumed by an MMA that has finished): the epilogue reuses its first bytes.
+  float* xs = reinterpret_cast<float*>(smem);  // [kBatch][kRows] fp32
+  if (p.splits == 1) {
     if (p.mode == LKV_GEMM_SILU_MUL) {
-      // the stage ring is idle once the accumulator is complete: exchange the up rows through it
-      float* xch = reinterpret_cast<float*>(smem);
       if (r >= 64) {
 #pragma unroll
-        for (int j = 0; j < kBatch; ++j) xch[(r - 64) * (kBatch + 1) + j] = bf16_round(acc[j]);
+        for (int j = 0; j < kBatch; ++j) xs[j * kRows + r] = acc[j];
       }
       __syncthreads();
       const int n = tile * 64 + r;
       if (r < 64 && n < p.n_out) {
 #pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-          if (j < p.m) {
-            const float g = bf16_round(acc[j]);
-            const float s = bf16_round(g / (1.0f + expf(-g)));
-            p.y[(int64_t)j * p.y_row + n] = __float2bfloat16_rn(s * xch[r * (kBatch + 1) + j]);
-          }
-        }
+        for (int j = 0; j < kBatch; ++j)
+          if (j < p.m) p.y[(int64_t)j * p.y_row + n] = __float2bfloat16_rn(silu_mul_round(acc[j], xs[j * kRows + r + 64]));
       }
     } else {
       const int n = tile * kRows + r;
@@ -228,6 +242,32 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (j < p.m) p.y[(int64_t)j * p.y_row + n] = __float2bfloat16_rn(acc[j]);
       }
     }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (j < p.m) xs[j * kRows + r] = acc[j];
+    cluster_sync_all();  // every CTA of the tile has published its partial
+    const int rank = (int)cluster_rank();
+    const uint32_t part = smem_u32(xs);
+    if (p.mode == LKV_GEMM_SILU_MUL) {
+      const int g0 = rank * 64 / p.splits, ng = (rank + 1) * 64 / p.splits - g0;
+      for (int idx = threadIdx.x; idx < ng * p.m; idx += kThreads) {
+        const int j = idx / ng, g = g0 + idx % ng;
+        const int n = tile * 64 + g;
+        const float gs = cluster_sum(part, p.splits, j * kRows + g);
+        const float us = cluster_sum(part, p.splits, j * kRows + g + 64);
+        if (n < p.n_out) p.y[(int64_t)j * p.y_row + n] = __float2bfloat16_rn(silu_mul_round(gs, us));
+      }
+    } else {
+      const int r0 = rank * kRows / p.splits, nr = (rank + 1) * kRows / p.splits - r0;
+      for (int idx = threadIdx.x; idx < nr * p.m; idx += kThreads) {
+        const int j = idx / nr, row = r0 + idx % nr;
+        const int n = tile * kRows + row;
+        const float s = cluster_sum(part, p.splits, j * kRows + row);
+        if (n < p.n_out) p.y[(int64_t)j * p.y_row + n] = __float2bfloat16_rn(s);
+      }
+    }
+    cluster_sync_all();  // the partials stay readable until every CTA has reduced its slice
   }
 
   tc_fence_before();
@@ -282,8 +322,8 @@ struct GemmPlan {
   int tiles, splits, kb_total, n_out;
 };
 
-// Split count: minimise (waves) x (k blocks per CTA + pipeline fill), as the
-// decode kernel does for its key splits.
+// Split count (a power of two <= 8): minimise (waves) x (k blocks per CTA +
+// pipeline fill), as the decode kernel does for its key splits.
 GemmPlan plan_gemm(int64_t n_rows, int64_t k, int mode, int slots) {
   GemmPlan g{};
   g.n_out = (int)(mode == LKV_GEMM_SILU_MUL ? n_rows / 2 : n_rows);
@@ -293,22 +333,17 @@ GemmPlan plan_gemm(int64_t n_rows, int64_t k, int mode, int slots) {
   int64_t best = INT64_MAX;
   g.splits = 1;
   const int smax = std::min(kMaxSplits, g.kb_total);
-  for (int s = 1; s <= smax; ++s) {
+  // power-of-two cluster sizes pack onto the GPCs' SM pairs without leftovers
+  for (int s = 1; s <= smax; s *= 2) {
     const int64_t ctas = (int64_t)g.tiles * s;
     const int64_t waves = (ctas + slots - 1) / slots;
-    const int64_t cost = waves * ((g.kb_total + s - 1) / s + fill) + (s > 1 ? 2 : 0);
+    const int64_t cost = waves * ((g.kb_total + s - 1) / s + fill) + (s > 1 ? 1 : 0);
     if (cost < best) {
       best = cost;
       g.splits = s;
     }
   }
   return g;
-}
-
-size_t ticket_bytes(int tiles) { return ((size_t)tiles * 4 + 255) / 256 * 256; }
-
-size_t plan_bytes(const GemmPlan& g) {
-  return ticket_bytes(g.tiles) + (g.splits > 1 ? (size_t)g.tiles * g.splits * kBatch * kRows * 4 : 0);
 }
 
 bool valid_shape(int64_t n_rows, int64_t k, int mode) {
@@ -332,16 +367,8 @@ int decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* split
   return LKV_OK;
 }
 
-size_t decode_gemm_workspace_bytes(int64_t n_rows, int64_t k, int mode) {
-  if (!valid_shape(n_rows, k, mode)) return 0;
-  int sms = 0, occ = 0;
-  if (gemm_device(&sms, &occ) != LKV_OK) return 0;
-  return plan_bytes(plan_gemm(n_rows, k, mode, sms * occ));
-}
-
 int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row, int m,
-                int64_t n_rows, int64_t k, int mode, void* workspace, size_t workspace_bytes, int32_t* error_word,
-                cudaStream_t stream, int* splits_out) {
+                int64_t n_rows, int64_t k, int mode, int32_t* error_word, cudaStream_t stream, int* splits_out) {
   if (!valid_shape(n_rows, k, mode) || m < 1 || m > kBatch || !x || !w || !y) return LKV_ERR_INVALID_ARGUMENT;
   int sms = 0, occ = 0;
   int st = gemm_device(&sms, &occ);
@@ -349,8 +376,6 @@ int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void
   const GemmPlan g = plan_gemm(n_rows, k, mode, sms * occ);
   if (y_row < g.n_out) return LKV_ERR_INVALID_ARGUMENT;
   if (splits_out) *splits_out = g.splits;
-  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < plan_bytes(g))
-    return LKV_ERR_WORKSPACE;
   CUtensorMap tmw, tmx;
   st = make_matrix_tensor_map(&tmw, w, n_rows, k, w_row, 64);
   if (st != LKV_OK) return st;
@@ -359,8 +384,6 @@ int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void
   GemmParams p{};
   p.y = static_cast<__nv_bfloat16*>(y);
   p.y_row = y_row;
-  p.tickets = static_cast<unsigned int*>(workspace);
-  p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ticket_bytes(g.tiles));
   p.m = m;
   p.n_out = g.n_out;
   p.half_rows = (int)(n_rows / 2);
@@ -368,8 +391,8 @@ int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void
   p.splits = g.splits;
   p.mode = mode;
   p.err = error_word;
-  return launch_pdl(decode_gemm_kernel, dim3(g.tiles, g.splits), dim3(kThreads), kSmemBytes, stream, tmw, tmx, p) ==
-                 cudaSuccess
+  return launch_pdl(decode_gemm_kernel, dim3(g.tiles, g.splits), dim3(kThreads), kSmemBytes, stream,
+                    dim3(1, g.splits, 1), tmw, tmx, p) == cudaSuccess
              ? LKV_OK
              : LKV_ERR_CUDA;
 }

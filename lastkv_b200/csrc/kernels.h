@@ -128,10 +128,8 @@ int rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual
 int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
              cudaStream_t stream);
 
-size_t decode_gemm_workspace_bytes(int64_t n_rows, int64_t k, int mode);
 int decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* splits, int* ctas_per_sm);
 int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row, int m,
-                int64_t n_rows, int64_t k, int mode, void* workspace, size_t workspace_bytes, int32_t* error_word,
-                cudaStream_t stream, int* splits_out);
+                int64_t n_rows, int64_t k, int mode, int32_t* error_word, cudaStream_t stream, int* splits_out);
 
 }  // namespace lkv

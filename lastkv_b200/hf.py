@@ -174,14 +174,13 @@ def _fused_ok(fused, linears) -> bool:
     return True
 
 
-def _decode_gate_up(x, weight):
-    """``silu(x @ gate.T) * (x @ up.T)`` on the tcgen05 decode GEMM (weight = [gate | up])
-    for at most 16 bf16 rows - one weight stream with the SiLU-and-mul in its epilogue;
-    None when the shapes are not decode-sized.  The other projections stay on cuBLAS,
-    which streams the narrower weights of a decode step faster than this kernel's
-    split-K launches."""
-    if ops.decode_gemm_supported(x, weight):
-        return ops.decode_gemm(x, weight, silu_mul=True)
+def _decode_linear(x, weight, bias=None, silu_mul=False):
+    """``F.linear`` (or, with ``silu_mul``, ``silu(x @ gate.T) * (x @ up.T)`` for
+    weight = [gate | up]) on the tcgen05 decode GEMM for at most 16 bf16 rows
+    without bias - the decode-step shapes, where every projection of a layer is
+    one weight stream chained to its neighbours by PDL; None otherwise."""
+    if bias is None and ops.decode_gemm_supported(x, weight):
+        return ops.decode_gemm(x, weight, silu_mul=silu_mul)
     return None
 
 
@@ -201,10 +200,11 @@ class MLP(nn.Module):
     def forward(self, x):
         if x.is_cuda and x.dtype == torch.bfloat16 and _fused_ok(self._gate_up, [self.gate_proj, self.up_proj]):
             w = self._gate_up[0]
-            h = _decode_gate_up(x, w)
+            h = _decode_linear(x, w, silu_mul=True)
             if h is None:
                 h = ops.silu_mul(F.linear(x, w))
-            return self.down_proj(h)
+            y = _decode_linear(h, self.down_proj.weight, self.down_proj.bias)
+            return y if y is not None else self.down_proj(h)
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -422,7 +422,10 @@ class LastKVAttention(nn.Module):
         meta = cache._meta if cache._meta is not None and cache._meta["n"] == L else cache.plan(L)
         fast = _fused_ok(self._qkv, [self.q_proj, self.k_proj, self.v_proj])
         if fast:
-            qkv = F.linear(hidden_states, *self._qkv).reshape(B * L, (Hq + 2 * Hkv) * D)
+            qkv = _decode_linear(hidden_states, *self._qkv)
+            if qkv is None:
+                qkv = F.linear(hidden_states, *self._qkv)
+            qkv = qkv.reshape(B * L, (Hq + 2 * Hkv) * D)
             q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
         else:
             q = self.q_proj(hidden_states).reshape(B * L, Hq * D)
@@ -459,7 +462,8 @@ class LastKVAttention(nn.Module):
             out = ops.prefill_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], meta["cu_q"], L,
                                     out_scale=out_scale, error_word=cache.error_word, max_pages=meta["W"])
         out = out.view(B, L, Hq * D).to(hidden_states.dtype)
-        return self.o_proj(out)
+        y = _decode_linear(out, self.o_proj.weight, self.o_proj.bias) if fast else None
+        return y if y is not None else self.o_proj(out)
 
 
 class LastKVDecoderLayer(nn.Module):
@@ -550,10 +554,10 @@ class LastKVForCausalLM(nn.Module):
 
     def fuse_projections_(self):
         """Inference fast path: each layer's q/k/v and gate/up projections become one
-        GEMM each, and decode-sized gate/up calls (<= 16 rows) run on the tcgen05
-        decode GEMM with the SiLU-and-mul in its epilogue.  Parameter names and
-        state-dict loading are unchanged; call after moving the model (a later move
-        falls back to the module path)."""
+        GEMM each, and decode-sized calls (<= 16 rows) of every projection run on the
+        tcgen05 decode GEMM (gate/up with the SiLU-and-mul in its epilogue).
+        Parameter names and state-dict loading are unchanged; call after moving the
+        model (a later move falls back to the module path)."""
         for layer in self.model.layers:
             layer.fuse_projections_()
         return self

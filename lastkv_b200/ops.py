@@ -337,19 +337,6 @@ def silu_mul(gate_up, *, out=None):
 
 GEMM_PLAIN, GEMM_SILU_MUL = 0, 1
 DECODE_GEMM_MAX_ROWS = 16
-_GEMM_WS: dict = {}
-
-
-def _gemm_workspace(device, nbytes: int) -> torch.Tensor:
-    """One zero-initialised workspace per device, grown (outside graph capture) to the largest shape seen."""
-    key = (device.type, device.index)
-    ws = _GEMM_WS.get(key)
-    if ws is None or ws.numel() < nbytes:
-        _require(not torch.cuda.is_current_stream_capturing(),
-                 "decode_gemm: run each shape once before CUDA-graph capture (its workspace is sized then)")
-        ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
-        _GEMM_WS[key] = ws
-    return ws
 
 
 def decode_gemm_supported(x, weight) -> bool:
@@ -379,7 +366,7 @@ def decode_gemm(x, weight, *, silu_mul: bool = False, out=None, error_word=None)
 
     ``silu_mul``: weight holds [gate (F rows) | up (F rows)] and the result is
     ``silu(x @ gate.T) * (x @ up.T)`` [..., F] with the eager rounding points.
-    Capturable in CUDA graphs once the shape has run eagerly.
+    Capturable in CUDA graphs.
     """
     K = x.shape[-1]
     x2 = _rows2d(x, "x")
@@ -394,12 +381,8 @@ def decode_gemm(x, weight, *, silu_mul: bool = False, out=None, error_word=None)
         out = torch.empty((*x.shape[:-1], n_out), dtype=torch.bfloat16, device=x.device)
     _require(out.is_contiguous() and out.shape == (*x.shape[:-1], n_out) and out.dtype == torch.bfloat16,
              "out must be contiguous bf16 [..., N]")
-    lib = _capi.lib()
-    nbytes = lib.lkv_decode_gemm_workspace_bytes(N, K, mode)
-    _require(nbytes > 0, "decode_gemm: unsupported shape")
-    ws = _gemm_workspace(x.device, nbytes)
-    st = lib.lkv_decode_gemm(x2.data_ptr(), x2.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(), n_out,
-                             M, N, K, mode, ws.data_ptr(), ws.numel(), _ptr(error_word), None, _stream())
+    st = _capi.lib().lkv_decode_gemm(x2.data_ptr(), x2.stride(0), weight.data_ptr(), weight.stride(0),
+                                     out.data_ptr(), n_out, M, N, K, mode, _ptr(error_word), None, _stream())
     _capi.check(st, "lkv_decode_gemm")
     return out
 
