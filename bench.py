@@ -62,9 +62,10 @@ def parse():
     ap.add_argument("--case", default="config2", choices=["config2", "small"],
                     help="small: 8 sequences x 2 layers, for ncu captures")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "cp128k", "e2e8b"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "cp128k", "e2e8b", "decode_gemm"],
                     help="cp128k: config 4, 128K-context decode sharded over the ranks; "
-                         "e2e8b: config 3, the 8B-architecture model end to end")
+                         "e2e8b: config 3, the 8B-architecture model end to end; "
+                         "decode_gemm: its projections on the decode GEMM vs cuBLAS")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
@@ -741,7 +742,14 @@ def run_e2e8b(args):
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
     splits, per_call = ops.decode_plan(B, c["q_heads"], Hkv, D, cache.pages_per_seq + cache.ring_pages,
                                        cache.workspace)
-    launches_per_step = 1 + L * (1 + per_call)  # block tables + per layer (append + decode [+ merge])
+    # ours per step: block tables + final RMSNorm + per layer (2 RMSNorm, 4 decode GEMMs
+    # [q|k|v, o, gate|up+SiLU, down], append, split-KV decode [+ merge]); the embedding
+    # gather, rotary table, LM head (cuBLAS) and argmax are torch ops
+    launches_per_step = 2 + L * (2 + 4 + 1 + per_call)
+    H, F_ = c["hidden"], c["ffn"]
+    gemm_plans = {name: ops.decode_gemm_plan(n, k, silu) for name, n, k, silu in
+                  (("qkv", (c["q_heads"] + 2 * Hkv) * D, H, False), ("o", c["q_heads"] * D, H, False),
+                   ("gate_up", 2 * F_, H, True), ("down", H, F_, False))}
     tokens = B * args.steps * world
     h2d = sum(t.numel() * t.element_size() for k, t in runner._h[0].items()
                                             if k != "done")
@@ -768,12 +776,66 @@ def run_e2e8b(args):
         "clocks": clk,
         "gpu_launches": int(args.steps * launches_per_step),
         "kv_splits": splits,
+        "decode_gemm_plans": gemm_plans,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     del runner
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_decode_gemm(args):
+    """The decode-step projections of the 8B architecture (M = 8 rows) on the tcgen05
+    decode GEMM and on cuBLAS (torch), each timed inside a CUDA graph over enough
+    weight copies (> 600 MB) that no weight is L2-resident between calls."""
+    import torch
+
+    from lastkv_b200 import _capi, ops
+
+    torch.cuda.set_device(0)
+    _capi.load()
+    c = E2E8B
+    H, F_, D = c["hidden"], c["ffn"], c["head_dim"]
+    shapes = [("qkv", (c["q_heads"] + 2 * c["kv_heads"]) * D, H, False), ("o", c["q_heads"] * D, H, False),
+              ("gate_up_silu", 2 * F_, H, True), ("down", H, F_, False), ("lm_head", c["vocab"], H, False)]
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    rows = []
+    for name, n, k, silu in shapes:
+        nbytes = n * k * 2
+        copies = max(2, int(600e6 // nbytes) + 1)
+        ws = [(torch.randn((n, k), generator=gen, device="cuda") * 0.02).bfloat16() for _ in range(copies)]
+        x = torch.randn((8, k), generator=gen, device="cuda").bfloat16()
+        res = {}
+        for impl in ("ours", "cublas"):
+            def run(w):
+                if impl == "ours":
+                    return ops.decode_gemm(x, w, silu_mul=silu)
+                y = torch.nn.functional.linear(x, w)
+                return ops.silu_mul(y) if silu else y
+            for w in ws:
+                run(w)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for w in ws:
+                    run(w)
+            for _ in range(max(args.warmup, 1)):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = max(args.steps, 1)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+            res[impl] = {"us": us, "gbs": nbytes / us / 1e3}
+            del g
+        rows.append({"name": name, "n_rows": n, "k": k, "weight_bytes": nbytes,
+                     "plan": ops.decode_gemm_plan(n, k, silu), "ours": res["ours"], "cublas": res["cublas"]})
+        del ws
+        torch.cuda.empty_cache()
+    print(json.dumps({"workload": "decode_gemm", "m": 8, "steps": args.steps, "shapes": rows}), flush=True)
 
 
 def main():
@@ -791,6 +853,8 @@ def main():
         run_cp(args)
     elif args.workload == "e2e8b":
         run_e2e8b(args)
+    elif args.workload == "decode_gemm":
+        run_decode_gemm(args)
     else:
         run_ours(args)
 
