@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
+    ap.add_argument("--cp-combine", default="p2p", choices=["p2p", "nccl"],
+                    help="cp128k: combine the partials over peer memory (one kernel) or NCCL all-gather + merge")
     ap.add_argument("--e2e-layers", type=int, default=None,
                     help="e2e8b with fewer layers (same per-layer shapes), for profiler captures; never a bench line")
     return ap.parse_args()
@@ -572,7 +574,7 @@ def run_cp(args):
     out = torch.empty((L, B, Hq, D), dtype=torch.bfloat16, device=device)
     scale = torch.ones(Hq, device=device)
     ws = ops.Workspace.for_decode(B, Hq, D, pages_mine, device=device)
-    cp = ContextParallelDecode()
+    cp = ContextParallelDecode(combine=args.cp_combine if world > 1 else "nccl")
 
     def step():
         for l in range(L):
@@ -592,6 +594,7 @@ def run_cp(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    cp.check_errors()
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -604,7 +607,9 @@ def run_cp(args):
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "cp128k", "batch": B, "context_tokens": N, "ring_window": Wt, "q_heads": Hq,
                        "kv_heads": H, "head_dim": D, "layers_per_step": L,
-                       "parallelism": f"cp{world} (shared pages sharded, NCCL all-gather + LSE merge)"},
+                       "parallelism": f"cp{world} (shared pages sharded; " + (
+                           "peer-memory push + LSE merge in one kernel)" if cp.combine == "p2p" and world > 1
+                           else "NCCL all-gather + LSE merge)")},
             "layer_ms": layer_ms, "attn_bytes_per_layer_total": bytes_layer,
             "hbm_gbs_per_gpu": bytes_layer / world / (layer_ms * 1e-3) / 1e9,
             "combine_bytes_per_rank_per_layer": B * Hq * (D + 1) * 4}

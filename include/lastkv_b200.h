@@ -279,6 +279,27 @@ int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, 
                     int m, int64_t n_rows, int64_t k, int mode, int32_t* error_word, int* splits,
                     void* stream);
 
+/* ------------------------------------------------------------------ context-parallel combine
+ * Exchange + LSE merge of sequence-sharded decode partials over NVLink peer
+ * memory, replacing the all-gather of the partials and lkv_merge_partials for
+ * the 128K-context path (the two-partial merge_state of
+ * flashinfer_executor.py:185-231 applied to `world` ranks; the reference
+ * itself enforces CP = 1, runtime_contract.py:124-133).
+ * send: this rank's partial packed as o fp32 [rows, head_dim] (normalised) |
+ * lse fp32 [rows] (natural log), send_floats floats (lkv_cp_combine_sizes).
+ * peer_recv[r] (a HOST array of `world` device addresses valid on this GPU):
+ * rank r's receive buffer of recv_words 8-byte words, zero before the first
+ * call.  Each value travels as one {value, epoch} word, so no fence or flag is
+ * needed.  epoch: 1, 2, 3, ... incremented by one per call, the same on every
+ * rank; every rank must make the same sequence of calls.  A rank waits at most
+ * ~2 s for its peers (then the error word is set and the rows it could not
+ * complete hold garbage).  out: bf16 rows (tok = row / hq, head = row % hq)
+ * scaled by out_scale[head] (may be NULL). */
+int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_floats, int64_t* recv_words);
+int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch,
+                   int64_t rows, int head_dim, int hq, const float* out_scale, void* out,
+                   int64_t out_stride_tok, int32_t* error_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

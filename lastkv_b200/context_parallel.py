@@ -46,23 +46,41 @@ class ShardPlan:
 
 
 def plan_shard(nsrc_pages: int, window_tokens: int, page: int, world: int, rank: int) -> ShardPlan:
-    p0, p1 = shard_range(nsrc_pages, world, rank)
+    """This rank's keys: the last rank holds the ring window, so its shared-page
+    share is its even share of all pages minus the ring pages (every rank then
+    streams about the same number of pages); the other ranks split the rest."""
+    ring = -(-window_tokens // page)
+    last_src = nsrc_pages if world == 1 else min(nsrc_pages, max(0, round((nsrc_pages + ring) / world) - ring))
+    first = nsrc_pages - last_src
     last = rank == world - 1
-    ring_pages = -(-window_tokens // page) if last else 0
-    return ShardPlan(p0, p1, ring_pages, (p1 - p0) * page + (window_tokens if last else 0))
+    if last:
+        p0, p1 = first, nsrc_pages
+    else:
+        if not 0 <= rank < world:
+            raise RMarinBackendContractError("invalid rank / world size")
+        p0, p1 = shard_range(first, world - 1, rank)
+    return ShardPlan(p0, p1, ring if last else 0, (p1 - p0) * page + (window_tokens if last else 0))
 
 
 class ContextParallelDecode:
     """Sequence-sharded decode for one process group (NCCL on GPUs, gloo for host tests).
 
-    With the default kernels each rank writes its partial (o, lse) into one
-    packed send buffer [B*Hq*D | B*Hq] so a single all-gather per layer moves
-    it, and the merge kernel reads the gathered parts in place.  ``partial_fn``
-    and ``merge_fn`` can be injected (host tests) and then use separate
-    o / lse tensors.
+    Each rank writes its partial (o, lse) into one packed send buffer
+    [B*Hq*D | B*Hq | pad].  ``combine`` picks how the partials meet:
+
+    * ``"p2p"`` (default with more than one CUDA rank): one ``lkv_cp_combine``
+      launch per layer pushes this rank's rows into every peer's receive buffer
+      over NVLink peer memory (torch symmetric memory), waits for the peers'
+      rows and merges in rank order - no collective call and no merge launch;
+    * ``"nccl"``: one ``all_gather_into_tensor`` of the packed buffers, then the
+      merge kernel over the gathered parts in place.
+
+    Both merge the same partials in the same order (identical outputs).
+    ``partial_fn`` and ``merge_fn`` can be injected (host tests) and then use
+    separate o / lse tensors over the process group's all-gather.
     """
 
-    def __init__(self, group=None, *, partial_fn=None, merge_fn=None):
+    def __init__(self, group=None, *, partial_fn=None, merge_fn=None, combine: str | None = None):
         import torch.distributed as dist
 
         self.dist = dist
@@ -72,7 +90,41 @@ class ContextParallelDecode:
         self.injected = partial_fn is not None or merge_fn is not None
         self.partial_fn = partial_fn or self._partial_kernel
         self.merge_fn = merge_fn or self._merge_kernel
+        if combine is None:
+            combine = "p2p" if self.world > 1 and not self.injected else "nccl"
+        if combine not in ("p2p", "nccl"):
+            raise RMarinBackendContractError(f"unknown combine {combine!r}")
+        if combine == "p2p" and self.injected:
+            raise RMarinBackendContractError("the p2p combine runs the CUDA kernels only")
+        self.combine = combine
         self._bufs = {}
+        self._p2p = {}
+
+    def _p2p_state(self, B, Hq, D, device):
+        """Receive buffers in symmetric memory (allocated and exchanged once per shape)."""
+        key = (B, Hq, D, str(device))
+        st = self._p2p.get(key)
+        if st is None:
+            import torch.distributed._symmetric_memory as symm
+
+            group = self.group if self.group is not None else self.dist.group.WORLD
+            sizes = ops.cp_combine_sizes(B * Hq, D, self.world)
+            recv = symm.empty(sizes["recv_words"], dtype=torch.int64, device=device)
+            recv.zero_()
+            torch.cuda.synchronize(device)
+            h_recv = symm.rendezvous(recv, group)
+            h_recv.barrier()  # every rank's receive words are zero before anyone pushes
+            st = {"recv": recv, "handle": h_recv, "recv_ptrs": [int(x) for x in h_recv.buffer_ptrs],
+                  "send": torch.empty(sizes["send_floats"], dtype=torch.float32, device=device),
+                  "error": torch.zeros(4, dtype=torch.int32, device=device), "epoch": 0}
+            self._p2p[key] = st
+        return st
+
+    def check_errors(self):
+        for st in self._p2p.values():
+            e = st["error"].cpu().tolist()
+            if e[0]:
+                raise RMarinBackendContractError(f"context-parallel combine error word set: {e}")
 
     @staticmethod
     def _partial_kernel(q, pool_k, pool_v, block_table, seq_k, workspace, max_pages):
@@ -94,6 +146,15 @@ class ContextParallelDecode:
         if self.injected:
             return self._layer_generic(q, pool_k, pool_v, block_table, seq_k, out_scale, out, workspace, max_pages)
         B, Hq, D = q.shape
+        if self.combine == "p2p":
+            st = self._p2p_state(B, Hq, D, q.device)
+            send = st["send"]
+            ops.decode_paged(q, pool_k, pool_v, block_table, seq_k, workspace=workspace, max_pages=max_pages,
+                             partial=True, partial_out=(send[: B * Hq * D].view(B, Hq, D),
+                                                        send[B * Hq * D: B * Hq * (D + 1)].view(B, Hq)))
+            st["epoch"] += 1
+            return ops.cp_combine(send, st["recv_ptrs"], self.rank, self.world, st["epoch"], B * Hq, D, Hq,
+                                  out_scale=out_scale, out=out, error_word=st["error"])
         n = -(-(B * Hq * (D + 1)) // 4) * 4  # o | lse | pad to a multiple of 4 floats (float4 reads)
         send, recv = self._buffers(("packed", n, str(q.device)), lambda: (
             torch.empty(n, dtype=torch.float32, device=q.device),

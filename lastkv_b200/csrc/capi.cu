@@ -329,4 +329,18 @@ int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, 
                           static_cast<cudaStream_t>(stream), splits);
 }
 
+int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_floats, int64_t* recv_words) {
+  if (rows < 1 || head_dim < 1 || world < 1 || world > lkv::kCpMaxRanks) return LKV_ERR_INVALID_ARGUMENT;
+  if (send_floats) *send_floats = (rows * (head_dim + 1) + 3) / 4 * 4;
+  if (recv_words) *recv_words = 2 * (int64_t)world * lkv::cp_part_words(rows, head_dim);
+  return LKV_OK;
+}
+
+int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch, int64_t rows,
+                   int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok,
+                   int32_t* error_word, void* stream) {
+  return lkv::cp_combine(send, peer_recv, rank, world, epoch, rows, head_dim, hq, out_scale, out, out_stride_tok,
+                         error_word, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -1,0 +1,193 @@
+// Context-parallel combine over NVLink peer memory (sm_100a): the exchange and
+// LSE merge of the per-rank decode partials for sequence-sharded (128K) decode,
+// in one kernel instead of an all-gather collective plus a merge launch.
+//
+// Every rank holds a partial (o fp32 [rows, D] normalised, lse [rows] natural
+// log) over its slice of each sequence's keys.  CTA c owns rows
+// [c * R, (c + 1) * R) on every rank and
+//   1. pushes those rows of this rank's partial into slot [epoch & 1][rank] of
+//      every peer's receive buffer with plain peer stores (NVLink P2P), each
+//      fp32 value travelling with the epoch in one 8-byte word {value, epoch}
+//      (an aligned 8-byte store arrives whole, so no fence or separate flag
+//      is needed: a word is valid once its epoch half matches);
+//   2. merges the world partials of its rows in rank order exactly as
+//      merge_partials_kernel does (same arithmetic, same order), reading the
+//      peers' words from its own receive buffer and polling each until its
+//      epoch half matches - bounded by wall time, with the error word set on
+//      expiry - then scales by s_l per query head and writes bf16.
+// A CTA waits only on CTAs of other GPUs, which push before they wait, so no
+// CTA depends on another CTA of its own grid.  Receive slots alternate with the
+// epoch parity: a peer can reuse a slot only after it has received this rank's
+// next epoch, which this rank pushes after it finished reading that slot.
+// No multicast and no NVLS: plain loads and stores to peer-mapped memory.
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+
+namespace lkv {
+
+namespace {
+
+constexpr int kCpThreads = 128;  // 4 warps: one output row each at a time
+constexpr int kCpKernelId = 8;
+
+struct CpPeers {
+  uint64_t* recv[kCpMaxRanks];
+};
+
+struct CpParams {
+  const float* send;    // this rank's packed partial: o [rows * D] | lse [rows]
+  int64_t part_words;   // words per partial in a receive slot (>= rows * (D + 1))
+  int64_t rows;
+  int rows_per_cta;
+  int Hq, rank, world;
+  uint32_t epoch;
+  const float* out_scale;
+  __nv_bfloat16* out;
+  int64_t out_stride_tok;
+  int* err;
+};
+
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | (uint64_t)__float_as_uint(v);
+}
+
+__device__ __forceinline__ void st_ll2(uint64_t* dst, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_ll(const uint64_t* src) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
+  return v;
+}
+
+// Poll one word until it carries `epoch` (or the wall-time limit passes: then `fail` is set).
+__device__ __forceinline__ float ll_take(const uint64_t* src, uint32_t epoch, uint64_t start, bool& fail) {
+  uint64_t w = ld_ll(src);
+  for (uint32_t it = 1; (uint32_t)(w >> 32) != epoch && !fail; ++it) {
+    if ((it & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) fail = true;
+    w = ld_ll(src);
+  }
+  return __uint_as_float((uint32_t)w);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kCpThreads)
+    cp_combine_kernel(const __grid_constant__ CpPeers peers, const __grid_constant__ CpParams p) {
+  constexpr int PER = D / 32;
+  pdl_launch_dependents();
+  pdl_wait();  // the partial comes from the decode kernel
+  const int c = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = (int64_t)c * p.rows_per_cta;
+  const int64_t r1 = r0 + p.rows_per_cta < p.rows ? r0 + p.rows_per_cta : p.rows;
+  const int slot = (int)(p.epoch & 1u);
+  const int64_t lse_off = p.rows * D;
+
+  // 1. push this CTA's rows to every peer: pairs of {value, epoch} words
+  const int64_t npair = (r1 - r0) * D / 2;
+  const float2* src_o = reinterpret_cast<const float2*>(p.send + r0 * D);
+  for (int peer = 0; peer < p.world; ++peer) {
+    if (peer == p.rank) continue;
+    uint64_t* dst = peers.recv[peer] + ((int64_t)slot * p.world + p.rank) * p.part_words;
+    for (int64_t i = threadIdx.x; i < npair; i += kCpThreads) {
+      const float2 v = src_o[i];
+      st_ll2(dst + r0 * D + 2 * i, ll_word(v.x, p.epoch), ll_word(v.y, p.epoch));
+    }
+    for (int64_t i = r0 + threadIdx.x; i < r1; i += kCpThreads) {
+      const uint64_t w = ll_word(p.send[lse_off + i], p.epoch);
+      asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst + lse_off + i), "l"(w) : "memory");
+    }
+  }
+
+  // 2. merge in rank order (merge_partials_kernel arithmetic); peers' words are polled
+  const uint64_t* slot_base = peers.recv[p.rank] + (int64_t)slot * p.world * p.part_words;
+  const uint64_t start = global_timer_ns();
+  bool fail = false;
+  constexpr float to2 = 1.4426950408889634f;
+  for (int64_t row = r0 + warp; row < r1; row += kCpThreads / 32) {
+    auto lse_of = [&](int s) -> float {
+      return s == p.rank ? p.send[lse_off + row]
+                         : ll_take(slot_base + (int64_t)s * p.part_words + lse_off + row, p.epoch, start, fail);
+    };
+    float M = -INFINITY;
+    for (int s = lane; s < p.world; s += 32) M = fmaxf(M, lse_of(s) * to2);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float acc[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+    float L = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < p.world; ++s) {
+        const float ls = lse_of(s) * to2;
+        if (ls == -INFINITY) continue;
+        const float w = exp2f(ls - M);
+        L += w;
+        float v[PER];
+        if (s == p.rank) {
+#pragma unroll
+          for (int e = 0; e < PER; ++e) v[e] = p.send[row * D + lane * PER + e];
+        } else {
+          const uint64_t* src = slot_base + (int64_t)s * p.part_words + row * D + lane * PER;
+#pragma unroll
+          for (int e = 0; e < PER; ++e) v[e] = ll_take(src + e, p.epoch, start, fail);
+        }
+#pragma unroll
+        for (int e = 0; e < PER; ++e) acc[e] += w * v[e];
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int h = (int)(row % p.Hq);
+    const int64_t tok = row / p.Hq;
+    const float sc = (p.out_scale ? p.out_scale[h] : 1.f) * inv;
+    __nv_bfloat16* dst = p.out + tok * p.out_stride_tok + (int64_t)h * D + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(acc[e] * sc, acc[e + 1] * sc);
+  }
+  if (fail) report_error(p.err, DEVERR_WAIT_TIMEOUT, kCpKernelId, (int)r0);
+}
+
+}  // namespace
+
+int64_t cp_part_words(int64_t rows, int head_dim) { return (rows * (head_dim + 1) + 1) / 2 * 2; }
+
+int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch, int64_t rows,
+               int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok, int32_t* error_word,
+               cudaStream_t stream) {
+  if (world < 1 || world > kCpMaxRanks || rank < 0 || rank >= world || rows < 1 || hq < 1 || rows % hq ||
+      (head_dim != 64 && head_dim != 128) || !send || !peer_recv || !out || epoch == 0)
+    return LKV_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(send) & 15) || out_stride_tok < (int64_t)hq * head_dim || (out_stride_tok % 2) ||
+      (reinterpret_cast<uintptr_t>(out) & 3))
+    return LKV_ERR_INVALID_ARGUMENT;
+  CpPeers peers{};
+  for (int r = 0; r < world; ++r) {
+    if (!peer_recv[r] || (peer_recv[r] & 15)) return LKV_ERR_INVALID_ARGUMENT;
+    peers.recv[r] = reinterpret_cast<uint64_t*>(peer_recv[r]);
+  }
+  CpParams p{};
+  p.send = send;
+  p.part_words = cp_part_words(rows, head_dim);
+  p.rows = rows;
+  p.rows_per_cta = kCpRowsPerCta;
+  p.Hq = hq;
+  p.rank = rank;
+  p.world = world;
+  p.epoch = epoch;
+  p.out_scale = out_scale;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride_tok = out_stride_tok;
+  p.err = error_word;
+  const unsigned grid = (unsigned)((rows + kCpRowsPerCta - 1) / kCpRowsPerCta);
+  const cudaError_t e = head_dim == 128
+                            ? launch_pdl(cp_combine_kernel<128>, dim3(grid), dim3(kCpThreads), 0, stream, peers, p)
+                            : launch_pdl(cp_combine_kernel<64>, dim3(grid), dim3(kCpThreads), 0, stream, peers, p);
+  return e == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+}  // namespace lkv

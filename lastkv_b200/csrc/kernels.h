@@ -128,6 +128,13 @@ int rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual
 int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
              cudaStream_t stream);
 
+constexpr int kCpMaxRanks = 8;
+constexpr int kCpRowsPerCta = 4;
+int64_t cp_part_words(int64_t rows, int head_dim);
+int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch, int64_t rows,
+               int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok, int32_t* error_word,
+               cudaStream_t stream);
+
 int decode_gemm_plan(int64_t n_rows, int64_t k, int mode, int* tiles, int* splits, int* ctas_per_sm);
 int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void* y, int64_t y_row, int m,
                 int64_t n_rows, int64_t k, int mode, int32_t* error_word, cudaStream_t stream, int* splits_out);

@@ -26,6 +26,14 @@ def test_shard_ranges_cover_everything():
     plans = [plan_shard(8192 // 16, 2048, 16, 4, r) for r in range(4)]
     assert sum(p.seq_k for p in plans) == 8192 + 2048
     assert [p.ring_pages for p in plans] == [0, 0, 0, 128]
+    # pages per rank (shared + ring) are balanced: the ring counts against the last rank
+    assert [p.p1 - p.p0 + p.ring_pages for p in plans] == [160, 160, 160, 160]
+    for nsrc, window, world in [(8064, 2048, 2), (8064, 2048, 8), (3, 2048, 4), (100, 17, 3), (5, 1, 1)]:
+        plans = [plan_shard(nsrc, window, 16, world, r) for r in range(world)]
+        assert plans[0].p0 == 0 and plans[-1].p1 == nsrc
+        assert all(a.p1 == b.p0 for a, b in zip(plans, plans[1:]))
+        assert sum(p.seq_k for p in plans) == nsrc * 16 + window
+    assert [plan_shard(8064, 2048, 16, 2, r).p1 - plan_shard(8064, 2048, 16, 2, r).p0 for r in range(2)] == [4096, 3968]
 
 
 def _free_port():

@@ -1,7 +1,9 @@
-"""Context-parallel decode over NCCL on 2 GPUs: each rank holds half of every
-sequence's shared pages (rank 1 also the ring window), runs the partial decode
-kernel, all-gathers the partials and merges them; every rank must reproduce
-the single-GPU decode of the whole history.  Skipped with fewer than 2 GPUs."""
+"""Context-parallel decode on 2 GPUs: each rank holds half of every sequence's
+shared pages (rank 1 also the ring window) and runs the partial decode kernel;
+the partials meet either through an NCCL all-gather + merge kernel or through
+the peer-memory combine kernel (three calls, both receive slots).  Every rank
+must reproduce the single-GPU decode of the whole history, and the two
+combines must agree bit for bit.  Skipped with fewer than 2 GPUs."""
 
 import os
 import socket
@@ -50,12 +52,16 @@ def _rank(rank, world, port, q, pk, pv, rows, scale, results):
         idx = np.array(local_pages if local_pages else [0])
         lk = torch.from_numpy(pk[idx]).to(dev).bfloat16()
         lv = torch.from_numpy(pv[idx]).to(dev).bfloat16()
-        cp = ContextParallelDecode()
-        out = cp.layer(torch.from_numpy(q).to(dev).bfloat16(), lk, lv, torch.from_numpy(bt_np).to(dev),
-                       torch.tensor(sk, dtype=torch.int32, device=dev),
-                       out_scale=torch.from_numpy(scale).to(dev))
+        args = (torch.from_numpy(q).to(dev).bfloat16(), lk, lv, torch.from_numpy(bt_np).to(dev),
+                torch.tensor(sk, dtype=torch.int32, device=dev))
+        scale_d = torch.from_numpy(scale).to(dev)
+        nccl = ContextParallelDecode(combine="nccl").layer(*args, out_scale=scale_d).float().cpu().numpy()
+        cp = ContextParallelDecode(combine="p2p")
+        # three calls: epochs 1..3 cycle both receive slots
+        p2p = [cp.layer(*args, out_scale=scale_d).float().cpu().numpy() for _ in range(3)]
         torch.cuda.synchronize()
-        results.put((rank, out.float().cpu().numpy()))
+        cp.check_errors()
+        results.put((rank, (nccl, p2p)))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -104,4 +110,7 @@ def test_two_gpu_context_parallel_matches_single_gpu():
                            torch.tensor(sk, dtype=torch.int32, device="cuda"),
                            out_scale=torch.from_numpy(scale).cuda()).float().cpu().numpy()
     for r in range(2):
-        assert_close_bf16(outs[r].reshape(B, Hq, D), ref, max_abs=1.6e-2, rel_l2=6e-3, what=f"rank {r}")
+        nccl, p2p = outs[r]
+        assert_close_bf16(nccl.reshape(B, Hq, D), ref, max_abs=1.6e-2, rel_l2=6e-3, what=f"rank {r}")
+        for i, o in enumerate(p2p):  # the peer-memory combine merges the same partials in the same order
+            np.testing.assert_array_equal(o, nccl, err_msg=f"rank {r} p2p call {i}")
