@@ -1,0 +1,68 @@
+"""The context-parallel combine on one GPU: world = 1 equals the merge kernel,
+and a peer that never pushes makes the bounded wait expire into the error word
+(the failure-detection path, exercised without any GPU fault: the "peer" is a
+local buffer nobody writes, the kernel gives up after its ~2 s limit and the
+context stays usable)."""
+
+import time
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _partial(rows, D, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    o = torch.randn((rows, D), generator=g, device="cuda")
+    lse = torch.randn(rows, generator=g, device="cuda") * 3
+    return o, lse
+
+
+def test_single_rank_equals_merge_kernel():
+    from lastkv_b200 import ops
+
+    B, Hq, D = 3, 8, 128
+    rows = B * Hq
+    sizes = ops.cp_combine_sizes(rows, D, 1)
+    o, lse = _partial(rows, D, 1)
+    send = torch.zeros(sizes["send_floats"], device="cuda")
+    send[: rows * D] = o.flatten()
+    send[rows * D: rows * (D + 1)] = lse
+    recv = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
+    scale = torch.rand(Hq, device="cuda") + 0.5
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    got = ops.cp_combine(send, [recv.data_ptr()], 0, 1, 1, rows, D, Hq, out_scale=scale, error_word=err)
+    ref = ops.merge_partials(o.view(1, B, Hq, D), lse.view(1, B, Hq), out_scale=scale)
+    torch.testing.assert_close(got.view(B, Hq, D), ref.view(B, Hq, D), rtol=0, atol=0)
+    assert err.cpu().tolist() == [0, 0, 0, 0]
+
+
+def test_missing_peer_times_out_into_error_word():
+    from lastkv_b200 import ops
+
+    B, Hq, D = 1, 4, 64
+    rows = B * Hq
+    sizes = ops.cp_combine_sizes(rows, D, 2)
+    o, lse = _partial(rows, D, 2)
+    send = torch.zeros(sizes["send_floats"], device="cuda")
+    send[: rows * D] = o.flatten()
+    send[rows * D: rows * (D + 1)] = lse
+    mine = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
+    peer = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")  # rank 1 never runs
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    t0 = time.time()
+    ops.cp_combine(send, [mine.data_ptr(), peer.data_ptr()], 0, 2, 1, rows, D, Hq, error_word=err)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    e = err.cpu().tolist()
+    assert e[0] == 1 and e[1] == 8, e  # wait timeout, reported by the combine kernel
+    assert 1.0 < waited < 30.0, waited
+    # this rank's push reached the "peer" buffer: {value, epoch = 1} words
+    words = peer.view(2, 2, -1)[1, 0, : rows * D].cpu().numpy().astype(np.uint64)
+    assert np.all((words >> np.uint64(32)) == 1)
+    vals = (words & np.uint64(0xFFFFFFFF)).astype(np.uint32).view(np.float32)
+    np.testing.assert_array_equal(vals, o.flatten().cpu().numpy())
+    # the context is still usable
+    assert float(torch.ones(4, device="cuda").sum()) == 4.0
