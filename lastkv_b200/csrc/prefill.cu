@@ -320,16 +320,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = mx;
       }
       const float neg_mref = (m == -INFINITY) ? 0.f : -m;
-      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(neg_mref, neg_mref);
+      float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int e = 0; e < kBN; e += 2) {
-        const float p0 = ex2_approx(__fmaf_rn(x[e], sl2, neg_mref));
-        const float p1 = ex2_approx(__fmaf_rn(x[e + 1], sl2, neg_mref));
-        sp[(e >> 1) & 7] += p0 + p1;
-        pk[e / 2] = pack_bf16(p0, p1);
+        // f32x2 FFMA / FADD halve the issue slots of the scale-and-subtract and the sums
+        const float2 a = __ffma2_rn(make_float2(x[e], x[e + 1]), sl2v, negm);
+        const float2 pv = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+        sp[(e >> 1) & 3] = __fadd2_rn(sp[(e >> 1) & 3], pv);
+        pk[e / 2] = pack_bf16(pv.x, pv.y);
       }
-      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      const float sum = ((sp[0].x + sp[0].y) + (sp[1].x + sp[1].y)) + ((sp[2].x + sp[2].y) + (sp[3].x + sp[3].y));
       l = l * alpha + sum;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         // O holds blocks < j once PV(j-1) is complete; rescale it in TMEM
