@@ -71,6 +71,7 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
     ap.add_argument("--cp-combine", default="p2p", choices=["p2p", "nccl"],
                     help="cp128k: combine the partials over peer memory (one kernel) or NCCL all-gather + merge")
+    ap.add_argument("--cp-eager", action="store_true", help="cp128k: launch per layer instead of a CUDA graph")
     ap.add_argument("--e2e-layers", type=int, default=None,
                     help="e2e8b with fewer layers (same per-layer shapes), for profiler captures; never a bench line")
     return ap.parse_args()
@@ -584,12 +585,23 @@ def run_cp(args):
     for _ in range(max(args.warmup, 1)):
         step()
     torch.cuda.synchronize()
+    graph = None
+    if not args.cp_eager:
+        # the 32 layer calls of one step (decode partial + combine each) as one CUDA graph
+        if world > 1:
+            dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        step()
+        run()
     e1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -609,12 +621,14 @@ def run_cp(args):
                        "kv_heads": H, "head_dim": D, "layers_per_step": L,
                        "parallelism": f"cp{world} (shared pages sharded; " + (
                            "peer-memory push + LSE merge in one kernel)" if cp.combine == "p2p" and world > 1
-                           else "NCCL all-gather + LSE merge)")},
+                           else "NCCL all-gather + LSE merge)"),
+                       "launch": "eager per layer" if graph is None else "one CUDA graph per step"},
             "layer_ms": layer_ms, "attn_bytes_per_layer_total": bytes_layer,
             "hbm_gbs_per_gpu": bytes_layer / world / (layer_ms * 1e-3) / 1e9,
             "combine_bytes_per_rank_per_layer": B * Hq * (D + 1) * 4}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    del graph, run  # a graph holding collectives goes before the process group
     if world > 1:
         dist.destroy_process_group()
 

@@ -290,13 +290,16 @@ int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, 
  * peer_recv[r] (a HOST array of `world` device addresses valid on this GPU):
  * rank r's receive buffer of recv_words 8-byte words, zero before the first
  * call.  Each value travels as one {value, epoch} word, so no fence or flag is
- * needed.  epoch: 1, 2, 3, ... incremented by one per call, the same on every
- * rank; every rank must make the same sequence of calls.  A rank waits at most
+ * needed.  state: 2 uint32 of device memory per rank (8-byte aligned, zero
+ * before the first call): the epoch of the previous call and a done counter;
+ * each call uses the next epoch, so a call can be captured in a CUDA graph and
+ * replayed.  Every rank must make the same sequence of calls (with its own
+ * state, advanced identically).  A rank waits at most
  * ~2 s for its peers (then the error word is set and the rows it could not
  * complete hold garbage).  out: bf16 rows (tok = row / hq, head = row % hq)
  * scaled by out_scale[head] (may be NULL). */
 int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_floats, int64_t* recv_words);
-int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch,
+int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state,
                    int64_t rows, int head_dim, int hq, const float* out_scale, void* out,
                    int64_t out_stride_tok, int32_t* error_word, void* stream);
 

@@ -49,7 +49,7 @@ _SIGNATURES = {
     "lkv_silu_mul": (I32, [P, I64, P, I64, I64, I32, P]),
     "lkv_decode_gemm_plan": (I32, [I64, I64, I32, P, P, P]),
     "lkv_cp_combine_sizes": (I32, [I64, I32, I32, P, P]),
-    "lkv_cp_combine": (I32, [P, P, I32, I32, ctypes.c_uint32, I64, I32, I32, P, P, I64, P, P]),
+    "lkv_cp_combine": (I32, [P, P, I32, I32, P, I64, I32, I32, P, P, I64, P, P]),
     "lkv_decode_gemm": (I32, [P, I64, P, I64, P, I64, I32, I64, I64, I32, P, P, P]),
     "lkv_prefill_paged": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
                                 I32, I32, I32, I32, I32, I32, I32, I32, F32, P, P]),

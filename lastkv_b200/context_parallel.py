@@ -116,7 +116,8 @@ class ContextParallelDecode:
             h_recv.barrier()  # every rank's receive words are zero before anyone pushes
             st = {"recv": recv, "handle": h_recv, "recv_ptrs": [int(x) for x in h_recv.buffer_ptrs],
                   "send": torch.empty(sizes["send_floats"], dtype=torch.float32, device=device),
-                  "error": torch.zeros(4, dtype=torch.int32, device=device), "epoch": 0}
+                  "state": torch.zeros(2, dtype=torch.int32, device=device),
+                  "error": torch.zeros(4, dtype=torch.int32, device=device)}
             self._p2p[key] = st
         return st
 
@@ -152,8 +153,7 @@ class ContextParallelDecode:
             ops.decode_paged(q, pool_k, pool_v, block_table, seq_k, workspace=workspace, max_pages=max_pages,
                              partial=True, partial_out=(send[: B * Hq * D].view(B, Hq, D),
                                                         send[B * Hq * D: B * Hq * (D + 1)].view(B, Hq)))
-            st["epoch"] += 1
-            return ops.cp_combine(send, st["recv_ptrs"], self.rank, self.world, st["epoch"], B * Hq, D, Hq,
+            return ops.cp_combine(send, st["recv_ptrs"], self.rank, self.world, st["state"], B * Hq, D, Hq,
                                   out_scale=out_scale, out=out, error_word=st["error"])
         n = -(-(B * Hq * (D + 1)) // 4) * 4  # o | lse | pad to a multiple of 4 floats (float4 reads)
         send, recv = self._buffers(("packed", n, str(q.device)), lambda: (

@@ -336,10 +336,10 @@ int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_fl
   return LKV_OK;
 }
 
-int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch, int64_t rows,
+int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state, int64_t rows,
                    int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok,
                    int32_t* error_word, void* stream) {
-  return lkv::cp_combine(send, peer_recv, rank, world, epoch, rows, head_dim, hq, out_scale, out, out_stride_tok,
+  return lkv::cp_combine(send, peer_recv, rank, world, state, rows, head_dim, hq, out_scale, out, out_stride_tok,
                          error_word, static_cast<cudaStream_t>(stream));
 }
 

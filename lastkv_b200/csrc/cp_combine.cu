@@ -4,7 +4,8 @@
 //
 // Every rank holds a partial (o fp32 [rows, D] normalised, lse [rows] natural
 // log) over its slice of each sequence's keys.  CTA c owns rows
-// [c * R, (c + 1) * R) on every rank and
+// [c * R, (c + 1) * R) on every rank and, with this call's epoch (a device
+// counter advanced once per call, so the launch can live in a CUDA graph),
 //   1. pushes those rows of this rank's partial into slot [epoch & 1][rank] of
 //      every peer's receive buffer with plain peer stores (NVLink P2P), each
 //      fp32 value travelling with the epoch in one 8-byte word {value, epoch}
@@ -44,7 +45,7 @@ struct CpParams {
   int64_t rows;
   int rows_per_cta;
   int Hq, rank, world;
-  uint32_t epoch;
+  uint32_t* state;      // [0] epoch of the previous call, [1] CTAs of this call done
   const float* out_scale;
   __nv_bfloat16* out;
   int64_t out_stride_tok;
@@ -80,12 +81,15 @@ __global__ void __launch_bounds__(kCpThreads)
     cp_combine_kernel(const __grid_constant__ CpPeers peers, const __grid_constant__ CpParams p) {
   constexpr int PER = D / 32;
   pdl_launch_dependents();
-  pdl_wait();  // the partial comes from the decode kernel
+  pdl_wait();  // the partial comes from the decode kernel (and the previous call's epoch update)
+  // This call's epoch: one more than the previous call's.  Every CTA reads it
+  // before it counts itself done, and only the last CTA to count advances it.
+  const uint32_t epoch = __ldcg(p.state) + 1u;
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r0 = (int64_t)c * p.rows_per_cta;
   const int64_t r1 = r0 + p.rows_per_cta < p.rows ? r0 + p.rows_per_cta : p.rows;
-  const int slot = (int)(p.epoch & 1u);
+  const int slot = (int)(epoch & 1u);
   const int64_t lse_off = p.rows * D;
 
   // 1. push this CTA's rows to every peer: pairs of {value, epoch} words
@@ -96,10 +100,10 @@ __global__ void __launch_bounds__(kCpThreads)
     uint64_t* dst = peers.recv[peer] + ((int64_t)slot * p.world + p.rank) * p.part_words;
     for (int64_t i = threadIdx.x; i < npair; i += kCpThreads) {
       const float2 v = src_o[i];
-      st_ll2(dst + r0 * D + 2 * i, ll_word(v.x, p.epoch), ll_word(v.y, p.epoch));
+      st_ll2(dst + r0 * D + 2 * i, ll_word(v.x, epoch), ll_word(v.y, epoch));
     }
     for (int64_t i = r0 + threadIdx.x; i < r1; i += kCpThreads) {
-      const uint64_t w = ll_word(p.send[lse_off + i], p.epoch);
+      const uint64_t w = ll_word(p.send[lse_off + i], epoch);
       asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst + lse_off + i), "l"(w) : "memory");
     }
   }
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(kCpThreads)
   for (int64_t row = r0 + warp; row < r1; row += kCpThreads / 32) {
     auto lse_of = [&](int s) -> float {
       return s == p.rank ? p.send[lse_off + row]
-                         : ll_take(slot_base + (int64_t)s * p.part_words + lse_off + row, p.epoch, start, fail);
+                         : ll_take(slot_base + (int64_t)s * p.part_words + lse_off + row, epoch, start, fail);
     };
     float M = -INFINITY;
     for (int s = lane; s < p.world; s += 32) M = fmaxf(M, lse_of(s) * to2);
@@ -135,7 +139,7 @@ __global__ void __launch_bounds__(kCpThreads)
         } else {
           const uint64_t* src = slot_base + (int64_t)s * p.part_words + row * D + lane * PER;
 #pragma unroll
-          for (int e = 0; e < PER; ++e) v[e] = ll_take(src + e, p.epoch, start, fail);
+          for (int e = 0; e < PER; ++e) v[e] = ll_take(src + e, epoch, start, fail);
         }
 #pragma unroll
         for (int e = 0; e < PER; ++e) acc[e] += w * v[e];
@@ -150,17 +154,23 @@ __global__ void __launch_bounds__(kCpThreads)
     for (int e = 0; e < PER; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(acc[e] * sc, acc[e + 1] * sc);
   }
   if (fail) report_error(p.err, DEVERR_WAIT_TIMEOUT, kCpKernelId, (int)r0);
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.state + 1, 1u) == gridDim.x - 1) {
+    p.state[1] = 0u;     // every CTA has read the epoch and counted itself
+    p.state[0] = epoch;  // the next call (stream-ordered after this one) uses epoch + 1
+  }
 }
 
 }  // namespace
 
 int64_t cp_part_words(int64_t rows, int head_dim) { return (rows * (head_dim + 1) + 1) / 2 * 2; }
 
-int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch, int64_t rows,
+int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state, int64_t rows,
                int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok, int32_t* error_word,
                cudaStream_t stream) {
   if (world < 1 || world > kCpMaxRanks || rank < 0 || rank >= world || rows < 1 || hq < 1 || rows % hq ||
-      (head_dim != 64 && head_dim != 128) || !send || !peer_recv || !out || epoch == 0)
+      (head_dim != 64 && head_dim != 128) || !send || !peer_recv || !out || !state ||
+      (reinterpret_cast<uintptr_t>(state) & 7))
     return LKV_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(send) & 15) || out_stride_tok < (int64_t)hq * head_dim || (out_stride_tok % 2) ||
       (reinterpret_cast<uintptr_t>(out) & 3))
@@ -178,7 +188,7 @@ int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world
   p.Hq = hq;
   p.rank = rank;
   p.world = world;
-  p.epoch = epoch;
+  p.state = state;
   p.out_scale = out_scale;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride_tok = out_stride_tok;

@@ -131,7 +131,7 @@ int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_ro
 constexpr int kCpMaxRanks = 8;
 constexpr int kCpRowsPerCta = 4;
 int64_t cp_part_words(int64_t rows, int head_dim);
-int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t epoch, int64_t rows,
+int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state, int64_t rows,
                int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok, int32_t* error_word,
                cudaStream_t stream);
 

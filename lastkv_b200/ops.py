@@ -397,15 +397,18 @@ def cp_combine_sizes(rows: int, head_dim: int, world: int) -> dict:
     return {"send_floats": a.value, "recv_words": b.value}
 
 
-def cp_combine(send, recv_ptrs, rank: int, world: int, epoch: int, rows: int, head_dim: int, hq: int, *,
+def cp_combine(send, recv_ptrs, rank: int, world: int, state, rows: int, head_dim: int, hq: int, *,
                out_scale=None, out=None, error_word=None):
     """Push this rank's packed partial to every peer over peer memory, wait for theirs,
     LSE-merge in rank order (see lkv_cp_combine).  recv_ptrs: per-rank receive-buffer
-    addresses valid on this GPU.  Returns out bf16 [rows / hq, hq, head_dim]."""
+    addresses valid on this GPU; state: int32 [2] device tensor, zero before the first
+    call (the call's epoch advances on the device, so calls can be graph-captured).
+    Returns out bf16 [rows / hq, hq, head_dim]."""
     import ctypes
 
     _require(send.dtype == torch.float32 and send.is_contiguous() and send.is_cuda, "send must be contiguous fp32")
     _require(len(recv_ptrs) == world, "one receive buffer per rank")
+    _require(state.dtype == torch.int32 and state.numel() >= 2 and state.is_cuda, "state must be int32 [2]")
     if out is None:
         out = torch.empty((rows // hq, hq, head_dim), dtype=torch.bfloat16, device=send.device)
     _require(out.dtype == torch.bfloat16 and out.stride(-1) == 1 and out.stride(-2) == head_dim, "out layout")
@@ -413,8 +416,8 @@ def cp_combine(send, recv_ptrs, rank: int, world: int, epoch: int, rows: int, he
         _require(out_scale.dtype == torch.float32 and out_scale.numel() == hq and out_scale.is_contiguous(),
                  "out_scale must be fp32 [hq]")
     rp = (ctypes.c_uint64 * world)(*recv_ptrs)
-    st = _capi.lib().lkv_cp_combine(send.data_ptr(), rp, rank, world, epoch, rows, head_dim, hq, _ptr(out_scale),
-                                    out.data_ptr(), out.stride(0), _ptr(error_word), _stream())
+    st = _capi.lib().lkv_cp_combine(send.data_ptr(), rp, rank, world, state.data_ptr(), rows, head_dim, hq,
+                                    _ptr(out_scale), out.data_ptr(), out.stride(0), _ptr(error_word), _stream())
     _capi.check(st, "lkv_cp_combine")
     return out
 

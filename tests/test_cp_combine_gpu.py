@@ -33,10 +33,14 @@ def test_single_rank_equals_merge_kernel():
     recv = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
     scale = torch.rand(Hq, device="cuda") + 0.5
     err = torch.zeros(4, dtype=torch.int32, device="cuda")
-    got = ops.cp_combine(send, [recv.data_ptr()], 0, 1, 1, rows, D, Hq, out_scale=scale, error_word=err)
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    got = ops.cp_combine(send, [recv.data_ptr()], 0, 1, state, rows, D, Hq, out_scale=scale, error_word=err)
     ref = ops.merge_partials(o.view(1, B, Hq, D), lse.view(1, B, Hq), out_scale=scale)
     torch.testing.assert_close(got.view(B, Hq, D), ref.view(B, Hq, D), rtol=0, atol=0)
     assert err.cpu().tolist() == [0, 0, 0, 0]
+    assert state.cpu().tolist() == [1, 0]  # epoch advanced once, done counter reset
+    ops.cp_combine(send, [recv.data_ptr()], 0, 1, state, rows, D, Hq, out_scale=scale, error_word=err)
+    assert state.cpu().tolist() == [2, 0]
 
 
 def test_missing_peer_times_out_into_error_word():
@@ -53,7 +57,8 @@ def test_missing_peer_times_out_into_error_word():
     peer = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")  # rank 1 never runs
     err = torch.zeros(4, dtype=torch.int32, device="cuda")
     t0 = time.time()
-    ops.cp_combine(send, [mine.data_ptr(), peer.data_ptr()], 0, 2, 1, rows, D, Hq, error_word=err)
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    ops.cp_combine(send, [mine.data_ptr(), peer.data_ptr()], 0, 2, state, rows, D, Hq, error_word=err)
     torch.cuda.synchronize()
     waited = time.time() - t0
     e = err.cpu().tolist()
