@@ -30,6 +30,8 @@ CASES = [
     (4, 5, 16, 2, 128, [4096, 1, 3000, 64, 65]),
     (5, 2, 12, 12, 64, [640, 513]),
     (6, 64, 32, 8, 128, [513] * 64),
+    (7, 3, 8, 2, 128, [0, 17, 0]),  # rows with no keys: zero output, -inf LSE (padding rows)
+    (8, 2, 4, 4, 64, [0, 0]),
 ]
 
 
