@@ -69,6 +69,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
+    ap.add_argument("--no-e2e8b", action="store_true", help="skip the 8B end-to-end decode measurement (config 3)")
     ap.add_argument("--cp-combine", default="p2p", choices=["p2p", "nccl"],
                     help="cp128k: combine the partials over peer memory (one kernel) or NCCL all-gather + merge")
     ap.add_argument("--cp-eager", action="store_true", help="cp128k: launch per layer instead of a CUDA graph")
@@ -495,6 +496,17 @@ def run_ours(args):
         # the small case (profiler captures) runs the same spans with 2 sequences
         line["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
         line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1)
+    if not args.no_e2e8b:
+        # config 3 on the same ranks: the 8B architecture end to end (weak scaling, batch 8 per GPU)
+        del wl
+        torch.cuda.empty_cache()
+        e = measure_e2e8b(max(E2E8B["decode_tokens"] - 3, 1), 3, world, device)
+        line["e2e8b"] = {"metric": e["metric"], "value": e["value"], "unit": e["unit"], "n_gpus": world,
+                         "batch_per_gpu": E2E8B["batch"], "layers": E2E8B["layers"],
+                         "ms_per_step": e["ms_per_step"], "steps": e["steps"], "e2e": e["e2e"]["value"],
+                         "roofline_frac": e["roofline"]["frac"], "achieved_gbs": e["roofline"]["achieved"],
+                         "prefill_tokens_per_s": e["prefill"]["tokens_per_s"],
+                         "gpu_launches": e["gpu_launches"]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times, threads = cpu_layer_step_sample(args.cpu_seconds, batch=8)
         med = statistics.median(times)
@@ -670,9 +682,7 @@ def run_e2e8b(args):
     import torch
     import torch.distributed as dist
 
-    from lastkv_b200 import _capi, ops
-    from lastkv_b200.hf import LastKVForCausalLM
-    from lastkv_b200.runner import GraphDecodeRunner, init_random_
+    from lastkv_b200 import _capi
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -683,6 +693,29 @@ def run_e2e8b(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     _capi.load()
     _capi.check(_capi.lib().lkv_check_device(local), "lkv_check_device")
+    line = measure_e2e8b(args.steps, args.warmup, world, device)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def measure_e2e8b(steps: int, warmup: int, world: int, device) -> dict:
+    """Config 3 on this rank's GPU (all ranks call it together); returns the bench line."""
+    import torch
+    import torch.distributed as dist
+
+    from lastkv_b200 import ops
+    from lastkv_b200.hf import LastKVForCausalLM
+    from lastkv_b200.runner import GraphDecodeRunner, init_random_
+
+    rank = dist.get_rank() if world > 1 else 0
+
+    class _Args:
+        pass
+
+    args = _Args()
+    args.steps, args.warmup = steps, warmup
     c = E2E8B
     B, P, call, L = c["batch"], c["prompt"], c["prefill_call"], c["layers"]
     Hkv, D = c["kv_heads"], c["head_dim"]
@@ -797,11 +830,9 @@ def run_e2e8b(args):
         "kv_splits": splits,
         "decode_gemm_plans": gemm_plans,
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    del runner
-    if world > 1:
-        dist.destroy_process_group()
+    del runner, cache, model
+    torch.cuda.empty_cache()
+    return line
 
 
 def run_decode_gemm(args):
