@@ -8,8 +8,6 @@ the caller passes ``out``/``workspace`` buffers.
 
 from __future__ import annotations
 
-import math
-
 import torch
 
 from . import _capi
@@ -420,7 +418,3 @@ def cp_combine(send, recv_ptrs, rank: int, world: int, state, rows: int, head_di
                                     _ptr(out_scale), out.data_ptr(), out.stride(0), _ptr(error_word), _stream())
     _capi.check(st, "lkv_cp_combine")
     return out
-
-
-def default_scale(head_dim: int) -> float:
-    return 1.0 / math.sqrt(head_dim)

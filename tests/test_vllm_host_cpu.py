@@ -28,6 +28,19 @@ def _fast(num_slots=3, max_tokens=200, chunk=32, layers=2, order=None):
     return pool, SharedKVFastPath(pool, max_batch=8, max_tokens=256, num_q_heads=8)
 
 
+def test_session_slots_are_reused_and_fail_closed():
+    from lastkv_b200.contract import RMarinBackendContractError
+
+    pool, _ = _fast(num_slots=2)
+    a, b = pool.acquire(), pool.acquire()
+    assert {a, b} == {0, 1}
+    pool.committed[a] = 64
+    with pytest.raises(RMarinBackendContractError, match="no free session slot"):
+        pool.acquire()
+    pool.release(a)
+    assert pool.acquire() == a and pool.committed[a] == 0  # a reused slot starts with nothing committed
+
+
 def test_pool_layout_matches_reference_formulas():
     pool, _ = _fast()
     # batching.py:2005-2013: src pages + scratch, ring stride (2C/16)*slots + 1
