@@ -391,8 +391,8 @@ int decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, void
   p.splits = g.splits;
   p.mode = mode;
   p.err = error_word;
-  return launch_pdl(decode_gemm_kernel, dim3(g.tiles, g.splits), dim3(kThreads), kSmemBytes, stream,
-                    dim3(1, g.splits, 1), tmw, tmx, p) == cudaSuccess
+  return launch_pdl_cluster(decode_gemm_kernel, dim3(g.tiles, g.splits), dim3(kThreads), kSmemBytes, stream,
+                            dim3(1, g.splits, 1), tmw, tmx, p) == cudaSuccess
              ? LKV_OK
              : LKV_ERR_CUDA;
 }
