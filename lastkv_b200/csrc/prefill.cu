@@ -121,6 +121,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int Lq = p.cu_q[b + 1] - q0;
   const int t0 = cta_tile * kTiles * TOK;
   if (t0 >= Lq) return;
+  // A trailing tile with no valid token (the last CTA of a span whose length is
+  // not a multiple of the CTA's tokens) is skipped: no Q load, MMAs or softmax.
+  const int ntiles = (t0 + TOK < Lq) ? kTiles : 1;
   const int n = p.seq_k[b];
   const int t_end = min(t0 + kTiles * TOK, Lq);
   int lim_max = p.causal ? n - Lq + t_end - 1 : n - 1;
@@ -181,9 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(map);
       if (is_k) {
         tma_prefetch_desc(&tmq);
-        mbar_arrive_expect_tx(&bars->q_full, kTiles * Cfg::Q_BYTES);
-#pragma unroll
-        for (int t = 0; t < kTiles; ++t)
+        mbar_arrive_expect_tx(&bars->q_full, ntiles * Cfg::Q_BYTES);
+        for (int t = 0; t < ntiles; ++t)
 #pragma unroll
           for (int h = 0; h < Cfg::HALVES; ++h)
             tma_load_3d(sQ + t * Cfg::Q_BYTES + h * Cfg::Q_HALF, &tmq, &bars->q_full, h * 64, hk * GROUP,
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = mbar_wait(&bars->v_full[(j - 1) % kStagesV], ((j - 1) / kStagesV) & 1);
           if (!ok) break;
         }
-        for (int t = 0; t < kTiles; ++t) {
+        for (int t = 0; t < ntiles; ++t) {
           if (j > 0) {
             ok = mbar_wait(&bars->p_full[t], (j - 1) & 1);
             tc_fence_after();
@@ -269,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->fail = 1;
       }
     }
-  } else {
+  } else if ((warp >> 2) < ntiles) {
     // ------------------------------------------------------------ softmax (rows)
     const int t = warp >> 2;                       // tile
     const int r = (warp & 3) * 32 + lane;          // TMEM lane = row within the tile
