@@ -85,3 +85,26 @@ def test_ops_fail_loudly_without_library(tmp_path, monkeypatch):
     monkeypatch.setattr(_capi, "_lib", None)
     with pytest.raises(RMarinBackendContractError, match="not built"):
         _capi.load(str(tmp_path / "missing.so"))
+
+
+def test_integration_bindings_match_the_abi():
+    """Every lkv_* call in INTEGRATION.md's Python snippets passes as many arguments
+    as the C ABI declares (the snippets are what a maintainer would copy)."""
+    import ast
+    import os
+    import re
+
+    from lastkv_b200 import _capi
+
+    text = open(os.path.join(os.path.dirname(__file__), "..", "INTEGRATION.md")).read()
+    blocks = re.findall(r"```python\n(.*?)```", text, flags=re.S)
+    assert blocks
+    seen = 0
+    for block in blocks:
+        for node in ast.walk(ast.parse(block)):
+            if isinstance(node, ast.Call) and isinstance(node.func, ast.Attribute) and node.func.attr.startswith("lkv_"):
+                name = node.func.attr
+                assert name in _capi._SIGNATURES, name
+                assert len(node.args) == len(_capi._SIGNATURES[name][1]), (name, len(node.args))
+                seen += 1
+    assert seen >= 4
