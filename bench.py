@@ -794,10 +794,10 @@ def measure_e2e8b(steps: int, warmup: int, world: int, device) -> dict:
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
     splits, per_call = ops.decode_plan(B, c["q_heads"], Hkv, D, cache.pages_per_seq + cache.ring_pages,
                                        cache.workspace)
-    # ours per step: block tables + final RMSNorm + per layer (2 RMSNorm, 4 decode GEMMs
-    # [q|k|v, o, gate|up+SiLU, down], append, split-KV decode [+ merge]); the embedding
-    # gather, rotary table, LM head (cuBLAS) and argmax are torch ops
-    launches_per_step = 2 + L * (2 + 4 + 1 + per_call)
+    # ours per step: block tables + final RMSNorm + argmax + per layer (2 RMSNorm, 4 decode
+    # GEMMs [q|k|v, o, gate|up+SiLU, down], append, split-KV decode [+ merge]); the
+    # embedding gather, rotary table and LM head (cuBLAS) are torch ops
+    launches_per_step = 3 + L * (2 + 4 + 1 + per_call)
     H, F_ = c["hidden"], c["ffn"]
     gemm_plans = {name: ops.decode_gemm_plan(n, k, silu) for name, n, k, silu in
                   (("qkv", (c["q_heads"] + 2 * Hkv) * D, H, False), ("o", c["q_heads"] * D, H, False),

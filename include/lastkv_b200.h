@@ -257,6 +257,11 @@ int lkv_rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t resi
 int lkv_silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row,
                  int64_t rows, int ffn, void* stream);
 
+/* Greedy token choice: out[r] = index of the largest bf16 logit of row r, the
+ * first such index on ties and NaN counted as largest (torch.argmax order);
+ * x 16-byte aligned, row_stride (elements) a multiple of 8; one launch. */
+int lkv_argmax_rows(const void* x, int64_t row_stride, int rows, int cols, int64_t* out, void* stream);
+
 /* ------------------------------------------------------------------ decode GEMM
  * y[m, n] = sum_k x[m, k] * w[n, k] for 1 <= m <= 16 activation rows (one decode
  * token per sequence) and a bf16 weight w [n_rows, k] in the nn.Linear layout:

@@ -47,6 +47,7 @@ _SIGNATURES = {
     "lkv_build_layer_block_tables": (I32, [P, I64, P, P, I32, I32, I32, P, P]),
     "lkv_rmsnorm": (I32, [P, I64, P, I64, P, I64, P, P, I64, I32, I32, F32, P]),
     "lkv_silu_mul": (I32, [P, I64, P, I64, I64, I32, P]),
+    "lkv_argmax_rows": (I32, [P, I64, I32, I32, P, P]),
     "lkv_decode_gemm_plan": (I32, [I64, I64, I32, P, P, P]),
     "lkv_cp_combine_sizes": (I32, [I64, I32, I32, P, P]),
     "lkv_cp_combine": (I32, [P, P, I32, I32, P, I64, I32, I32, P, P, I64, P, P]),

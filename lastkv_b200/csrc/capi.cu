@@ -329,6 +329,10 @@ int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, 
                           static_cast<cudaStream_t>(stream), splits);
 }
 
+int lkv_argmax_rows(const void* x, int64_t row_stride, int rows, int cols, int64_t* out, void* stream) {
+  return lkv::argmax_rows(x, row_stride, rows, cols, out, static_cast<cudaStream_t>(stream));
+}
+
 int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_floats, int64_t* recv_words) {
   if (rows < 1 || head_dim < 1 || world < 1 || world > lkv::kCpMaxRanks) return LKV_ERR_INVALID_ARGUMENT;
   if (send_floats) *send_floats = (rows * (head_dim + 1) + 3) / 4 * 4;

@@ -132,6 +132,64 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
   }
 }
 
+// (value, index) order of torch.argmax: NaN above everything, then larger values,
+// and the smaller index between equal values.
+struct ArgMax {
+  float v;
+  int i;
+};
+
+__device__ __forceinline__ bool argmax_before(const ArgMax& a, const ArgMax& b) {
+  const bool an = a.v != a.v, bn = b.v != b.v;
+  if (an != bn) return an;
+  if (!an && a.v != b.v) return a.v > b.v;
+  return a.i < b.i;
+}
+
+constexpr int kArgmaxThreads = 1024;
+
+// One CTA per row: 16-byte loads of 8 bf16 logits, a per-thread running best, a
+// warp-shuffle and shared-memory reduction, one int64 index written per row.
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                     int64_t row_stride, int cols,
+                                                                     int64_t* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const __nv_bfloat16* row = x + (int64_t)blockIdx.x * row_stride;
+  ArgMax best{-INFINITY, 0x7fffffff};
+  const int nvec = cols / 8;
+  for (int c = threadIdx.x; c < nvec; c += kArgmaxThreads) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(row + c * 8), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const ArgMax cand{f[j], c * 8 + j};
+      if (argmax_before(cand, best)) best = cand;
+    }
+  }
+  for (int c = nvec * 8 + threadIdx.x; c < cols; c += kArgmaxThreads) {
+    const ArgMax cand{__bfloat162float(row[c]), c};
+    if (argmax_before(cand, best)) best = cand;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+    if (argmax_before(other, best)) best = other;
+  }
+  __shared__ ArgMax part[kArgmaxThreads / 32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = threadIdx.x < kArgmaxThreads / 32 ? part[threadIdx.x] : ArgMax{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+      if (argmax_before(other, best)) best = other;
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = best.i == 0x7fffffff ? 0 : best.i;
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -175,6 +233,16 @@ int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_ro
   return launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, stream,
                     static_cast<const __nv_bfloat16*>(gate_up), gate_up_row, static_cast<__nv_bfloat16*>(out),
                     out_row, rows, ffn) == cudaSuccess
+             ? LKV_OK
+             : LKV_ERR_CUDA;
+}
+
+int argmax_rows(const void* x, int64_t row_stride, int rows, int cols, int64_t* out, cudaStream_t stream) {
+  if (rows < 0 || cols < 1 || row_stride < cols || (row_stride % 8) || !x || !out || !aligned16(x))
+    return LKV_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return LKV_OK;
+  return launch_pdl(argmax_rows_kernel, dim3(rows), dim3(kArgmaxThreads), 0, stream,
+                    static_cast<const __nv_bfloat16*>(x), row_stride, cols, out) == cudaSuccess
              ? LKV_OK
              : LKV_ERR_CUDA;
 }

@@ -127,6 +127,7 @@ int rmsnorm(const void* x, int64_t x_row, const void* residual, int64_t residual
             cudaStream_t stream);
 int silu_mul(const void* gate_up, int64_t gate_up_row, void* out, int64_t out_row, int64_t rows, int ffn,
              cudaStream_t stream);
+int argmax_rows(const void* x, int64_t row_stride, int rows, int cols, int64_t* out, cudaStream_t stream);
 
 constexpr int kCpMaxRanks = 8;
 constexpr int kCpRowsPerCta = 4;

@@ -333,6 +333,17 @@ def silu_mul(gate_up, *, out=None):
     return out
 
 
+def argmax_rows(logits, *, out=None):
+    """torch.argmax(logits, -1) for bf16 rows (first index on ties, NaN largest), int64 [rows]."""
+    x2 = _rows2d(logits, "logits")
+    if out is None:
+        out = torch.empty(x2.shape[0], dtype=torch.int64, device=logits.device)
+    _require(out.dtype == torch.int64 and out.is_contiguous() and out.numel() == x2.shape[0], "out must be int64 [rows]")
+    st = _capi.lib().lkv_argmax_rows(x2.data_ptr(), x2.stride(0), x2.shape[0], x2.shape[1], out.data_ptr(), _stream())
+    _capi.check(st, "lkv_argmax_rows")
+    return out
+
+
 GEMM_PLAIN, GEMM_SILU_MUL = 0, 1
 DECODE_GEMM_MAX_ROWS = 16
 

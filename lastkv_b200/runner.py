@@ -88,7 +88,10 @@ class GraphDecodeRunner:
         hidden = m.embed_tokens(self.ids)
         pe = m.rotary_emb(hidden, self.pos)
         logits = self.model.lm_head(m.run_layers(hidden, pe, self.cache)[:, -1])
-        self.ids.copy_(logits.float().argmax(-1, keepdim=True))
+        if logits.dtype == torch.bfloat16 and logits.shape[-1] % 8 == 0:
+            ops.argmax_rows(logits, out=self.ids.view(-1))  # torch.argmax order, one launch
+        else:
+            self.ids.copy_(logits.float().argmax(-1, keepdim=True))
 
     def capture(self):
         """Capture one decode step at the current position (the warm-up runs do not advance)."""

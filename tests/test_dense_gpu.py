@@ -81,3 +81,20 @@ def test_dense_rejects_bad_shapes():
         ops.rmsnorm(x, torch.ones(12, device="cuda", dtype=torch.bfloat16), 1e-6)
     with pytest.raises(RMarinBackendContractError):
         ops.silu_mul(torch.zeros((4, 12), device="cuda", dtype=torch.bfloat16))
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 128256), (3, 1000), (1, 8), (5, 77)])
+def test_argmax_rows_matches_torch(rows, cols):
+    from lastkv_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(rows * cols)
+    pad = -(-cols // 8) * 8
+    buf = torch.randn((rows, pad), generator=g, device="cuda").bfloat16()
+    x = buf[:, :cols]  # row stride a multiple of 8, any column count
+    x[0, cols // 3] = x[0].max() + 1  # a clear winner
+    if rows > 1:
+        x[1, :] = 0.5                  # all tied: the first index
+    if rows > 2:
+        x[2, cols // 2] = float("nan")  # NaN counts as the largest (torch.argmax)
+    got = ops.argmax_rows(x)
+    torch.testing.assert_close(got, x.argmax(-1), rtol=0, atol=0)
