@@ -182,6 +182,37 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max.f32).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two 2^x on the FMA pipe (f32x2), for softmax exponentials moved off the SFU.
+// Range reduction x = j + f with j = round(x), f in [-0.5, 0.5]: adding
+// 1.5 * 2^23 rounds x to an integer held in the low mantissa bits of t; then
+// 2^f by a degree-3 polynomial and j added into the exponent field.  The
+// coefficients are a minimax fit of the relative error of 2^f on [-0.5, 0.5]
+// (Remez exchange, exp2_poly_fit.py beside this file): max relative error
+// 7.5e-5, far below the bf16 rounding (2^-9) applied to softmax weights.
+// Inputs are clamped at -125 (2^-125 instead of the SFU's flush to zero; a
+// masked -inf therefore yields 2^-125, a weight 1e-38 below any visible key's).
+constexpr float kExp2C0 = 0.99992806f, kExp2C1 = 0.69326097f, kExp2C2 = 0.24261113f, kExp2C3 = 0.05517167f;
+
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(make_float2(-1.f, -1.f), j, x);
+  float2 p = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+  p = __ffma2_rn(p, f, make_float2(kExp2C1, kExp2C1));
+  p = __ffma2_rn(p, f, make_float2(kExp2C0, kExp2C0));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -16,12 +16,15 @@
 // tile B holds the TOK tokens after tile A.  Every K/V block brought on chip
 // serves 256 rows (the whole GQA group of 2 TOK tokens).
 //
-// Warp roles (352 threads):
+// Warp roles (384 threads; warp w runs on SM sub-partition w % 4):
 //   warps 0-3  softmax + epilogue of tile A, one thread per row (TMEM lane)
 //   warps 4-7  softmax + epilogue of tile B
 //   warp 8     TMA producer: Q tiles once, then K blocks (128 keys = 8 pages)
 //   warp 9     TMA producer: V blocks
-//   warp 10    TMEM allocator and the single MMA-issuing thread
+//   warp 10    idle (keeps the MMA warp off the producers' sub-partitions)
+//   warp 11    TMEM allocator and MMA issuer: the whole warp runs the issue
+//              loop (warp-uniform descriptors, no per-MMA rebuild) and one
+//              elected lane issues every tcgen05.mma / commit
 // TMEM columns: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [256+D, 256+2D).
 // Per key block j the MMA thread issues, in order,
 //   PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
@@ -30,10 +33,12 @@
 // works on the other tile.  P (bf16, two per column) overwrites the first 64
 // columns of its own tile's S; the next S of that tile is issued after the PV
 // that reads P, and tcgen05.mma from one thread executes in issue order.
-// K and V stream through separate rings (3 and 2 stages).  The running max is
+// K and V stream through separate rings (2 and 3 stages).  The running max is
 // only raised (and O rescaled in TMEM) when a row's max grows by more than
 // 2^8; otherwise exp2 is taken against the stale max, which stays exact
-// because the final normalisation uses the same reference.
+// because the final normalisation uses the same reference.  The softmax takes
+// a quarter of its exponentials on the FMA pipe (ex2_poly2) and the rest on the
+// SFU, and stores P in 32-key chunks as they are ready.
 
 #include <math.h>
 
@@ -52,9 +57,9 @@ constexpr int kTiles = 2;  // query tiles per CTA
 constexpr int kBN = 128;  // keys per block
 constexpr int kPageTok = 16;
 constexpr int kPagesPerBlock = kBN / kPageTok;
-constexpr int kWarpK = 8, kWarpV = 9, kWarpMma = 10;
-constexpr int kThreads = 11 * 32;
-constexpr int kStagesK = 3, kStagesV = 2;
+constexpr int kWarpK = 8, kWarpV = 9, kWarpMma = 11;
+constexpr int kThreads = 12 * 32;
+constexpr int kStagesK = 2, kStagesV = 3;
 constexpr float kRescaleLog2 = 8.0f;
 
 struct PrefillParams {
@@ -218,58 +223,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t kb = k_base + (j % kStagesK) * Cfg::KV_BYTES;
-        const uint32_t qb = q_base + t * Cfg::Q_BYTES;
+    const bool leader = elect_one();
+    // Descriptors of each operand's first 16-element K slice; the slices and
+    // ring stages are constant offsets (16-byte units) from them.
+    const uint64_t qd = umma_sdesc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t kd = umma_sdesc_sw128(smem_u32(sK), 16, 1024);
+    const uint64_t vd = umma_sdesc_sw128(smem_u32(sV), Cfg::KV_HALF, 1024);
+    auto issue_s = [&](int t, int j) {
+      const uint64_t kb = kd + (uint64_t)(((j % kStagesK) * Cfg::KV_BYTES) >> 4);
+      const uint64_t qb = qd + (uint64_t)((t * Cfg::Q_BYTES) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint64_t a = umma_sdesc_sw128(qb + (ks >> 2) * Cfg::Q_HALF + (ks & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_sdesc_sw128(kb + (ks >> 2) * Cfg::KV_HALF + (ks & 3) * 32, 16, 1024);
-          umma_bf16_ss(tmem + Cfg::COL_S + t * kBN, a, bd, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
-        }
-        umma_commit(&bars->s_full[t]);
-      };
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t vb = v_base + (j % kStagesV) * Cfg::KV_BYTES;
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint32_t oq = ((ks >> 2) * Cfg::Q_HALF + (ks & 3) * 32) >> 4;
+        const uint32_t okv = ((ks >> 2) * Cfg::KV_HALF + (ks & 3) * 32) >> 4;
+        if (leader) umma_bf16_ss(tmem + Cfg::COL_S + t * kBN, qb + oq, kb + okv, Cfg::IDESC_S, ks > 0 ? 1u : 0u);
+      }
+      if (leader) umma_commit(&bars->s_full[t]);
+    };
+    auto issue_pv = [&](int t, int j) {
+      const uint64_t vb = vd + (uint64_t)(((j % kStagesV) * Cfg::KV_BYTES) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint64_t bd = umma_sdesc_sw128(vb + ks * (kPageTok * 128), Cfg::KV_HALF, 1024);
-          umma_bf16_ts(tmem + Cfg::COL_O + t * D, tmem + Cfg::COL_S + t * kBN + ks * 8, bd, Cfg::IDESC_PV,
-                       (j > 0 || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(&bars->pv_done[t]);
-      };
-      bool ok = mbar_wait(&bars->q_full, 0);
-      for (int j = 0; ok && j <= nb; ++j) {
-        // PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
-        if (j < nb) {
-          ok = mbar_wait(&bars->k_full[j % kStagesK], (j / kStagesK) & 1);
+      for (int ks = 0; ks < kBN / 16; ++ks)
+        if (leader)
+          umma_bf16_ts(tmem + Cfg::COL_O + t * D, tmem + Cfg::COL_S + t * kBN + ks * 8,
+                       vb + (uint64_t)((ks * (kPageTok * 128)) >> 4), Cfg::IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+      if (leader) umma_commit(&bars->pv_done[t]);
+    };
+    // Wait results are made warp-uniform so the whole warp leaves together.
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full, 0));
+    for (int j = 0; ok && j <= nb; ++j) {
+      // PV_A(j-1), S_A(j), PV_B(j-1), S_B(j)
+      if (j < nb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->k_full[j % kStagesK], (j / kStagesK) & 1));
+        tc_fence_after();
+        if (!ok) break;
+      }
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->v_full[(j - 1) % kStagesV], ((j - 1) / kStagesV) & 1));
+        if (!ok) break;
+      }
+      for (int t = 0; t < ntiles; ++t) {
+        if (j > 0) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_full[t], (j - 1) & 1));
           tc_fence_after();
           if (!ok) break;
+          issue_pv(t, j - 1);
         }
-        if (j > 0) {
-          ok = mbar_wait(&bars->v_full[(j - 1) % kStagesV], ((j - 1) / kStagesV) & 1);
-          if (!ok) break;
-        }
-        for (int t = 0; t < ntiles; ++t) {
-          if (j > 0) {
-            ok = mbar_wait(&bars->p_full[t], (j - 1) & 1);
-            tc_fence_after();
-            if (!ok) break;
-            issue_pv(t, j - 1);
-          }
-          if (j < nb) issue_s(t, j);
-        }
-        if (!ok) break;
+        if (j < nb) issue_s(t, j);
+      }
+      if (!ok) break;
+      if (leader) {
         if (j < nb) umma_commit(&bars->k_empty[j % kStagesK]);
         if (j > 0) umma_commit(&bars->v_empty[(j - 1) % kStagesV]);
       }
-      if (!ok) {
-        report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 100);
-        bars->fail = 1;
-      }
+    }
+    if (!ok && leader) {
+      report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 100);
+      bars->fail = 1;
     }
   } else if ((warp >> 2) < ntiles) {
     // ------------------------------------------------------------ softmax (rows)
@@ -306,14 +316,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < kBN; ++e)
           if (key0 + e > lim) x[e] = -INFINITY;
       }
-      // 8 independent partial maxima (short dependency chains), then a tree
+      // 8 independent partial maxima (short dependency chains, three-input max), then a tree
       float mp[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mp[u] = x[u];
+      for (int u = 0; u < 8; ++u) mp[u] = fmaxf(x[u], x[kBN - 8 + u]);
 #pragma unroll
-      for (int e = 8; e < kBN; e += 8)
+      for (int e = 8; e + 16 <= kBN - 8; e += 16)
 #pragma unroll
-        for (int u = 0; u < 8; ++u) mp[u] = fmaxf(mp[u], x[e + u]);
+        for (int u = 0; u < 8; ++u) mp[u] = fmax3f(mp[u], x[e + u], x[e + 8 + u]);
       float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       mx *= sl2;  // scale > 0, so max commutes with it
       float alpha = 1.f;
@@ -324,14 +334,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float neg_mref = (m == -INFINITY) ? 0.f : -m;
       const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(neg_mref, neg_mref);
       float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      uint32_t pk[kBN / 2];
+      // P(j) (bf16 pairs) over the first 64 columns of this tile's S, which is fully
+      // read: 16 columns per 32 keys, stored as each chunk is ready.  f32x2 FFMA /
+      // FADD halve the issue slots of the scale-and-subtract and the sums; pairs 0
+      // and 1 of every 8 take their exponentials on the FMA pipe, the rest on the SFU.
 #pragma unroll
-      for (int e = 0; e < kBN; e += 2) {
-        // f32x2 FFMA / FADD halve the issue slots of the scale-and-subtract and the sums
-        const float2 a = __ffma2_rn(make_float2(x[e], x[e + 1]), sl2v, negm);
-        const float2 pv = make_float2(ex2_approx(a.x), ex2_approx(a.y));
-        sp[(e >> 1) & 3] = __fadd2_rn(sp[(e >> 1) & 3], pv);
-        pk[e / 2] = pack_bf16(pv.x, pv.y);
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t pc[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int e = c * 32 + 2 * q;
+          const float2 a = __ffma2_rn(make_float2(x[e], x[e + 1]), sl2v, negm);
+          const float2 pv = (q & 7) < 2 ? ex2_poly2(a) : make_float2(ex2_approx(a.x), ex2_approx(a.y));
+          sp[q & 3] = __fadd2_rn(sp[q & 3], pv);
+          pc[q] = pack_bf16(pv.x, pv.y);
+        }
+        tmem_st16(lane_base + col_s + c * 16, pc);
       }
       const float sum = ((sp[0].x + sp[0].y) + (sp[1].x + sp[1].y)) + ((sp[2].x + sp[2].y) + (sp[3].x + sp[3].y));
       l = l * alpha + sum;
@@ -349,17 +367,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * alpha);
           tmem_st32(lane_base + col_o + c * 32, raw);
         }
-      }
-      // P(j) (bf16 pairs) over the first 64 columns of this tile's S, which is fully read.
-      {
-        uint32_t lo[32], hi[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          lo[e] = pk[e];
-          hi[e] = pk[32 + e];
-        }
-        tmem_st32(lane_base + col_s, lo);
-        tmem_st32(lane_base + col_s + 32, hi);
       }
       tmem_wait_st();
       tc_fence_before();
