@@ -406,7 +406,9 @@ def run_ours(args):
 
     uuid = str(torch.cuda.get_device_properties(device).uuid)
     clocks = ClockSampler(uuid)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps * L)]
+    # The layer calls go back to back (no events between them, which would cut the
+    # programmatic-dependent-launch overlap of consecutive kernels, as a real decode
+    # step has none); the average launch time is the timed region over the calls.
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks.start()
     barrier()
@@ -414,16 +416,13 @@ def run_ours(args):
     t0.record(stream)
     for s in range(args.steps):
         for l in range(L):
-            a, b = ev[s * L + l]
-            a.record(stream)
             layer(l)
-            b.record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
     total_ms = t0.elapsed_time(t1)
-    op_ms = [a.elapsed_time(b) for a, b in ev]
+    op_ms = [total_ms / (args.steps * L)]
     err = wl["ws"].error()
     if err[0] != 0:
         raise RuntimeError(f"device error word set: {err}")

@@ -1,18 +1,22 @@
 // Split-KV decode over the shared last-layer paged K/V pool (sm_100a).
 //
-// One CTA = (sequence b, KV head hk, split).  A producer warp streams the
-// split's pages with TMA (4-D tensor map over [pages, 16, Hkv, D], one
-// 16 x 64 half-tile per copy, 128-byte swizzle) into a STAGES-deep ring of
-// shared-memory stages holding NW pages each; NW consumer warps each take one
-// page of a stage.  All query heads of the GQA group are folded into one MMA
+// Work item = (sequence b, KV head hk, split).  The grid is persistent: as
+// many CTAs as fit on the GPU at once, CTA c taking items c, c + grid, ...
+// A producer warp streams the pages of all its items back to back with TMA
+// (4-D tensor map over [pages, 16, Hkv, D], one 16 x 64 half-tile per copy,
+// 128-byte swizzle) into a STAGES-deep ring of shared-memory stages holding NW
+// pages of one item each; NW consumer warps each take one page of a stage.  The
+// ring therefore fills once per CTA, and each item's epilogue (cross-warp
+// merge, output write) overlaps the loads of the next item.  All query heads of the GQA group are folded into one MMA
 // tile with the keys as the M dimension:
 //     S^T[16 keys, 8 heads] = K[16, D] * Q^T[D, 8]           (mma m16n8k16)
 //     O^T[D, 8 heads]      += V^T[D, 16] * P^T[16 keys, 8]    (mma m16n8k16)
 // P^T is produced from the S^T accumulators with movmatrix (8x8 transposes),
 // so probabilities never leave registers.  The online softmax keeps a running
 // max per head (4-lane groups share a head pair) and per-thread partial sums.
-// At the end the NW warps merge in shared memory and the CTA writes either the
-// final bf16 output (single split) or a normalised fp32 partial + log2 LSE.
+// At the end of an item the NW warps merge in a shared-memory area of their
+// own (four heads at a time) and the CTA writes either the final bf16 output
+// (single split) or a normalised fp32 partial + log2 LSE.
 // A second small kernel merges the splits (and serves as the context-parallel
 // combine).
 //
@@ -61,10 +65,10 @@ struct DecodeCfg {
   static constexpr int PAGE_BYTES = 2 * HALVES * TILE_BYTES;  // K and V of one page, one head
   static constexpr int STAGE_BYTES = NW * PAGE_BYTES;
   static constexpr int OSTRIDE = D + 4;                       // padded fp32 row of the merge area
-  static constexpr int MERGE_BYTES = NW * 8 * (OSTRIDE + 2) * 4;
   static constexpr int DATA_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + 2 * STAGES * 8 + 16;  // + failure flag
-  static_assert(MERGE_BYTES <= DATA_BYTES, "merge area must fit in the stage ring");
+  // merge area after the ring: o [NW][4 heads][OSTRIDE], then m and l [NW][8]
+  static constexpr int MERGE_BYTES = NW * 4 * OSTRIDE * 4 + 2 * NW * 8 * 4;
+  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + MERGE_BYTES + 2 * STAGES * 8 + 16;  // + failure flag
 };
 
 __device__ __forceinline__ float warp_max_g(float v) {
@@ -90,59 +94,83 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   constexpr int KT = D / 16;  // 16-wide d tiles
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::DATA_BYTES);
+  float* mo = reinterpret_cast<float*>(smem + Cfg::DATA_BYTES);  // [NW][4][OSTRIDE]
+  float* mm = mo + NW * 4 * Cfg::OSTRIDE;                         // [NW][8]
+  float* ml = mm + NW * 8;                                        // [NW][8]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::DATA_BYTES + Cfg::MERGE_BYTES);
   uint64_t* empty = full + STAGES;
+  volatile int* fail_flag = reinterpret_cast<volatile int*>(empty + STAGES);
 
-  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
   pdl_wait();  // q, the appended keys and the tables come from the previous kernels
-
-  const int n = max(0, p.seq_k[b]);
-  const int npages = min((n + PAGE - 1) / PAGE, p.W);
-  const int per = (npages + p.S - 1) / p.S;
-  const int p0 = min(npages, split * per);
-  const int p1 = min(npages, p0 + per);
-  const int n_iter = (p1 - p0 + NW - 1) / NW;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NW);
     }
-    *reinterpret_cast<int*>(empty + STAGES) = 0;  // CTA failure flag
+    *fail_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
+  // item i -> (split, hk, b) = (i % S, i / S % Hkv, i / (S * Hkv)); its pages [p0, p1)
+  const int n_items = p.S * p.Hkv * p.B;
+  struct Item {
+    int b, hk, split, n, p0, p1, n_iter;
+  };
+  auto item_at = [&](int i) {
+    Item it;
+    it.split = i % p.S;
+    it.hk = (i / p.S) % p.Hkv;
+    it.b = i / (p.S * p.Hkv);
+    it.n = max(0, p.seq_k[it.b]);
+    const int npages = min((it.n + PAGE - 1) / PAGE, p.W);
+    const int per = (npages + p.S - 1) / p.S;
+    it.p0 = min(npages, it.split * per);
+    it.p1 = min(npages, it.p0 + per);
+    it.n_iter = (it.p1 - it.p0 + NW - 1) / NW;
+    return it;
+  };
+
   if (warp == NW) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && n_iter > 0) {
+    // Stages are numbered across items (gs), so the ring never drains between
+    // items.  On a failed wait it stops; the consumers' own bounded waits then
+    // end their loops.
+    if (lane == 0) {
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
       const uint64_t policy = policy_evict_first();
-      const int32_t* row = p.bt + (int64_t)b * p.bt_stride;
-      for (int it = 0; it < n_iter; ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u)) {
-          report_error(p.err, DEVERR_WAIT_TIMEOUT, 1, it);
-          break;
-        }
-        const int first = p0 + it * NW;
-        const int cnt = min(NW, p1 - first);
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * Cfg::PAGE_BYTES));
-        uint8_t* dst = smem + s * Cfg::STAGE_BYTES;
-        for (int w = 0; w < cnt; ++w) {
-          const int pid = row[first + w];
-          if (pid < 0 || (int64_t)pid >= p.num_pages) report_error(p.err, DEVERR_BAD_PAGE, 1, pid);
-          // An out-of-range page reads as zeros (TMA bounds-fills), never faults.
+      uint32_t gs = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < n_items; i += gridDim.x) {
+        const Item w = item_at(i);
+        const int32_t* row = p.bt + (int64_t)w.b * p.bt_stride;
+        for (int it = 0; it < w.n_iter; ++it, ++gs) {
+          const int s = (int)(gs % STAGES);
+          const uint32_t ph = (gs / STAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u)) {
+            report_error(p.err, DEVERR_WAIT_TIMEOUT, 1, it);
+            ok = false;
+            break;
+          }
+          const int first = w.p0 + it * NW;
+          const int cnt = min(NW, w.p1 - first);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * Cfg::PAGE_BYTES));
+          uint8_t* dst = smem + s * Cfg::STAGE_BYTES;
+          for (int k = 0; k < cnt; ++k) {
+            const int pid = row[first + k];
+            if (pid < 0 || (int64_t)pid >= p.num_pages) report_error(p.err, DEVERR_BAD_PAGE, 1, pid);
+            // An out-of-range page reads as zeros (TMA bounds-fills), never faults.
 #pragma unroll
-          for (int h = 0; h < Cfg::HALVES; ++h) {
-            tma_load_4d_hint(dst + w * Cfg::PAGE_BYTES + h * Cfg::TILE_BYTES, &tmk, &full[s], h * 64, hk, 0, pid,
-                             policy);
-            tma_load_4d_hint(dst + w * Cfg::PAGE_BYTES + (Cfg::HALVES + h) * Cfg::TILE_BYTES, &tmv, &full[s],
-                             h * 64, hk, 0, pid, policy);
+            for (int h = 0; h < Cfg::HALVES; ++h) {
+              tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + h * Cfg::TILE_BYTES, &tmk, &full[s], h * 64, w.hk, 0, pid,
+                               policy);
+              tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + (Cfg::HALVES + h) * Cfg::TILE_BYTES, &tmv, &full[s],
+                               h * 64, w.hk, 0, pid, policy);
+            }
           }
         }
       }
@@ -152,149 +180,161 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 
   // -------------------------------------------------------------- consumers
   const int g = lane >> 2, c = lane & 3;
-  uint32_t qf[KT][2];
-  {
-    const bool valid = g < GROUP;
-    const __nv_bfloat16* qrow = p.q + (int64_t)b * p.q_stride_tok + (int64_t)(hk * GROUP + (valid ? g : 0)) * D;
-#pragma unroll
-    for (int j = 0; j < KT; ++j) {
-      const int d0 = 16 * j + 2 * c;
-      qf[j][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
-      qf[j][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
-    }
-  }
-  float o[KT][4];
-#pragma unroll
-  for (int i = 0; i < KT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
   // ldmatrix source rows/chunks (see the fragment derivation in the header comment)
   const uint32_t k_row = (lane & 7) + ((lane >> 3) & 1) * 8, k_chunk_hi = lane >> 4;
   const uint32_t v_row = (lane & 7) + (lane >> 4) * 8, v_chunk_hi = (lane >> 3) & 1;
-
+  uint32_t gs = 0;
   bool failed = false;
-  for (int it = 0; it < n_iter; ++it) {
-    const int s = it % STAGES;
-    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-    if (!mbar_wait(&full[s], ph)) {
-      report_error(p.err, DEVERR_WAIT_TIMEOUT, 1, 1000000 + it);
-      failed = true;
-      break;
-    }
-    const int page_idx = p0 + it * NW + warp;
-    if (page_idx < p1) {
-      uint8_t* kt = smem + s * Cfg::STAGE_BYTES + warp * Cfg::PAGE_BYTES;
-      uint8_t* vt = kt + Cfg::HALVES * Cfg::TILE_BYTES;
-      const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+
+  for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+    const Item w = item_at(i);
+    const int b = w.b, hk = w.hk, n = w.n;
+    uint32_t qf[KT][2];
+    {
+      const bool valid = g < GROUP;
+      const __nv_bfloat16* qrow =
+          p.q + (int64_t)b * p.q_stride_tok + (int64_t)(hk * GROUP + (valid ? g : 0)) * D;
 #pragma unroll
       for (int j = 0; j < KT; ++j) {
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4(a0, a1, a2, a3,
-                    kbase + (j >> 2) * Cfg::TILE_BYTES + swz128(k_row, 2 * (j & 3) + k_chunk_hi));
-        mma_bf16_16816(sc, a0, a1, a2, a3, qf[j][0], qf[j][1]);
-      }
-      const int key0 = page_idx * PAGE;
-      const int valid_rows = n - key0;  // >= 1
-      const bool r0 = g < valid_rows, r1 = g + 8 < valid_rows;
-      const float s00 = r0 ? sc[0] * p.scale_log2 : -INFINITY;
-      const float s01 = r0 ? sc[1] * p.scale_log2 : -INFINITY;
-      const float s10 = r1 ? sc[2] * p.scale_log2 : -INFINITY;
-      const float s11 = r1 ? sc[3] * p.scale_log2 : -INFINITY;
-      const float mn0 = fmaxf(m0, warp_max_g(fmaxf(s00, s10)));
-      const float mn1 = fmaxf(m1, warp_max_g(fmaxf(s01, s11)));
-      const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-      m0 = mn0;
-      m1 = mn1;
-      const float p00 = exp2f(s00 - mn0), p01 = exp2f(s01 - mn1);
-      const float p10 = exp2f(s10 - mn0), p11 = exp2f(s11 - mn1);
-      l0 = l0 * al0 + p00 + p10;
-      l1 = l1 * al1 + p01 + p11;
-#pragma unroll
-      for (int i = 0; i < KT; ++i) {
-        o[i][0] *= al0;
-        o[i][1] *= al1;
-        o[i][2] *= al0;
-        o[i][3] *= al1;
-      }
-      const uint32_t pb0 = movmatrix_trans(pack_bf16(p00, p01));
-      const uint32_t pb1 = movmatrix_trans(pack_bf16(p10, p11));
-      if (valid_rows < PAGE) {
-        // Rows past the sequence end carry P = 0, but 0 * NaN would still poison
-        // O; clear them (a swizzled row stays inside its own 128 bytes).
-        const int nz = (PAGE - valid_rows) * 8 * Cfg::HALVES;
-        for (int e = lane; e < nz; e += 32) {
-          const int hv = e / ((PAGE - valid_rows) * 8);
-          const int rem = e % ((PAGE - valid_rows) * 8);
-          const int r = valid_rows + rem / 8;
-          *reinterpret_cast<uint4*>(vt + hv * Cfg::TILE_BYTES + r * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
-        }
-        __syncwarp();
-      }
-#pragma unroll
-      for (int i = 0; i < KT; ++i) {
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4_trans(a0, a1, a2, a3,
-                          vbase + (i >> 2) * Cfg::TILE_BYTES + swz128(v_row, 2 * (i & 3) + v_chunk_hi));
-        mma_bf16_16816(o[i], a0, a1, a2, a3, pb0, pb1);
+        const int d0 = 16 * j + 2 * c;
+        qf[j][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0) : 0u;
+        qf[j][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + d0 + 8) : 0u;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
+    float o[KT][4];
+#pragma unroll
+    for (int k = 0; k < KT; ++k) o[k][0] = o[k][1] = o[k][2] = o[k][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-  // ---------------------------------------------------------------- merge
-  l0 = warp_sum_g(l0);
-  l1 = warp_sum_g(l1);
-  volatile int* fail_flag = reinterpret_cast<volatile int*>(empty + STAGES);
-  if (failed && lane == 0) *fail_flag = 1;
-  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));  // all consumer warps are done with the stages
-  if (*fail_flag) return;                          // uniform across the consumer warps
-  float* mo = reinterpret_cast<float*>(smem);                       // [NW][8][OSTRIDE]
-  float* mm = mo + NW * 8 * Cfg::OSTRIDE;                           // [NW][8]
-  float* ml = mm + NW * 8;                                          // [NW][8]
-  {
-    float* w0 = mo + (warp * 8 + 2 * c) * Cfg::OSTRIDE;
-    float* w1 = w0 + Cfg::OSTRIDE;
+    for (int it = 0; it < w.n_iter; ++it, ++gs) {
+      const int s = (int)(gs % STAGES);
+      const uint32_t ph = (gs / STAGES) & 1u;
+      if (!mbar_wait(&full[s], ph)) {
+        report_error(p.err, DEVERR_WAIT_TIMEOUT, 1, 1000000 + it);
+        failed = true;
+        break;
+      }
+      const int page_idx = w.p0 + it * NW + warp;
+      if (page_idx < w.p1) {
+        uint8_t* kt = smem + s * Cfg::STAGE_BYTES + warp * Cfg::PAGE_BYTES;
+        uint8_t* vt = kt + Cfg::HALVES * Cfg::TILE_BYTES;
+        const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < KT; ++i) {
-      w0[16 * i + g] = o[i][0];
-      w1[16 * i + g] = o[i][1];
-      w0[16 * i + g + 8] = o[i][2];
-      w1[16 * i + g + 8] = o[i][3];
+        for (int j = 0; j < KT; ++j) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(a0, a1, a2, a3,
+                      kbase + (j >> 2) * Cfg::TILE_BYTES + swz128(k_row, 2 * (j & 3) + k_chunk_hi));
+          mma_bf16_16816(sc, a0, a1, a2, a3, qf[j][0], qf[j][1]);
+        }
+        const int key0 = page_idx * PAGE;
+        const int valid_rows = n - key0;  // >= 1
+        const bool r0 = g < valid_rows, r1 = g + 8 < valid_rows;
+        const float s00 = r0 ? sc[0] * p.scale_log2 : -INFINITY;
+        const float s01 = r0 ? sc[1] * p.scale_log2 : -INFINITY;
+        const float s10 = r1 ? sc[2] * p.scale_log2 : -INFINITY;
+        const float s11 = r1 ? sc[3] * p.scale_log2 : -INFINITY;
+        const float mn0 = fmaxf(m0, warp_max_g(fmaxf(s00, s10)));
+        const float mn1 = fmaxf(m1, warp_max_g(fmaxf(s01, s11)));
+        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        const float p00 = exp2f(s00 - mn0), p01 = exp2f(s01 - mn1);
+        const float p10 = exp2f(s10 - mn0), p11 = exp2f(s11 - mn1);
+        l0 = l0 * al0 + p00 + p10;
+        l1 = l1 * al1 + p01 + p11;
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+          o[k][0] *= al0;
+          o[k][1] *= al1;
+          o[k][2] *= al0;
+          o[k][3] *= al1;
+        }
+        const uint32_t pb0 = movmatrix_trans(pack_bf16(p00, p01));
+        const uint32_t pb1 = movmatrix_trans(pack_bf16(p10, p11));
+        if (valid_rows < PAGE) {
+          // Rows past the sequence end carry P = 0, but 0 * NaN would still poison
+          // O; clear them (a swizzled row stays inside its own 128 bytes).
+          const int nz = (PAGE - valid_rows) * 8 * Cfg::HALVES;
+          for (int e = lane; e < nz; e += 32) {
+            const int hv = e / ((PAGE - valid_rows) * 8);
+            const int rem = e % ((PAGE - valid_rows) * 8);
+            const int r = valid_rows + rem / 8;
+            *reinterpret_cast<uint4*>(vt + hv * Cfg::TILE_BYTES + r * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+          }
+          __syncwarp();
+        }
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(a0, a1, a2, a3,
+                            vbase + (k >> 2) * Cfg::TILE_BYTES + swz128(v_row, 2 * (k & 3) + v_chunk_hi));
+          mma_bf16_16816(o[k], a0, a1, a2, a3, pb0, pb1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
+
+    // ------------------------------------------------------------ item merge
+    // Only consumer warps write the failure flag, and only before this barrier;
+    // every consumer warp reads it after the barrier, so they leave together.
+    l0 = warp_sum_g(l0);
+    l1 = warp_sum_g(l1);
+    if (failed && lane == 0) *fail_flag = 1;
     if (g == 0) {
       mm[warp * 8 + 2 * c] = m0;
       mm[warp * 8 + 2 * c + 1] = m1;
       ml[warp * 8 + 2 * c] = l0;
       ml[warp * 8 + 2 * c + 1] = l1;
     }
-  }
-  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
-  for (int idx = threadIdx.x; idx < GROUP * D; idx += NW * 32) {
-    const int h = idx / D, d = idx % D;
-    float M = -INFINITY;
+    // Heads go through the o area four at a time: thread (g, c) holds heads 2c
+    // and 2c + 1, so chunk hc is held by the threads with c >> 1 == hc.
 #pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, mm[w * 8 + h]);
-    float L = 0.f, acc = 0.f;
-    if (M != -INFINITY) {
+    for (int hc = 0; hc < (GROUP + 3) / 4; ++hc) {
+      if ((c >> 1) == hc) {
+        float* w0 = mo + (warp * 4 + 2 * c - 4 * hc) * Cfg::OSTRIDE;
+        float* w1 = w0 + Cfg::OSTRIDE;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float f = exp2f(mm[w * 8 + h] - M);
-        L += ml[w * 8 + h] * f;
-        acc += mo[(w * 8 + h) * Cfg::OSTRIDE + d] * f;
+        for (int k = 0; k < KT; ++k) {
+          w0[16 * k + g] = o[k][0];
+          w1[16 * k + g] = o[k][1];
+          w0[16 * k + g + 8] = o[k][2];
+          w1[16 * k + g + 8] = o[k][3];
+        }
       }
-    }
-    const float val = L > 0.f ? acc / L : 0.f;
-    const int hq = hk * GROUP + h;
-    if (p.final_out) {
-      const float sc = p.out_scale ? p.out_scale[hq] : 1.f;
-      p.out[(int64_t)b * p.out_stride_tok + (int64_t)hq * D + d] = __float2bfloat16_rn(val * sc);
-      if (p.lse && d == 0) p.lse[(int64_t)b * p.Hq + hq] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
-    } else {
-      const int64_t rowi = ((int64_t)b * p.Hq + hq) * p.S + split;
-      p.part_o[rowi * D + d] = val;
-      if (d == 0) p.part_lse[rowi] = L > 0.f ? M + log2f(L) : -INFINITY;
+      asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+      if (*fail_flag) return;  // uniform across the consumer warps
+      constexpr int HC = GROUP < 4 ? GROUP : 4;
+      for (int idx = threadIdx.x; idx < HC * D; idx += NW * 32) {
+        const int hl = idx / D, d = idx % D, h = 4 * hc + hl;
+        float M = -INFINITY;
+#pragma unroll
+        for (int v = 0; v < NW; ++v) M = fmaxf(M, mm[v * 8 + h]);
+        float L = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+          for (int v = 0; v < NW; ++v) {
+            const float f = exp2f(mm[v * 8 + h] - M);
+            L += ml[v * 8 + h] * f;
+            acc += mo[(v * 4 + hl) * Cfg::OSTRIDE + d] * f;
+          }
+        }
+        const float val = L > 0.f ? acc / L : 0.f;
+        const int hq = hk * GROUP + h;
+        if (p.final_out) {
+          const float sc = p.out_scale ? p.out_scale[hq] : 1.f;
+          p.out[(int64_t)b * p.out_stride_tok + (int64_t)hq * D + d] = __float2bfloat16_rn(val * sc);
+          if (p.lse && d == 0)
+            p.lse[(int64_t)b * p.Hq + hq] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : -INFINITY;
+        } else {
+          const int64_t rowi = ((int64_t)b * p.Hq + hq) * p.S + w.split;
+          p.part_o[rowi * D + d] = val;
+          if (d == 0) p.part_lse[rowi] = L > 0.f ? M + log2f(L) : -INFINITY;
+        }
+      }
+      // the area (and mm / ml) is rewritten by the next chunk or item
+      asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
     }
   }
 }
@@ -413,19 +453,21 @@ int prepare_kernel(int dev) {
   return info.occ[di][gi];
 }
 
-// Split count: minimise (waves) x (pages per CTA + pipeline fill), the time of
-// a grid of equal CTAs, so the last wave is as full as possible.
+// Split count for the persistent grid (min(items, slots) CTAs): minimise the
+// busiest CTA's time, (items per CTA) x (pages per item + per-item merge),
+// plus one pipeline fill, plus the merge launch when there are splits.
 int choose_splits(int units, int max_pages, int slots) {
   if (max_pages <= 0) return 1;
-  const int fill = 6;  // pipeline fill + merge, in page-times
+  const int fill = 6;     // pipeline fill, in page-times (once per CTA)
+  const int per_item = 1;  // cross-warp merge and output of an item, in page-times
   int best = 1;
   int64_t best_cost = INT64_MAX;
   const int smax = std::min(kMaxSplits, std::max(1, max_pages / 4));
   for (int s = 1; s <= smax; ++s) {
-    const int64_t ctas = (int64_t)units * s;
-    const int64_t waves = (ctas + slots - 1) / slots;
+    const int64_t items = (int64_t)units * s;
+    const int64_t per_cta = (items + slots - 1) / slots;
     const int64_t per = (max_pages + s - 1) / s;
-    const int64_t cost = waves * (per + fill) + (s > 1 ? 2 : 0);
+    const int64_t cost = per_cta * (per + per_item) + fill + (s > 1 ? 2 : 0);
     if (cost < best_cost) {
       best_cost = cost;
       best = s;
@@ -445,7 +487,9 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
   const int64_t rows = (int64_t)prm.B * prm.Hq;
   prm.S = S;
   prm.final_out = (S == 1 && !partial_mode) ? 1 : 0;
-  dim3 grid(S, prm.Hkv, prm.B);
+  const int64_t items = (int64_t)S * prm.Hkv * prm.B;
+  if (items > INT_MAX) return LKV_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)std::min<int64_t>(items, slots));
   if (launch_pdl(decode_splitkv_kernel<D, GROUP, kNW, STAGES>, grid, dim3((kNW + 1) * 32), Cfg::SMEM_BYTES, stream,
                  tmk, tmv, prm) != cudaSuccess)
     return LKV_ERR_CUDA;
