@@ -44,14 +44,15 @@ def algo_bytes() -> int:
     return 2 * CFG["batch"] * CFG["kv_heads"] * CFG["context"] * CFG["head_dim"] * 2
 
 
-# DRAM read + write bytes of one decode_splitkv launch from one ncu capture of the
-# small case (8 sequences: 268,550,144 read + 5,634,560 written), scaled by the
-# sequences processed (traffic grows in proportion to the pages and partials).
-NCU_SMALL_TRAFFIC = 268_550_144 + 5_634_560
+# DRAM read + write bytes of one full-size decode_splitkv launch (config 2): reads
+# 268,544,000 per 8 sequences in the small-case capture (x 8 = 2,148,352,000; the
+# full-size one-pass capture reads 2.15 GB), writes 4.95 MB in the full-size capture
+# (the split partials that leave L2 during the launch).
+NCU_FULL_TRAFFIC = 2_148_352_000 + 4_950_000
 
 
 def traffic_per_launch() -> int:
-    return NCU_SMALL_TRAFFIC * CFG["batch"] // SMALL["batch"]
+    return NCU_FULL_TRAFFIC * CFG["batch"] // 64
 
 
 def parse():
@@ -512,7 +513,7 @@ def run_ours(args):
                      "kernel": "decode op = decode_splitkv_kernel + merge_partials_kernel",
                      "algorithmic_bytes_per_launch": algo_bytes(), "avg_launch_ms": avg_op_ms,
                      "traffic": traffic_per_launch(),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, small case x batch/8"},
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch"},
         "attn_hbm_gbs": achieved,
         "clocks": clk,
         "gpu_launches": int(args.steps * L * launches_per_call),

@@ -32,6 +32,9 @@ CASES = [
     (6, 64, 32, 8, 128, [513] * 64),
     (7, 3, 8, 2, 128, [0, 17, 0]),  # rows with no keys: zero output, -inf LSE (padding rows)
     (8, 2, 4, 4, 64, [0, 0]),
+    (9, 3, 32, 4, 64, [300, 2000, 17]),  # GQA group 8 at D 64 (the merge takes heads four at a time)
+    # many ragged items per persistent CTA (batch 200 x 2 KV heads x splits > resident CTAs)
+    (10, 200, 16, 2, 128, [(37 * i * i + 11 * i) % 3001 for i in range(200)]),
 ]
 
 
