@@ -377,15 +377,46 @@ __global__ void __launch_bounds__(128) merge_partials_kernel(const MergeParams p
   auto o_at = [&](int s) -> const float* {
     return p.split_major ? p.part_o + (int64_t)s * p.o_part_stride + row * D : p.part_o + (row * p.S + s) * D;
   };
-  float M = -INFINITY;
-  for (int s = lane; s < p.S; s += 32) M = fmaxf(M, lse_at(s));
+  // With at most 32 parts, lane s holds part s's LSE, so the accumulation loop
+  // below has no load-dependent branch and its part loads can all be in flight
+  // at once; the arithmetic and its order are the same as the general loop.
+  const float my_ls = (p.S <= 32 && lane < p.S) ? lse_at(lane) : -INFINITY;
+  float M = my_ls;
+  for (int s = lane + 32; s < p.S; s += 32) M = fmaxf(M, lse_at(s));
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   float acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; ++e) acc[e] = 0.f;
   float L = 0.f;
-  if (M != -INFINITY) {
+  if (M != -INFINITY && p.S <= 32) {
+    const float my_w = my_ls == -INFINITY ? 0.f : exp2f(my_ls - M);
+#pragma unroll 4
+    for (int s = 0; s < p.S; ++s) {
+      const float w = __shfl_sync(0xffffffffu, my_w, s);
+      const float* src = o_at(s) + lane * PER;
+      float v[PER];
+      if constexpr (PER == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(src);
+        v[0] = t.x;
+        v[1] = t.y;
+        v[2] = t.z;
+        v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) v[e] = src[e];
+      }
+      // a part with -inf LSE (w == 0) leaves L and acc untouched, whatever its o holds
+      const bool use = w != 0.f;
+      const float Ln = L + w;
+      L = use ? Ln : L;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const float an = acc[e] + w * v[e];
+        acc[e] = use ? an : acc[e];
+      }
+    }
+  } else if (M != -INFINITY) {
     for (int s = 0; s < p.S; ++s) {
       const float ls = lse_at(s);
       if (ls == -INFINITY) continue;
