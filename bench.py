@@ -366,7 +366,8 @@ def measure_wan(device, reps: int = 5, batch: int | None = None):
                         f"{S + BT} keys ([1560 prefix | shared | blended prev block | block]), non-causal",
             "flops_per_layer": flops, "attn_ms": attn_ms, "tflops": tf, "frac": tf / peak,
             "layer_ms_incl_rope_append": layer_ms, "peak_tflops": peak, "peak_source": src,
-            "kernel": "prefill_tcgen05_kernel<128, 1> (non-causal)"}
+            "kernel": "prefill_tcgen05_kernel<128, 1> (non-causal, keys split in one launch) + merge_partials_kernel",
+            "kv_splits": ops.prefill_split_plan(B, BT, H, H, D, int(m["W"]), False)}
 
 
 def run_ours(args):

@@ -149,6 +149,33 @@ int lkv_prefill_paged(const void* q, int64_t q_stride_tok,
                       int head_dim, int max_pages_per_seq, int causal, float softmax_scale,
                       int32_t* error_word, void* stream);
 
+/* Non-causal lkv_prefill_paged with the keys split `kv_splits` ways inside one
+ * launch (block attention over a long shared history: Wan's
+ * videogen/src/lastkv/videogen/attention.py:9-32, non-causal SDPA over
+ * [prefix | shared | blended previous block | block]).  With one CTA per SM a
+ * grid of C CTAs takes ceil(C / SMs) waves; S * C CTAs of 1/S the keys fill
+ * the last wave better.  Each split writes a normalised fp32 partial and its
+ * natural-log LSE, then the call merges them exactly (lkv_merge_partials) into
+ * `out` (x out_scale) and `lse`; two launches.  Caller-owned scratch:
+ *   partial_o   fp32 [kv_splits][total_q * num_q_heads][head_dim], 16-byte aligned
+ *   partial_lse fp32 [kv_splits][total_q * num_q_heads]
+ * kv_splits 1..8 (1 = lkv_prefill_paged with causal = 0). */
+int lkv_prefill_paged_split(const void* q, int64_t q_stride_tok,
+                            const void* pool_k, const void* pool_v, int64_t num_pages,
+                            const int32_t* block_table, int64_t block_table_stride,
+                            const int32_t* seq_k, const int32_t* cu_seqlens_q,
+                            void* out, int64_t out_stride_tok, float* lse, const float* out_scale,
+                            int batch, int total_q, int max_q, int num_q_heads, int num_kv_heads,
+                            int head_dim, int max_pages_per_seq, float softmax_scale,
+                            int kv_splits, float* partial_o, float* partial_lse,
+                            int32_t* error_word, void* stream);
+
+/* Key-split count lkv_prefill_paged_split should use for this shape on the
+ * current device (1 for causal calls, short key ranges, or grids that already
+ * fill their last wave). */
+int lkv_prefill_split_plan(int batch, int max_q, int num_q_heads, int num_kv_heads, int head_dim,
+                           int max_pages_per_seq, int causal, int* kv_splits);
+
 /* ------------------------------------------------------------------ merge
  * Exact log-sum-exp merge of `num_parts` attention partials over disjoint key
  * sets (flashinfer cascade.merge_state / vLLM merge_attn_states, used at

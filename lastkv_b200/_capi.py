@@ -54,6 +54,9 @@ _SIGNATURES = {
     "lkv_decode_gemm": (I32, [P, I64, P, I64, P, I64, I32, I64, I64, I32, P, P, P]),
     "lkv_prefill_paged": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
                                 I32, I32, I32, I32, I32, I32, I32, I32, F32, P, P]),
+    "lkv_prefill_paged_split": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
+                                      I32, I32, I32, I32, I32, I32, I32, F32, I32, P, P, P, P]),
+    "lkv_prefill_split_plan": (I32, [I32, I32, I32, I32, I32, I32, I32, P]),
 }
 
 

@@ -300,6 +300,50 @@ int lkv_prefill_paged(const void* q, int64_t q_stride_tok, const void* pool_k, c
   return lkv::prefill_paged(a);
 }
 
+int lkv_prefill_split_plan(int batch, int max_q, int num_q_heads, int num_kv_heads, int head_dim,
+                           int max_pages_per_seq, int causal, int* kv_splits) {
+  return lkv::prefill_split_plan(batch, max_q, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq, causal,
+                                 kv_splits);
+}
+
+int lkv_prefill_paged_split(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
+                            int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,
+                            const int32_t* seq_k, const int32_t* cu_seqlens_q, void* out, int64_t out_stride_tok,
+                            float* lse, const float* out_scale, int batch, int total_q, int max_q, int num_q_heads,
+                            int num_kv_heads, int head_dim, int max_pages_per_seq, float softmax_scale,
+                            int kv_splits, float* partial_o, float* partial_lse, int32_t* error_word,
+                            void* stream) {
+  lkv::PrefillArgs a{};
+  a.q = q;
+  a.q_stride_tok = q_stride_tok;
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.block_table = block_table;
+  a.block_table_stride = block_table_stride;
+  a.seq_k = seq_k;
+  a.cu_q = cu_seqlens_q;
+  a.out = out;
+  a.out_stride_tok = out_stride_tok;
+  a.lse = lse;
+  a.out_scale = out_scale;
+  a.batch = batch;
+  a.total_q = total_q;
+  a.max_q = max_q;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.max_pages_per_seq = max_pages_per_seq;
+  a.causal = 0;
+  a.softmax_scale = softmax_scale;
+  a.error_word = error_word;
+  a.stream = stream;
+  a.kv_splits = kv_splits;
+  a.part_o = partial_o;
+  a.part_lse = partial_lse;
+  return lkv::prefill_paged(a);
+}
+
 int lkv_build_layer_block_tables(const int32_t* block_table, int64_t block_table_stride, const int32_t* nsrc,
                                  const int32_t* ring_base, int num_layers, int batch, int width, int32_t* bt_all,
                                  void* stream) {

@@ -683,7 +683,7 @@ int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspa
 
 int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim, int hq,
                    int64_t o_part_stride, int64_t lse_part_stride, const float* out_scale, void* out,
-                   float* lse_out, cudaStream_t stream) {
+                   float* lse_out, cudaStream_t stream, int64_t out_stride_tok) {
   if (head_dim != 64 && head_dim != 128) return LKV_ERR_UNSUPPORTED;
   if (num_parts < 1 || rows < 0 || hq < 1 || rows % hq) return LKV_ERR_INVALID_ARGUMENT;
   if (rows == 0) return LKV_OK;
@@ -706,7 +706,9 @@ int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, 
   mp.Hq = hq;
   mp.out_scale = out_scale;
   mp.out = static_cast<__nv_bfloat16*>(out);
-  mp.out_stride_tok = (int64_t)hq * head_dim;
+  if (out_stride_tok == 0) out_stride_tok = (int64_t)hq * head_dim;
+  if (out_stride_tok < (int64_t)hq * head_dim || (out_stride_tok & 1)) return LKV_ERR_INVALID_ARGUMENT;
+  mp.out_stride_tok = out_stride_tok;
   mp.lse_out = lse_out;
   const unsigned blocks = (unsigned)((rows + 3) / 4);
   const cudaError_t e = head_dim == 128 ? launch_pdl(merge_partials_kernel<128>, dim3(blocks), dim3(128), 0, stream, mp)

@@ -36,8 +36,14 @@ struct PrefillArgs {
   float softmax_scale;
   int32_t* error_word;
   void* stream;
+  // key splits (non-causal only): > 1 writes fp32 partials here, then merges into out / lse
+  int kv_splits = 1;
+  float* part_o = nullptr;    // [kv_splits][total_q * num_q_heads][head_dim]
+  float* part_lse = nullptr;  // [kv_splits][total_q * num_q_heads], natural log
 };
 int prefill_paged(const PrefillArgs& a);
+int prefill_split_plan(int batch, int max_q, int num_q_heads, int num_kv_heads, int head_dim, int max_pages,
+                       int causal, int* kv_splits);
 
 struct DecodeArgs {
   const void* q;
@@ -67,7 +73,7 @@ int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspa
                 int* launches);
 int merge_partials(const float* o_parts, const float* lse_parts, int num_parts, int64_t rows, int head_dim, int hq,
                    int64_t o_part_stride, int64_t lse_part_stride, const float* out_scale, void* out,
-                   float* lse_out, cudaStream_t stream);
+                   float* lse_out, cudaStream_t stream, int64_t out_stride_tok = 0);
 
 struct AppendArgs {
   const void* q;

@@ -61,6 +61,7 @@ constexpr int kWarpK = 8, kWarpV = 9, kWarpMma = 11;
 constexpr int kThreads = 12 * 32;
 constexpr int kStagesK = 2, kStagesV = 3;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kMaxKvSplits = 8;
 
 struct PrefillParams {
   const int32_t* bt;
@@ -76,6 +77,10 @@ struct PrefillParams {
   int64_t num_pages;
   int causal;
   float scale_log2;
+  int S;                 // key splits: blockIdx.z = sequence * S + split
+  float* part_o;         // S > 1: fp32 partials [S][rows][D], rows = token * Hq + head
+  float* part_lse;       // S > 1: natural-log LSE [S][rows]
+  int64_t part_rows;     // rows per split
 };
 
 template <int D>
@@ -120,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + Cfg::OFF_BAR);
 
-  const int cta_tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int cta_tile = blockIdx.x, hk = blockIdx.y, b = blockIdx.z / p.S, split = blockIdx.z % p.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = p.cu_q[b];
   const int Lq = p.cu_q[b + 1] - q0;
@@ -133,16 +138,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t_end = min(t0 + kTiles * TOK, Lq);
   int lim_max = p.causal ? n - Lq + t_end - 1 : n - 1;
   lim_max = min(lim_max, n - 1);
-  const int nb = lim_max >= 0 ? lim_max / kBN + 1 : 0;
+  // Key blocks [j0, j0 + nb) of this CTA: all visible blocks, or this split's share
+  // of them (non-causal calls with S > 1).
+  const int nb_all = lim_max >= 0 ? lim_max / kBN + 1 : 0;
+  const int per_split = (nb_all + p.S - 1) / p.S;
+  const int j0 = min(nb_all, split * per_split);
+  const int nb = min(nb_all, j0 + per_split) - j0;
   if (nb == 0) {
     // no visible keys: zero output rows (and -inf LSE), as an empty softmax
     for (int r = threadIdx.x; r < kTiles * TOK * GROUP; r += kThreads) {
       const int tok = t0 + r / GROUP;
       if (tok >= Lq) continue;
       const int hq = hk * GROUP + r % GROUP;
+      const int64_t row = (int64_t)(q0 + tok) * p.Hq + hq;
+      if (p.S > 1) {
+        float* o = p.part_o + ((int64_t)split * p.part_rows + row) * D;
+        for (int d = 0; d < D; ++d) o[d] = 0.f;
+        p.part_lse[(int64_t)split * p.part_rows + row] = -INFINITY;
+        continue;
+      }
       __nv_bfloat16* o = p.out + (int64_t)(q0 + tok) * p.out_stride_tok + (int64_t)hq * D;
       for (int d = 0; d < D; ++d) o[d] = __float2bfloat16_rn(0.f);
-      if (p.lse) p.lse[(int64_t)(q0 + tok) * p.Hq + hq] = -INFINITY;
+      if (p.lse) p.lse[row] = -INFINITY;
     }
     return;
   }
@@ -209,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[s], Cfg::KV_BYTES);
         uint8_t* dst = ring + s * Cfg::KV_BYTES;
         for (int pg = 0; pg < kPagesPerBlock; ++pg) {
-          const int pi = j * kPagesPerBlock + pg;
+          const int pi = (j0 + j) * kPagesPerBlock + pg;
           int pid = (int)p.num_pages;  // past the pool: TMA fills zeros
           if (pi < npages) {
             pid = btrow[pi];
@@ -310,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(raw[c][e]);
       }
-      const int key0 = j * kBN;
+      const int key0 = (j0 + j) * kBN;
       if (key0 + kBN - 1 > lim) {
 #pragma unroll
         for (int e = 0; e < kBN; ++e)
@@ -382,27 +399,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int hq = hk * GROUP + r % GROUP;
       const bool valid = tok < Lq;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const float sc = inv * (p.out_scale ? p.out_scale[hq] : 1.f);
-      __nv_bfloat16* orow = p.out + (int64_t)(q0 + (valid ? tok : 0)) * p.out_stride_tok + (int64_t)hq * D;
+      const float lse_e = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+      const int64_t row = (int64_t)(q0 + (valid ? tok : 0)) * p.Hq + hq;
+      if (p.S > 1) {
+        // this split's normalised partial (fp32) and its natural-log LSE
+        float* orow = p.part_o + ((int64_t)split * p.part_rows + row) * D;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(lane_base + col_o + c * 32, raw);
-        tmem_wait_ld();
-        if (valid) {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(lane_base + col_o + c * 32, raw);
+          tmem_wait_ld();
+          if (valid) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 v;
-            v.x = pack_bf16(__uint_as_float(raw[e + 0]) * sc, __uint_as_float(raw[e + 1]) * sc);
-            v.y = pack_bf16(__uint_as_float(raw[e + 2]) * sc, __uint_as_float(raw[e + 3]) * sc);
-            v.z = pack_bf16(__uint_as_float(raw[e + 4]) * sc, __uint_as_float(raw[e + 5]) * sc);
-            v.w = pack_bf16(__uint_as_float(raw[e + 6]) * sc, __uint_as_float(raw[e + 7]) * sc);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(orow + c * 32 + e) =
+                  make_float4(__uint_as_float(raw[e]) * inv, __uint_as_float(raw[e + 1]) * inv,
+                              __uint_as_float(raw[e + 2]) * inv, __uint_as_float(raw[e + 3]) * inv);
           }
         }
+        if (valid) p.part_lse[(int64_t)split * p.part_rows + row] = lse_e;
+      } else {
+        const float sc = inv * (p.out_scale ? p.out_scale[hq] : 1.f);
+        __nv_bfloat16* orow = p.out + (int64_t)(q0 + (valid ? tok : 0)) * p.out_stride_tok + (int64_t)hq * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(lane_base + col_o + c * 32, raw);
+          tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              uint4 v;
+              v.x = pack_bf16(__uint_as_float(raw[e + 0]) * sc, __uint_as_float(raw[e + 1]) * sc);
+              v.y = pack_bf16(__uint_as_float(raw[e + 2]) * sc, __uint_as_float(raw[e + 3]) * sc);
+              v.z = pack_bf16(__uint_as_float(raw[e + 4]) * sc, __uint_as_float(raw[e + 5]) * sc);
+              v.w = pack_bf16(__uint_as_float(raw[e + 6]) * sc, __uint_as_float(raw[e + 7]) * sc);
+              *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+            }
+          }
+        }
+        if (valid && p.lse) p.lse[row] = lse_e;
       }
-      if (valid && p.lse)
-        p.lse[(int64_t)(q0 + tok) * p.Hq + hq] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
     }
   }
 
@@ -426,7 +463,7 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
       return LKV_ERR_CUDA;
     attr_done[dev] = true;
   }
-  dim3 grid((max_q + TOK - 1) / TOK, prm.Hkv, prm.B);
+  dim3 grid((max_q + TOK - 1) / TOK, prm.Hkv, prm.B * prm.S);
   prefill_tcgen05_kernel<D, GROUP><<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
   return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
 }
@@ -446,6 +483,12 @@ int prefill_paged(const PrefillArgs& a) {
   if ((reinterpret_cast<uintptr_t>(a.out) & 15) || ((a.out_stride_tok * 2) & 15)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.batch > 65535 || a.num_kv_heads > 65535) return LKV_ERR_UNSUPPORTED;
   if (!a.error_word) return LKV_ERR_INVALID_ARGUMENT;
+  const int S = a.kv_splits < 1 ? 1 : a.kv_splits;
+  if (S > 1) {
+    // key splits need a non-causal call (every query sees the same key range)
+    if (a.causal || S > kMaxKvSplits || (int64_t)a.batch * S > 65535) return LKV_ERR_UNSUPPORTED;
+    if (!a.part_o || !a.part_lse || (reinterpret_cast<uintptr_t>(a.part_o) & 15)) return LKV_ERR_INVALID_ARGUMENT;
+  }
 
   CUtensorMap tq, tk, tv;
   int st = make_query_tensor_map(&tq, a.q, a.total_q, a.q_stride_tok, a.num_q_heads, a.head_dim, group);
@@ -472,8 +515,13 @@ int prefill_paged(const PrefillArgs& a) {
   prm.num_pages = a.num_pages;
   prm.causal = a.causal ? 1 : 0;
   prm.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+  prm.S = S;
+  prm.part_o = a.part_o;
+  prm.part_lse = a.part_lse;
+  prm.part_rows = (int64_t)a.total_q * a.num_q_heads;
   cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
-#define LKV_PF(DD, GG) return launch_prefill<DD, GG>(tq, tk, tv, prm, a.max_q, stream)
+  int rc = LKV_OK;
+#define LKV_PF(DD, GG) rc = launch_prefill<DD, GG>(tq, tk, tv, prm, a.max_q, stream); break
   if (a.head_dim == 128) {
     switch (group) {
       case 1: LKV_PF(128, 1);
@@ -490,6 +538,46 @@ int prefill_paged(const PrefillArgs& a) {
     }
   }
 #undef LKV_PF
+  if (rc != LKV_OK || S == 1) return rc;
+  // exact LSE merge of the splits into out (x out_scale) and lse
+  return merge_partials(a.part_o, a.part_lse, S, prm.part_rows, a.head_dim, a.num_q_heads,
+                        prm.part_rows * a.head_dim, prm.part_rows, a.out_scale, a.out, a.lse, stream,
+                        a.out_stride_tok);
+}
+
+// Key splits for a non-causal call: with one CTA per SM, a grid of C CTAs runs
+// ceil(C / SMs) waves of equal CTAs of `blocks` key blocks; splitting the keys S
+// ways gives S * C CTAs of blocks / S, ceil(S * C / SMs) / S waves, plus per
+// extra split the partials' write and merge and the extra CTAs' start-up, about
+// 28 block-times (measured on the Wan-1.3B shape: 456 CTAs x 256 blocks ran
+// 1.80 / 1.70 / 1.68 / 1.69 / 1.71 / 1.81 ms at S = 1 / 2 / 3 / 4 / 5 / 8).
+// Short key ranges (under 16 blocks per split) are not split.
+int prefill_split_plan(int batch, int max_q, int num_q_heads, int num_kv_heads, int head_dim, int max_pages,
+                       int causal, int* kv_splits) {
+  if (!kv_splits) return LKV_ERR_INVALID_ARGUMENT;
+  *kv_splits = 1;
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return LKV_ERR_INVALID_ARGUMENT;
+  if (head_dim != 64 && head_dim != 128) return LKV_ERR_UNSUPPORTED;
+  if (causal || batch <= 0 || max_q <= 0 || max_pages <= 0) return LKV_OK;
+  const int group = num_q_heads / num_kv_heads;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return LKV_ERR_CUDA;
+  const int64_t tok_per_cta = (int64_t)kTiles * kBM / group;
+  const int64_t ctas = (max_q + tok_per_cta - 1) / tok_per_cta * num_kv_heads * batch;
+  const int64_t blocks = ((int64_t)max_pages * kPageTok + kBN - 1) / kBN;
+  double best = 1e30;
+  for (int s = 1; s <= kMaxKvSplits; ++s) {
+    if (s > 1 && (blocks / s < 16 || (int64_t)batch * s > 65535)) break;
+    const double waves = (double)((ctas * s + sms - 1) / sms) / s;
+    const double cost = waves * (double)blocks + 28.0 * (s - 1);
+    if (cost < best - 1e-9) {
+      best = cost;
+      *kv_splits = s;
+    }
+  }
+  return LKV_OK;
 }
 
 }  // namespace lkv

@@ -8,6 +8,8 @@ the caller passes ``out``/``workspace`` buffers.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _capi
@@ -115,8 +117,6 @@ def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, o
 
 def decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages, workspace: Workspace, partial=False):
     """(splits, kernel launches) lkv_decode_paged will use for this shape on the current device."""
-    import ctypes
-
     s, n = ctypes.c_int(0), ctypes.c_int(0)
     _capi.check(_capi.lib().lkv_decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages,
                                             workspace.nbytes, int(partial), ctypes.byref(s), ctypes.byref(n)),
@@ -124,12 +124,23 @@ def decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages, workspace
     return s.value, n.value
 
 
+def prefill_split_plan(batch, max_q, num_q_heads, num_kv_heads, head_dim, max_pages, causal) -> int:
+    """Key splits lkv_prefill_paged_split would use for this shape (1 = no split)."""
+    s = ctypes.c_int(1)
+    _capi.check(_capi.lib().lkv_prefill_split_plan(batch, max_q, num_q_heads, num_kv_heads, head_dim, max_pages,
+                                                   int(bool(causal)), ctypes.byref(s)), "lkv_prefill_split_plan")
+    return s.value
+
+
 def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, causal=True, softmax_scale=None,
-                  out=None, lse=None, out_scale=None, error_word=None, max_pages: int | None = None):
+                  out=None, lse=None, out_scale=None, error_word=None, max_pages: int | None = None,
+                  kv_splits: int | None = None):
     """Varlen chunked prefill on tcgen05 tensor cores.
 
     q [T, Hq, D] bf16 rows; cu_q int32 [B+1]; seq_k int32 [B] (>= span when
-    causal; bottom-right alignment); returns out [T, Hq, D] bf16.
+    causal; bottom-right alignment); returns out [T, Hq, D] bf16.  Non-causal
+    calls may split the keys (``kv_splits``; None = the library's plan) into
+    fp32 partials merged in a second launch.
     """
     _check_pool(pool_k, pool_v)
     T, Hq, D = q.shape
@@ -149,6 +160,20 @@ def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, ca
         error_word = torch.zeros(4, dtype=torch.int32, device=q.device)
     if out_scale is not None:
         _require(out_scale.dtype == torch.float32 and out_scale.numel() == Hq, "out_scale must be fp32 [Hq]")
+    if causal:
+        kv_splits = 1
+    elif kv_splits is None:
+        kv_splits = prefill_split_plan(B, int(max_q), Hq, Hkv, D, W, False)
+    if kv_splits > 1:
+        part_o = torch.empty((kv_splits, T * Hq, D), dtype=torch.float32, device=q.device)
+        part_lse = torch.empty((kv_splits, T * Hq), dtype=torch.float32, device=q.device)
+        st = _capi.lib().lkv_prefill_paged_split(
+            q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
+            block_table.stride(0), seq_k.data_ptr(), cu_q.data_ptr(), out.data_ptr(), out.stride(0), _ptr(lse),
+            _ptr(out_scale), B, T, int(max_q), Hq, Hkv, D, W, float(softmax_scale), int(kv_splits),
+            part_o.data_ptr(), part_lse.data_ptr(), error_word.data_ptr(), _stream())
+        _capi.check(st, "lkv_prefill_paged_split")
+        return out
     st = _capi.lib().lkv_prefill_paged(
         q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
         block_table.stride(0), seq_k.data_ptr(), cu_q.data_ptr(), out.data_ptr(), out.stride(0), _ptr(lse),
@@ -361,8 +386,6 @@ def decode_gemm_supported(x, weight) -> bool:
 
 def decode_gemm_plan(n_rows: int, k: int, silu_mul: bool = False) -> dict:
     """{tiles, splits, ctas_per_sm} of the decode GEMM launch for a weight [n_rows, k] on this device."""
-    import ctypes
-
     t, s, o = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
     _capi.check(_capi.lib().lkv_decode_gemm_plan(n_rows, k, GEMM_SILU_MUL if silu_mul else GEMM_PLAIN,
                                                  ctypes.byref(t), ctypes.byref(s), ctypes.byref(o)),
@@ -398,8 +421,6 @@ def decode_gemm(x, weight, *, silu_mul: bool = False, out=None, error_word=None)
 
 def cp_combine_sizes(rows: int, head_dim: int, world: int) -> dict:
     """{send_floats, recv_words} of the context-parallel combine buffers."""
-    import ctypes
-
     a, b = ctypes.c_int64(0), ctypes.c_int64(0)
     _capi.check(_capi.lib().lkv_cp_combine_sizes(rows, head_dim, world, ctypes.byref(a), ctypes.byref(b)),
                 "lkv_cp_combine_sizes")
@@ -413,8 +434,6 @@ def cp_combine(send, recv_ptrs, rank: int, world: int, state, rows: int, head_di
     addresses valid on this GPU; state: int32 [2] device tensor, zero before the first
     call (the call's epoch advances on the device, so calls can be graph-captured).
     Returns out bf16 [rows / hq, hq, head_dim]."""
-    import ctypes
-
     _require(send.dtype == torch.float32 and send.is_contiguous() and send.is_cuda, "send must be contiguous fp32")
     _require(len(recv_ptrs) == world, "one receive buffer per rank")
     _require(state.dtype == torch.int32 and state.numel() >= 2 and state.is_cuda, "state must be int32 [2]")

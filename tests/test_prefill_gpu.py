@@ -74,6 +74,50 @@ def test_prefill_matches_oracle(case):
     np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, rtol=1e-4, atol=2e-3)
 
 
+SPLIT_CASES = [
+    # seed, lq, nk, Hq, Hkv, D, kv_splits (non-causal, keys split inside one launch, then merged)
+    (20, [256, 100], [256 + 4680, 100 + 3000], 32, 4, 128, 2),
+    (21, [77, 300], [1000, 5000], 12, 12, 64, 3),
+    (22, [130], [2100], 8, 8, 128, 8),        # 17 key blocks over 8 splits: 3 per split, the last empty
+    (23, [64, 64], [64, 20], 16, 8, 128, 5),  # more splits than key blocks: empty splits merge to nothing
+]
+
+
+@pytest.mark.parametrize("case", SPLIT_CASES, ids=lambda c: f"s{c[0]}_D{c[5]}_S{c[6]}")
+def test_prefill_key_splits_match_oracle(case):
+    from lastkv_b200 import ops
+
+    seed, lq, nk, Hq, Hkv, D, S = case
+    dev, host = _case(seed, lq, nk, Hq, Hkv, D)
+    s_h = np.random.default_rng(seed + 50).uniform(0.5, 1.5, Hq).astype(np.float32)
+    lse = torch.empty((sum(lq), Hq), dtype=torch.float32, device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    out = ops.prefill_paged(dev["q"], dev["pool_k"], dev["pool_v"], dev["bt"], dev["seq_k"], dev["cu"], max(lq),
+                            causal=False, lse=lse, out_scale=torch.from_numpy(s_h).cuda(), error_word=err,
+                            kv_splits=S)
+    one = ops.prefill_paged(dev["q"], dev["pool_k"], dev["pool_v"], dev["bt"], dev["seq_k"], dev["cu"], max(lq),
+                            causal=False, out_scale=torch.from_numpy(s_h).cuda(), kv_splits=1)
+    torch.cuda.synchronize()
+    assert err.cpu().tolist()[0] == 0
+    ref, ref_lse = O.paged_attention(host["q"], host["pool_k"], host["pool_v"], host["bt"], host["seq_k"],
+                                     host["cu"], scale=D ** -0.5, out_scale=s_h, causal=False)
+    assert_close_bf16(out.float().cpu().numpy(), ref, what="split prefill")
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, rtol=1e-4, atol=2e-3)
+    # the same attention as the unsplit kernel up to the order of the fp32 sums
+    assert_close_bf16(out.float().cpu().numpy(), one.float().cpu().numpy(), max_abs=1.6e-2, rel_l2=4e-3,
+                      what="split vs unsplit")
+
+
+def test_prefill_split_plan_is_one_for_causal_and_short_keys():
+    from lastkv_b200 import ops
+
+    assert ops.prefill_split_plan(2, 4680, 12, 12, 128, 2048, True) == 1
+    assert ops.prefill_split_plan(2, 4680, 12, 12, 128, 20, False) == 1
+    # Wan-1.3B block attention (batch 2, 12 heads, 4680 queries x 32760 keys): 456 CTAs on the SMs
+    s = ops.prefill_split_plan(2, 4680, 12, 12, 128, 2048, False)
+    assert 1 <= s <= 8
+
+
 def test_prefill_single_token_equals_decode():
     from lastkv_b200 import ops
 
