@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill tensor-core measurement")
     ap.add_argument("--no-e2e8b", action="store_true", help="skip the 8B end-to-end decode measurement (config 3)")
+    ap.add_argument("--wan-kv-splits", type=int, default=None,
+                    help="force the Wan attention's key-split count (default: lkv_prefill_split_plan)")
     ap.add_argument("--cp-combine", default="p2p", choices=["p2p", "nccl"],
                     help="cp128k: combine the partials over peer memory (one kernel) or NCCL all-gather + merge")
     ap.add_argument("--cp-eager", action="store_true", help="cp128k: launch per layer instead of a CUDA graph")
@@ -302,7 +304,7 @@ WAN = dict(batch=2, heads=12, head_dim=128, frame_h=30, frame_w=52, frames_per_b
            prefix_tokens=1560)
 
 
-def measure_wan(device, reps: int = 5, batch: int | None = None):
+def measure_wan(device, reps: int = 5, batch: int | None = None, kv_splits: int | None = None):
     """Wan-1.3B causal block attention (config 5): the last 3-frame block (4680 queries) against the
     full 21-frame history (32760 keys), per layer: fused 3-D-RoPE append + non-causal tcgen05 prefill."""
     import torch
@@ -338,9 +340,11 @@ def measure_wan(device, reps: int = 5, batch: int | None = None):
     qa = torch.randn((B * BT, H, D), generator=gen, device=device, dtype=torch.bfloat16)
     out = torch.empty_like(qa)
 
+    splits = kv_splits or ops.prefill_split_plan(B, BT, H, H, D, int(m["W"]), False)
+
     def attn_only():
         ops.prefill_paged(qa, cache.pool_k, cache.pool_v, m["bt"][0], m["seq_k"], m["cu_q"], BT, causal=False,
-                          out=out, error_word=cache.error_word, max_pages=m["W"])
+                          out=out, error_word=cache.error_word, max_pages=m["W"], kv_splits=splits)
 
     attn_only()
     torch.cuda.synchronize()
@@ -367,7 +371,7 @@ def measure_wan(device, reps: int = 5, batch: int | None = None):
             "flops_per_layer": flops, "attn_ms": attn_ms, "tflops": tf, "frac": tf / peak,
             "layer_ms_incl_rope_append": layer_ms, "peak_tflops": peak, "peak_source": src,
             "kernel": "prefill_tcgen05_kernel<128, 1> (non-causal, keys split in one launch) + merge_partials_kernel",
-            "kv_splits": ops.prefill_split_plan(B, BT, H, H, D, int(m["W"]), False)}
+            "kv_splits": splits}
 
 
 def run_ours(args):
@@ -523,7 +527,7 @@ def run_ours(args):
     if not args.no_prefill:
         # the small case (profiler captures) runs the same spans with 2 sequences
         line["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
-        line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1)
+        line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1, kv_splits=args.wan_kv_splits)
     if not args.no_e2e8b:
         # config 3 on the same ranks: the 8B architecture end to end (weak scaling, batch 8 per GPU)
         del wl
