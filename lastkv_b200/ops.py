@@ -134,13 +134,16 @@ def prefill_split_plan(batch, max_q, num_q_heads, num_kv_heads, head_dim, max_pa
 
 def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, causal=True, softmax_scale=None,
                   out=None, lse=None, out_scale=None, error_word=None, max_pages: int | None = None,
-                  kv_splits: int | None = None):
+                  kv_splits: int | None = None, partials=None):
     """Varlen chunked prefill on tcgen05 tensor cores.
 
     q [T, Hq, D] bf16 rows; cu_q int32 [B+1]; seq_k int32 [B] (>= span when
     causal; bottom-right alignment); returns out [T, Hq, D] bf16.  Non-causal
     calls may split the keys (``kv_splits``; None = the library's plan) into
-    fp32 partials merged in a second launch.
+    fp32 partials merged in a second launch; ``partials`` = (o fp32
+    [S, T * Hq, D], lse fp32 [S, T * Hq]) with S >= kv_splits supplies their
+    scratch (otherwise it is allocated per call, so pass it, or kv_splits=1,
+    inside a CUDA-graph capture).
     """
     _check_pool(pool_k, pool_v)
     T, Hq, D = q.shape
@@ -165,8 +168,17 @@ def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, ca
     elif kv_splits is None:
         kv_splits = prefill_split_plan(B, int(max_q), Hq, Hkv, D, W, False)
     if kv_splits > 1:
-        part_o = torch.empty((kv_splits, T * Hq, D), dtype=torch.float32, device=q.device)
-        part_lse = torch.empty((kv_splits, T * Hq), dtype=torch.float32, device=q.device)
+        if partials is not None:
+            part_o, part_lse = partials
+            _require(part_o.dtype == torch.float32 and part_o.is_contiguous() and part_o.dim() == 3
+                     and part_o.shape[0] >= kv_splits and part_o.shape[1:] == (T * Hq, D),
+                     "partials[0] must be contiguous fp32 [S >= kv_splits, T * Hq, D]")
+            _require(part_lse.dtype == torch.float32 and part_lse.is_contiguous()
+                     and part_lse.shape[0] >= kv_splits and part_lse.shape[1:] == (T * Hq,),
+                     "partials[1] must be contiguous fp32 [S >= kv_splits, T * Hq]")
+        else:
+            part_o = torch.empty((kv_splits, T * Hq, D), dtype=torch.float32, device=q.device)
+            part_lse = torch.empty((kv_splits, T * Hq), dtype=torch.float32, device=q.device)
         st = _capi.lib().lkv_prefill_paged_split(
             q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
             block_table.stride(0), seq_k.data_ptr(), cu_q.data_ptr(), out.data_ptr(), out.stride(0), _ptr(lse),

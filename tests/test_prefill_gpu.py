@@ -193,3 +193,36 @@ def test_prefill_graph_capture_replays_identically():
     torch.cuda.synchronize()
     assert torch.equal(out, first)
     assert err.cpu().tolist()[0] == 0
+
+
+def test_prefill_key_split_graph_capture_with_caller_partials():
+    """Key-split non-causal prefill with caller-owned partials records into a CUDA graph
+    and replays bit for bit (the split launch and its merge, no allocation)."""
+    from lastkv_b200 import ops
+
+    dev, _ = _case(24, [256, 100], [3000, 2500], 16, 4, 128)
+    T, Hq, D, S = 356, 16, 128, 3
+    out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty((T, Hq), dtype=torch.float32, device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    parts = (torch.empty((S, T * Hq, D), device="cuda"), torch.empty((S, T * Hq), device="cuda"))
+
+    def call():
+        ops.prefill_paged(dev["q"], dev["pool_k"], dev["pool_v"], dev["bt"], dev["seq_k"], dev["cu"], 256,
+                          causal=False, out=out, lse=lse, error_word=err, kv_splits=S, partials=parts)
+
+    call()
+    first, first_lse = out.clone(), lse.clone()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            call()
+    torch.cuda.current_stream().wait_stream(s)
+    out.zero_()
+    lse.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, first) and torch.equal(lse, first_lse)
+    assert err.cpu().tolist()[0] == 0
