@@ -219,14 +219,17 @@ __global__ void __launch_bounds__((NW + 1) * 32)
         uint8_t* kt = smem + s * Cfg::STAGE_BYTES + warp * Cfg::PAGE_BYTES;
         uint8_t* vt = kt + Cfg::HALVES * Cfg::TILE_BYTES;
         const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < KT; ++j) {
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4(a0, a1, a2, a3,
                       kbase + (j >> 2) * Cfg::TILE_BYTES + swz128(k_row, 2 * (j & 3) + k_chunk_hi));
-          mma_bf16_16816(sc, a0, a1, a2, a3, qf[j][0], qf[j][1]);
+          if (j & 1) mma_bf16_16816(sd, a0, a1, a2, a3, qf[j][0], qf[j][1]);
+          else mma_bf16_16816(sc, a0, a1, a2, a3, qf[j][0], qf[j][1]);
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] += sd[e];
         const int key0 = page_idx * PAGE;
         const int valid_rows = n - key0;  // >= 1
         const bool r0 = g < valid_rows, r1 = g + 8 < valid_rows;
@@ -236,11 +239,11 @@ __global__ void __launch_bounds__((NW + 1) * 32)
         const float s11 = r1 ? sc[3] * p.scale_log2 : -INFINITY;
         const float mn0 = fmaxf(m0, warp_max_g(fmaxf(s00, s10)));
         const float mn1 = fmaxf(m1, warp_max_g(fmaxf(s01, s11)));
-        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        const float al0 = ex2_approx(m0 - mn0), al1 = ex2_approx(m1 - mn1);
         m0 = mn0;
         m1 = mn1;
-        const float p00 = exp2f(s00 - mn0), p01 = exp2f(s01 - mn1);
-        const float p10 = exp2f(s10 - mn0), p11 = exp2f(s11 - mn1);
+        const float p00 = ex2_approx(s00 - mn0), p01 = ex2_approx(s01 - mn1);
+        const float p10 = ex2_approx(s10 - mn0), p11 = ex2_approx(s11 - mn1);
         l0 = l0 * al0 + p00 + p10;
         l1 = l1 * al1 + p01 + p11;
 #pragma unroll
