@@ -39,6 +39,12 @@
 // because the final normalisation uses the same reference.  The softmax takes
 // a quarter of its exponentials on the FMA pipe (ex2_poly2) and the rest on the
 // SFU, and stores P in 32-key chunks as they are ready.
+//
+// Key splits (non-causal calls, S > 1): blockIdx.z = sequence * S + split and
+// a CTA covers its split's share of the key blocks, writing the normalised
+// fp32 partial and natural-log LSE of its rows; merge_partials_kernel then
+// combines the splits exactly.  With one CTA per SM, this fills the last wave
+// of a grid of few, long CTAs (Wan's block attention).
 
 #include <math.h>
 
