@@ -631,7 +631,7 @@ def run_cp(args):
     torch.cuda.synchronize()
     graph = None
     if not args.cp_eager:
-        # the 32 layer calls of one step (decode partial + combine each) as one CUDA graph
+        # the 32 layer calls of one step (decode with push + combine each) as one CUDA graph
         if world > 1:
             dist.barrier()
         graph = torch.cuda.CUDAGraph()
@@ -664,7 +664,8 @@ def run_cp(args):
             "config": {"workload": "cp128k", "batch": B, "context_tokens": N, "ring_window": Wt, "q_heads": Hq,
                        "kv_heads": H, "head_dim": D, "layers_per_step": L,
                        "parallelism": f"cp{world} (shared pages sharded; " + (
-                           "peer-memory push + LSE merge in one kernel)" if cp.combine == "p2p" and world > 1
+                           "decode kernel pushes each unit's merged rows over peer memory; one poll + LSE "
+                           "merge launch)" if cp.combine == "p2p" and world > 1
                            else "NCCL all-gather + LSE merge)"),
                        "launch": "eager per layer" if graph is None else "one CUDA graph per step"},
             "layer_ms": layer_ms, "attn_bytes_per_layer_total": bytes_layer,

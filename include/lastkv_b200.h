@@ -331,6 +331,30 @@ int lkv_decode_gemm(const void* x, int64_t x_row, const void* w, int64_t w_row, 
  * complete hold garbage).  out: bf16 rows (tok = row / hq, head = row % hq)
  * scaled by out_scale[head] (may be NULL). */
 int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_floats, int64_t* recv_words);
+
+/* Sequence-sharded decode in one call, the exchange fused into the decode:
+ * lkv_decode_paged over this rank's slice of every sequence's keys, whose
+ * kernel, as each (sequence, KV head) finishes, merges that unit's splits and
+ * pushes the merged rows to every rank's receive buffer (the same {value,
+ * epoch} words lkv_cp_combine pushes, so the transfer overlaps the rest of the
+ * decode), then lkv_cp_combine with send = NULL polls and merges the `world`
+ * ranks' rows in rank order into `out` (x out_scale).  Two launches, no merge
+ * launch and no collective call; the result equals lkv_decode_paged (partial)
+ * + all-gather + lkv_merge_partials bit for bit.  peer_recv / recv sizes as for
+ * lkv_cp_combine (rows = batch * num_q_heads); `workspace` as for
+ * lkv_decode_paged; state: lkv_decode_cp_state_words uint32 of device memory
+ * (8-byte aligned, zero before the first call; every completed call leaves it
+ * ready for the next; zero it again after a call reports a device error). */
+int lkv_decode_cp_state_words(int batch, int num_kv_heads, int64_t* state_words);
+int lkv_decode_paged_cp(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
+                        int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,
+                        const int32_t* seq_k, void* out, int64_t out_stride_tok, const float* out_scale,
+                        int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_pages_per_seq,
+                        float softmax_scale, void* workspace, size_t workspace_bytes,
+                        const uint64_t* peer_recv, int rank, int world, uint32_t* state,
+                        int32_t* error_word, void* stream);
+/* send may be NULL when this rank's rows were already pushed into every receive
+ * buffer (lkv_decode_paged_cp's decode kernel); the call then only polls and merges. */
 int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state,
                    int64_t rows, int head_dim, int hq, const float* out_scale, void* out,
                    int64_t out_stride_tok, int32_t* error_word, void* stream);

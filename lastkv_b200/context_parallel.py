@@ -65,15 +65,17 @@ def plan_shard(nsrc_pages: int, window_tokens: int, page: int, world: int, rank:
 class ContextParallelDecode:
     """Sequence-sharded decode for one process group (NCCL on GPUs, gloo for host tests).
 
-    Each rank writes its partial (o, lse) into one packed send buffer
-    [B*Hq*D | B*Hq | pad].  ``combine`` picks how the partials meet:
+    ``combine`` picks how the ranks' partials (o, lse) meet:
 
-    * ``"p2p"`` (default with more than one CUDA rank): one ``lkv_cp_combine``
-      launch per layer pushes this rank's rows into every peer's receive buffer
-      over NVLink peer memory (torch symmetric memory), waits for the peers'
-      rows and merges in rank order - no collective call and no merge launch;
-    * ``"nccl"``: one ``all_gather_into_tensor`` of the packed buffers, then the
-      merge kernel over the gathered parts in place.
+    * ``"p2p"`` (default with more than one CUDA rank): ``lkv_decode_paged_cp``
+      - the decode kernel itself, as each (sequence, KV head) finishes, merges
+      its splits and pushes the merged rows into every rank's receive buffer
+      over NVLink peer memory (torch symmetric memory), so the transfer overlaps
+      the rest of the decode; one poll-and-merge launch then combines the ranks
+      in rank order - no collective call and no split-merge launch;
+    * ``"nccl"``: the decode's partial into one packed send buffer
+      [B*Hq*D | B*Hq | pad], one ``all_gather_into_tensor``, then the merge
+      kernel over the gathered parts in place.
 
     Both merge the same partials in the same order (identical outputs).
     ``partial_fn`` and ``merge_fn`` can be injected (host tests) and then use
@@ -100,9 +102,9 @@ class ContextParallelDecode:
         self._bufs = {}
         self._p2p = {}
 
-    def _p2p_state(self, B, Hq, D, device):
+    def _p2p_state(self, B, Hq, D, device, Hkv=1):
         """Receive buffers in symmetric memory (allocated and exchanged once per shape)."""
-        key = (B, Hq, D, str(device))
+        key = (B, Hq, D, Hkv, str(device))
         st = self._p2p.get(key)
         if st is None:
             import torch.distributed._symmetric_memory as symm
@@ -118,6 +120,8 @@ class ContextParallelDecode:
                   "send": torch.empty(sizes["send_floats"], dtype=torch.float32, device=device),
                   "state": torch.zeros(2, dtype=torch.int32, device=device),
                   "error": torch.zeros(4, dtype=torch.int32, device=device)}
+            # fused path: epoch, done counter and per-(sequence, KV head) arrivals
+            st["cp_state"] = torch.zeros(ops.decode_cp_state_words(B, Hkv), dtype=torch.int32, device=device)
             self._p2p[key] = st
         return st
 
@@ -148,13 +152,11 @@ class ContextParallelDecode:
             return self._layer_generic(q, pool_k, pool_v, block_table, seq_k, out_scale, out, workspace, max_pages)
         B, Hq, D = q.shape
         if self.combine == "p2p":
-            st = self._p2p_state(B, Hq, D, q.device)
-            send = st["send"]
-            ops.decode_paged(q, pool_k, pool_v, block_table, seq_k, workspace=workspace, max_pages=max_pages,
-                             partial=True, partial_out=(send[: B * Hq * D].view(B, Hq, D),
-                                                        send[B * Hq * D: B * Hq * (D + 1)].view(B, Hq)))
-            return ops.cp_combine(send, st["recv_ptrs"], self.rank, self.world, st["state"], B * Hq, D, Hq,
-                                  out_scale=out_scale, out=out, error_word=st["error"])
+            # the decode kernel pushes every unit's merged rows as it finishes; one poll-and-merge launch follows
+            st = self._p2p_state(B, Hq, D, q.device, pool_k.shape[2])
+            return ops.decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, st["recv_ptrs"], self.rank, self.world,
+                                       st["cp_state"], out=out, out_scale=out_scale, workspace=workspace,
+                                       max_pages=max_pages, error_word=st["error"])
         n = -(-(B * Hq * (D + 1)) // 4) * 4  # o | lse | pad to a multiple of 4 floats (float4 reads)
         send, recv = self._buffers(("packed", n, str(q.device)), lambda: (
             torch.empty(n, dtype=torch.float32, device=q.device),

@@ -181,6 +181,47 @@ int lkv_decode_paged(const void* q, int64_t q_stride_tok, const void* pool_k, co
   return lkv::decode_paged(a);
 }
 
+int lkv_decode_cp_state_words(int batch, int num_kv_heads, int64_t* state_words) {
+  if (batch < 1 || num_kv_heads < 1 || !state_words) return LKV_ERR_INVALID_ARGUMENT;
+  *state_words = 2 + (int64_t)batch * num_kv_heads;
+  return LKV_OK;
+}
+
+int lkv_decode_paged_cp(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v, int64_t num_pages,
+                        const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_k, void* out,
+                        int64_t out_stride_tok, const float* out_scale, int batch, int num_q_heads, int num_kv_heads,
+                        int head_dim, int max_pages_per_seq, float softmax_scale, void* workspace,
+                        size_t workspace_bytes, const uint64_t* peer_recv, int rank, int world, uint32_t* state,
+                        int32_t* error_word, void* stream) {
+  lkv::DecodeArgs a{};
+  a.q = q;
+  a.q_stride_tok = q_stride_tok;
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.block_table = block_table;
+  a.block_table_stride = block_table_stride;
+  a.seq_k = seq_k;
+  a.out = out;
+  a.out_stride_tok = out_stride_tok;
+  a.out_scale = out_scale;
+  a.batch = batch;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.max_pages_per_seq = max_pages_per_seq;
+  a.softmax_scale = softmax_scale;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  a.stream = stream;
+  a.cp_recv = peer_recv;
+  a.cp_rank = rank;
+  a.cp_world = world;
+  a.cp_state = state;
+  a.cp_error = error_word;
+  return lkv::decode_paged_cp(a);
+}
+
 int lkv_decode_plan(int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_pages_per_seq,
                     size_t workspace_bytes, int partial, int* num_splits, int* num_launches) {
   return lkv::decode_plan(batch, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq, workspace_bytes, partial,

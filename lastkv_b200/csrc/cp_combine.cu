@@ -21,6 +21,10 @@
 // epoch parity: a peer can reuse a slot only after it has received this rank's
 // next epoch, which this rank pushes after it finished reading that slot.
 // No multicast and no NVLS: plain loads and stores to peer-mapped memory.
+// With send == null the push already happened inside the decode kernel (its
+// context-parallel mode writes every rank's merged rows into the receive slots
+// with the same words); the kernel then only polls and merges, reading this
+// rank's own rows from its receive buffer like a peer's.
 
 #include <algorithm>
 
@@ -40,7 +44,7 @@ struct CpPeers {
 };
 
 struct CpParams {
-  const float* send;    // this rank's packed partial: o [rows * D] | lse [rows]
+  const float* send;    // this rank's packed partial: o [rows * D] | lse [rows]; null: already pushed
   int64_t part_words;   // words per partial in a receive slot (>= rows * (D + 1))
   int64_t rows;
   int rows_per_cta;
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(kCpThreads)
   // 1. push this CTA's rows to every peer: pairs of {value, epoch} words
   const int64_t npair = (r1 - r0) * D / 2;
   const float2* src_o = reinterpret_cast<const float2*>(p.send + r0 * D);
-  for (int peer = 0; peer < p.world; ++peer) {
+  for (int peer = 0; p.send && peer < p.world; ++peer) {
     if (peer == p.rank) continue;
     uint64_t* dst = peers.recv[peer] + ((int64_t)slot * p.world + p.rank) * p.part_words;
     for (int64_t i = threadIdx.x; i < npair; i += kCpThreads) {
@@ -115,8 +119,8 @@ __global__ void __launch_bounds__(kCpThreads)
   constexpr float to2 = 1.4426950408889634f;
   for (int64_t row = r0 + warp; row < r1; row += kCpThreads / 32) {
     auto lse_of = [&](int s) -> float {
-      return s == p.rank ? p.send[lse_off + row]
-                         : ll_take(slot_base + (int64_t)s * p.part_words + lse_off + row, epoch, start, fail);
+      return (s == p.rank && p.send) ? p.send[lse_off + row]
+                                     : ll_take(slot_base + (int64_t)s * p.part_words + lse_off + row, epoch, start, fail);
     };
     float M = -INFINITY;
     for (int s = lane; s < p.world; s += 32) M = fmaxf(M, lse_of(s) * to2);
@@ -133,7 +137,7 @@ __global__ void __launch_bounds__(kCpThreads)
         const float w = exp2f(ls - M);
         L += w;
         float v[PER];
-        if (s == p.rank) {
+        if (s == p.rank && p.send) {
 #pragma unroll
           for (int e = 0; e < PER; ++e) v[e] = p.send[row * D + lane * PER + e];
         } else {
@@ -169,7 +173,7 @@ int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world
                int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok, int32_t* error_word,
                cudaStream_t stream) {
   if (world < 1 || world > kCpMaxRanks || rank < 0 || rank >= world || rows < 1 || hq < 1 || rows % hq ||
-      (head_dim != 64 && head_dim != 128) || !send || !peer_recv || !out || !state ||
+      (head_dim != 64 && head_dim != 128) || !peer_recv || !out || !state ||
       (reinterpret_cast<uintptr_t>(state) & 7))
     return LKV_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(send) & 15) || out_stride_tok < (int64_t)hq * head_dim || (out_stride_tok % 2) ||

@@ -56,7 +56,65 @@ struct DecodeParams {
   int64_t num_pages;
   float scale_log2;  // softmax_scale * log2(e)
   int final_out;     // 1: this kernel writes `out` (S == 1 and not partial mode)
+  // Context parallel: the last CTA to finish a (sequence, KV head) unit merges its
+  // split partials and pushes the merged rows to every rank's receive buffer.
+  uint64_t* cp_recv[kCpMaxRanks];
+  uint32_t* cp_state;      // [0] epoch of the previous call, [2 + unit] arrivals (null: no push)
+  int64_t cp_part_words;   // words per rank partial in a receive slot
+  int cp_rank, cp_world;
 };
+
+// Exact LSE merge of one row's S partials (S <= 32): lane s holds part s's LSE,
+// so the accumulation loop has no load-dependent branch and its part loads are
+// all in flight at once.  Shared by merge_partials_kernel and the
+// context-parallel push, which must produce the same bits.
+//   part s of the row: o at o_base + s * o_step (D floats), LSE at lse_base + s * lse_step
+//   to2 converts the stored LSE to log2 units.  Returns this lane's D / 32
+//   weighted sums in acc (unnormalised), their normaliser in inv (1 / sum of
+//   weights, 0 when empty) and the log2 LSE in lse2.
+template <int D>
+__device__ __forceinline__ void merge_row_parts(const float* o_base, int64_t o_step, const float* lse_base,
+                                                int64_t lse_step, int S, float to2, int lane,
+                                                float (&acc)[D / 32], float& inv, float& lse2) {
+  constexpr int PER = D / 32;
+  const float my_ls = lane < S ? __ldcg(lse_base + lane * lse_step) * to2 : -INFINITY;
+  float M = my_ls;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+#pragma unroll
+  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+  float L = 0.f;
+  if (M != -INFINITY) {
+    const float my_w = my_ls == -INFINITY ? 0.f : exp2f(my_ls - M);
+#pragma unroll 4
+    for (int s = 0; s < S; ++s) {
+      const float w = __shfl_sync(0xffffffffu, my_w, s);
+      const float* src = o_base + s * o_step + lane * PER;
+      float v[PER];
+      if constexpr (PER == 4) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
+        v[0] = t.x;
+        v[1] = t.y;
+        v[2] = t.z;
+        v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) v[e] = __ldcg(src + e);
+      }
+      // a part with -inf LSE (w == 0) leaves L and acc untouched, whatever its o holds
+      const bool use = w != 0.f;
+      const float Ln = L + w;
+      L = use ? Ln : L;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const float an = acc[e] + w * v[e];
+        acc[e] = use ? an : acc[e];
+      }
+    }
+  }
+  inv = L > 0.f ? 1.f / L : 0.f;
+  lse2 = L > 0.f ? M + log2f(L) : -INFINITY;
+}
 
 template <int D, int NW, int STAGES>
 struct DecodeCfg {
@@ -68,7 +126,7 @@ struct DecodeCfg {
   static constexpr int DATA_BYTES = STAGES * STAGE_BYTES;
   // merge area after the ring: o [NW][4 heads][OSTRIDE], then m and l [NW][8]
   static constexpr int MERGE_BYTES = NW * 4 * OSTRIDE * 4 + 2 * NW * 8 * 4;
-  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + MERGE_BYTES + 2 * STAGES * 8 + 16;  // + failure flag
+  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + MERGE_BYTES + 2 * STAGES * 8 + 16;  // + failure / last flags
 };
 
 __device__ __forceinline__ float warp_max_g(float v) {
@@ -100,10 +158,13 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::DATA_BYTES + Cfg::MERGE_BYTES);
   uint64_t* empty = full + STAGES;
   volatile int* fail_flag = reinterpret_cast<volatile int*>(empty + STAGES);
+  volatile int* last_flag = fail_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
   pdl_wait();  // q, the appended keys and the tables come from the previous kernels
+  // this call's epoch (the combine launch that follows advances the stored one)
+  const uint32_t cp_epoch = p.cp_state ? __ldcg(p.cp_state) + 1u : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -339,6 +400,47 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       // the area (and mm / ml) is rewritten by the next chunk or item
       asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
     }
+    if (p.cp_state) {
+      // Context parallel: count this split; the unit's last CTA merges the S
+      // partials (merge_partials_kernel's arithmetic) and pushes the merged rows
+      // as {value, epoch} words into every rank's receive slot, as
+      // cp_combine_kernel's push would.
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+      uint32_t* arrivals = p.cp_state + 2 + (int64_t)b * p.Hkv + hk;
+      if (threadIdx.x == 0) *last_flag = atomicAdd(arrivals, 1u) == (uint32_t)(p.S - 1);
+      asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+      if (*last_flag) {
+        __threadfence();
+        const int64_t rows = (int64_t)p.B * p.Hq;
+        const int slot = (int)(cp_epoch & 1u);
+        for (int h = warp; h < GROUP; h += NW) {
+          const int64_t row = (int64_t)b * p.Hq + hk * GROUP + h;
+          float acc[D / 32];
+          float inv, lse2;
+          merge_row_parts<D>(p.part_o + row * p.S * D, D, p.part_lse + row * p.S, 1, p.S, 1.f, lane, acc, inv, lse2);
+#pragma unroll
+          for (int e = 0; e < D / 32; ++e) acc[e] = acc[e] * inv;  // as merge_partials_kernel's fp32 output
+          const float lse_e = lse2 * 0.6931471805599453f;
+          for (int r = 0; r < p.cp_world; ++r) {
+            uint64_t* dst = p.cp_recv[r] + ((int64_t)slot * p.cp_world + p.cp_rank) * p.cp_part_words;
+            uint64_t* od = dst + row * D + lane * (D / 32);
+#pragma unroll
+            for (int e = 0; e < D / 32; e += 2) {
+              const uint64_t w0 = ((uint64_t)cp_epoch << 32) | (uint64_t)__float_as_uint(acc[e]);
+              const uint64_t w1 = ((uint64_t)cp_epoch << 32) | (uint64_t)__float_as_uint(acc[e + 1]);
+              asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(od + e), "l"(w0), "l"(w1) : "memory");
+            }
+            if (lane == 0) {
+              const uint64_t wl = ((uint64_t)cp_epoch << 32) | (uint64_t)__float_as_uint(lse_e);
+              asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst + rows * D + row), "l"(wl) : "memory");
+            }
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+        if (threadIdx.x == 0) *arrivals = 0u;  // every split has arrived: ready for the next call
+      }
+    }
   }
 }
 
@@ -380,66 +482,37 @@ __global__ void __launch_bounds__(128) merge_partials_kernel(const MergeParams p
   auto o_at = [&](int s) -> const float* {
     return p.split_major ? p.part_o + (int64_t)s * p.o_part_stride + row * D : p.part_o + (row * p.S + s) * D;
   };
-  // With at most 32 parts, lane s holds part s's LSE, so the accumulation loop
-  // below has no load-dependent branch and its part loads can all be in flight
-  // at once; the arithmetic and its order are the same as the general loop.
-  const float my_ls = (p.S <= 32 && lane < p.S) ? lse_at(lane) : -INFINITY;
-  float M = my_ls;
-  for (int s = lane + 32; s < p.S; s += 32) M = fmaxf(M, lse_at(s));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   float acc[PER];
+  float inv = 0.f, lse2 = -INFINITY;
+  if (p.S <= 32) {
+    if (p.split_major)
+      merge_row_parts<D>(p.part_o + row * D, p.o_part_stride, p.part_lse + row, p.lse_part_stride, p.S, to2, lane,
+                         acc, inv, lse2);
+    else
+      merge_row_parts<D>(p.part_o + row * p.S * D, D, p.part_lse + row * p.S, 1, p.S, to2, lane, acc, inv, lse2);
+  } else {
+    // general path (more than 32 parts): the same arithmetic, one part at a time
+    float M = -INFINITY;
+    for (int s = lane; s < p.S; s += 32) M = fmaxf(M, lse_at(s));
 #pragma unroll
-  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-  float L = 0.f;
-  if (M != -INFINITY && p.S <= 32) {
-    const float my_w = my_ls == -INFINITY ? 0.f : exp2f(my_ls - M);
-#pragma unroll 4
-    for (int s = 0; s < p.S; ++s) {
-      const float w = __shfl_sync(0xffffffffu, my_w, s);
-      const float* src = o_at(s) + lane * PER;
-      float v[PER];
-      if constexpr (PER == 4) {
-        const float4 t = *reinterpret_cast<const float4*>(src);
-        v[0] = t.x;
-        v[1] = t.y;
-        v[2] = t.z;
-        v[3] = t.w;
-      } else {
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
 #pragma unroll
-        for (int e = 0; e < PER; ++e) v[e] = src[e];
-      }
-      // a part with -inf LSE (w == 0) leaves L and acc untouched, whatever its o holds
-      const bool use = w != 0.f;
-      const float Ln = L + w;
-      L = use ? Ln : L;
-#pragma unroll
-      for (int e = 0; e < PER; ++e) {
-        const float an = acc[e] + w * v[e];
-        acc[e] = use ? an : acc[e];
-      }
-    }
-  } else if (M != -INFINITY) {
-    for (int s = 0; s < p.S; ++s) {
-      const float ls = lse_at(s);
-      if (ls == -INFINITY) continue;
-      const float w = exp2f(ls - M);
-      L += w;
-      const float* src = o_at(s) + lane * PER;
-      if constexpr (PER == 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src);
-        acc[0] += w * v.x;
-        acc[1] += w * v.y;
-        acc[2] += w * v.z;
-        acc[3] += w * v.w;
-      } else {
+    for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+    float L = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < p.S; ++s) {
+        const float ls = lse_at(s);
+        if (ls == -INFINITY) continue;
+        const float w = exp2f(ls - M);
+        L += w;
+        const float* src = o_at(s) + lane * PER;
 #pragma unroll
         for (int e = 0; e < PER; ++e) acc[e] += w * src[e];
       }
     }
+    inv = L > 0.f ? 1.f / L : 0.f;
+    lse2 = L > 0.f ? M + log2f(L) : -INFINITY;
   }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  const float lse2 = L > 0.f ? M + log2f(L) : -INFINITY;
   const int h = (int)(row % p.Hq);
   const int64_t tok = row / p.Hq;
   if (p.out_f32) {
@@ -512,7 +585,8 @@ int choose_splits(int units, int max_pages, int slots) {
 
 template <int D, int GROUP, int STAGES>
 int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams prm, int max_pages, int smax, int dev,
-                 cudaStream_t stream, bool partial_mode, float* part_o_user, float* part_lse_user) {
+                 cudaStream_t stream, bool partial_mode, float* part_o_user, float* part_lse_user,
+                 const DecodeArgs* cp) {
   using Cfg = DecodeCfg<D, kNW, STAGES>;
   const int occ = prepare_kernel<D, GROUP, STAGES>(dev);
   if (occ < 0) return LKV_ERR_CUDA;
@@ -520,7 +594,7 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
   const int S = std::min(smax, choose_splits(prm.B * prm.Hkv, max_pages, slots));
   const int64_t rows = (int64_t)prm.B * prm.Hq;
   prm.S = S;
-  prm.final_out = (S == 1 && !partial_mode) ? 1 : 0;
+  prm.final_out = (S == 1 && !partial_mode && !cp) ? 1 : 0;
   const int64_t items = (int64_t)S * prm.Hkv * prm.B;
   if (items > INT_MAX) return LKV_ERR_UNSUPPORTED;
   dim3 grid((unsigned)std::min<int64_t>(items, slots));
@@ -528,6 +602,9 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
                  tmk, tmv, prm) != cudaSuccess)
     return LKV_ERR_CUDA;
   if (prm.final_out) return LKV_OK;
+  if (cp)  // every rank's merged rows are pushed: poll them and merge in rank order
+    return cp_combine(nullptr, cp->cp_recv, cp->cp_rank, cp->cp_world, cp->cp_state, rows, D, prm.Hq,
+                      cp->out_scale, cp->out, cp->out_stride_tok, cp->cp_error, stream);
   MergeParams mp{};
   mp.part_o = prm.part_o;
   mp.part_lse = prm.part_lse;
@@ -615,11 +692,18 @@ int decode_paged(const DecodeArgs& a) {
   if (smax < 1 && (partial_mode || a.max_pages_per_seq > 0)) return LKV_ERR_WORKSPACE;
   prm.part_lse = reinterpret_cast<float*>(ws);
   prm.part_o = reinterpret_cast<float*>(ws + (((size_t)rows * std::max(smax, 1) * sizeof(float) + 255) & ~size_t(255)));
+  if (a.cp_state) {
+    prm.cp_state = a.cp_state;
+    prm.cp_rank = a.cp_rank;
+    prm.cp_world = a.cp_world;
+    prm.cp_part_words = cp_part_words(rows, a.head_dim);
+    for (int r = 0; r < a.cp_world; ++r) prm.cp_recv[r] = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(a.cp_recv[r]));
+  }
 
   cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
 #define LKV_LAUNCH(DD, GG, SS) \
   return launch_group<DD, GG, SS>(tmk, tmv, prm, a.max_pages_per_seq, std::max(smax, 1), dev, stream, \
-                                  partial_mode, a.partial_o, a.partial_lse)
+                                  partial_mode, a.partial_o, a.partial_lse, a.cp_state ? &a : nullptr)
   if (a.head_dim == 128) {
     switch (group) {
       case 1: LKV_LAUNCH(128, 1, 3);
@@ -636,6 +720,19 @@ int decode_paged(const DecodeArgs& a) {
     }
   }
 #undef LKV_LAUNCH
+}
+
+// Sequence-sharded decode: this rank's keys with the merged rows pushed to every
+// rank (decode_splitkv_kernel, context-parallel push), then cp_combine_kernel
+// polling and merging the ranks' rows - two launches, no collective call.
+int decode_paged_cp(const DecodeArgs& a) {
+  if (a.cp_world < 1 || a.cp_world > kCpMaxRanks || a.cp_rank < 0 || a.cp_rank >= a.cp_world || !a.cp_recv ||
+      !a.cp_state || (reinterpret_cast<uintptr_t>(a.cp_state) & 7) || !a.out || a.partial_o || a.partial_lse)
+    return LKV_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < a.cp_world; ++r)
+    if (!a.cp_recv[r] || (a.cp_recv[r] & 15)) return LKV_ERR_INVALID_ARGUMENT;
+  if (a.out_stride_tok < (int64_t)a.num_q_heads * a.head_dim || (a.out_stride_tok % 2)) return LKV_ERR_INVALID_ARGUMENT;
+  return decode_paged(a);
 }
 
 int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspace_bytes, int partial, int* splits,

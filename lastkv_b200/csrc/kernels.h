@@ -65,6 +65,11 @@ struct DecodeArgs {
   void* workspace;
   size_t workspace_bytes;
   void* stream;
+  // context parallel (decode_paged_cp): every unit's merged partial is pushed to these receive buffers
+  const uint64_t* cp_recv = nullptr;  // host array of cp_world device addresses
+  int cp_rank = 0, cp_world = 0;
+  uint32_t* cp_state = nullptr;       // [0] epoch, [1] combine done counter, [2 + unit] unit arrivals
+  int32_t* cp_error = nullptr;
 };
 
 size_t decode_workspace_bytes(int batch, int hq, int d, int max_pages);
@@ -137,6 +142,8 @@ int argmax_rows(const void* x, int64_t row_stride, int rows, int cols, int64_t* 
 
 constexpr int kCpMaxRanks = 8;
 constexpr int kCpRowsPerCta = 4;
+// decode + push + combine for sequence-sharded decode (see decode.cu, cp_combine.cu)
+int decode_paged_cp(const DecodeArgs& a);
 int64_t cp_part_words(int64_t rows, int head_dim);
 int cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state, int64_t rows,
                int head_dim, int hq, const float* out_scale, void* out, int64_t out_stride_tok, int32_t* error_word,

@@ -439,6 +439,52 @@ def cp_combine_sizes(rows: int, head_dim: int, world: int) -> dict:
     return {"send_floats": a.value, "recv_words": b.value}
 
 
+def decode_cp_state_words(batch: int, num_kv_heads: int) -> int:
+    """uint32 words of device state lkv_decode_paged_cp needs (epoch, done counter, unit arrivals)."""
+    n = ctypes.c_int64(0)
+    _capi.check(_capi.lib().lkv_decode_cp_state_words(batch, num_kv_heads, ctypes.byref(n)),
+                "lkv_decode_cp_state_words")
+    return n.value
+
+
+def decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, recv_ptrs, rank: int, world: int, state, *,
+                    softmax_scale=None, out=None, out_scale=None, workspace: Workspace | None = None,
+                    max_pages: int | None = None, error_word=None):
+    """Sequence-sharded decode with the exchange fused into the decode kernel (lkv_decode_paged_cp):
+    this rank's slice of the keys, every unit's merged rows pushed to every rank's receive
+    buffer as the unit finishes, then the poll-and-merge launch.  state: int32 device tensor
+    of decode_cp_state_words(B, Hkv) words, zero before the first call.  Returns out bf16 [B, Hq, D]."""
+    _check_pool(pool_k, pool_v)
+    B, Hq, D = q.shape
+    Hkv = pool_k.shape[2]
+    require_heads(Hq, Hkv, D)
+    _require(q.dtype == torch.bfloat16 and q.stride(2) == 1 and q.stride(1) == D, "q must be bf16 [B, Hq, D] rows")
+    _require(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.stride(1) == 1,
+             "block_table must be int32 [B, W] with unit column stride")
+    _require(len(recv_ptrs) == world, "one receive buffer per rank")
+    _require(state.dtype == torch.int32 and state.is_cuda and state.numel() >= decode_cp_state_words(B, Hkv),
+             "state must be int32 [decode_cp_state_words(B, Hkv)]")
+    W = int(max_pages if max_pages is not None else block_table.shape[1])
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    if workspace is None:
+        workspace = Workspace.for_decode(B, Hq, D, W, device=q.device)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    _require(out.dtype == torch.bfloat16 and out.stride(-1) == 1 and out.stride(-2) == D, "out layout")
+    if out_scale is not None:
+        _require(out_scale.dtype == torch.float32 and out_scale.numel() == Hq and out_scale.is_contiguous(),
+                 "out_scale must be fp32 [Hq]")
+    rp = (ctypes.c_uint64 * world)(*recv_ptrs)
+    st = _capi.lib().lkv_decode_paged_cp(
+        q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
+        block_table.stride(0), seq_k.data_ptr(), out.data_ptr(), out.stride(0), _ptr(out_scale), B, Hq, Hkv, D, W,
+        float(softmax_scale), workspace.ptr(), workspace.nbytes, rp, rank, world, state.data_ptr(),
+        _ptr(error_word), _stream())
+    _capi.check(st, "lkv_decode_paged_cp")
+    return out
+
+
 def cp_combine(send, recv_ptrs, rank: int, world: int, state, rows: int, head_dim: int, hq: int, *,
                out_scale=None, out=None, error_word=None):
     """Push this rank's packed partial to every peer over peer memory, wait for theirs,
@@ -446,17 +492,18 @@ def cp_combine(send, recv_ptrs, rank: int, world: int, state, rows: int, head_di
     addresses valid on this GPU; state: int32 [2] device tensor, zero before the first
     call (the call's epoch advances on the device, so calls can be graph-captured).
     Returns out bf16 [rows / hq, hq, head_dim]."""
-    _require(send.dtype == torch.float32 and send.is_contiguous() and send.is_cuda, "send must be contiguous fp32")
+    _require(send is None or (send.dtype == torch.float32 and send.is_contiguous() and send.is_cuda),
+             "send must be contiguous fp32 (or None: rows already pushed)")
     _require(len(recv_ptrs) == world, "one receive buffer per rank")
     _require(state.dtype == torch.int32 and state.numel() >= 2 and state.is_cuda, "state must be int32 [2]")
     if out is None:
-        out = torch.empty((rows // hq, hq, head_dim), dtype=torch.bfloat16, device=send.device)
+        out = torch.empty((rows // hq, hq, head_dim), dtype=torch.bfloat16, device=state.device)
     _require(out.dtype == torch.bfloat16 and out.stride(-1) == 1 and out.stride(-2) == head_dim, "out layout")
     if out_scale is not None:
         _require(out_scale.dtype == torch.float32 and out_scale.numel() == hq and out_scale.is_contiguous(),
                  "out_scale must be fp32 [hq]")
     rp = (ctypes.c_uint64 * world)(*recv_ptrs)
-    st = _capi.lib().lkv_cp_combine(send.data_ptr(), rp, rank, world, state.data_ptr(), rows, head_dim, hq,
+    st = _capi.lib().lkv_cp_combine(_ptr(send), rp, rank, world, state.data_ptr(), rows, head_dim, hq,
                                     _ptr(out_scale), out.data_ptr(), out.stride(0), _ptr(error_word), _stream())
     _capi.check(st, "lkv_cp_combine")
     return out

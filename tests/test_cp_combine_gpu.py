@@ -71,3 +71,31 @@ def test_missing_peer_times_out_into_error_word():
     np.testing.assert_array_equal(vals, o.flatten().cpu().numpy())
     # the context is still usable
     assert float(torch.ones(4, device="cuda").sum()) == 4.0
+
+
+def test_fused_decode_push_equals_partial_merge_path():
+    """lkv_decode_paged_cp on one rank (the decode kernel merges each unit's splits and
+    pushes the rows into the receive buffer; the combine only polls and merges) equals
+    decode partial + merge of the packed parts bit for bit, over several calls (epochs)."""
+    from lastkv_b200 import ops
+    from tests.gpu_helpers import make_paged_case
+
+    B, Hq, Hkv, D = 4, 32, 8, 128
+    t, _ = make_paged_case(31, B, Hq, Hkv, D, [3000, 17, 900, 2048])
+    scale = torch.rand(Hq, device="cuda") + 0.5
+    rows = B * Hq
+    sizes = ops.cp_combine_sizes(rows, D, 1)
+    recv = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
+    state = torch.zeros(ops.decode_cp_state_words(B, Hkv), dtype=torch.int32, device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws = ops.Workspace.for_decode(B, Hq, D, t["bt"].shape[1], device="cuda")
+    po, pl = ops.decode_paged(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], partial=True)
+    ref = ops.merge_partials(po.view(1, B, Hq, D), pl.view(1, B, Hq), out_scale=scale)
+    for call in range(3):
+        got = ops.decode_paged_cp(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], [recv.data_ptr()], 0, 1,
+                                  state, out_scale=scale, workspace=ws, error_word=err)
+        torch.cuda.synchronize()
+        assert err.cpu().tolist() == [0, 0, 0, 0]
+        torch.testing.assert_close(got.view(B, Hq, D), ref.view(B, Hq, D), rtol=0, atol=0)
+        st = state.cpu().tolist()
+        assert st[0] == call + 1 and st[1] == 0 and all(v == 0 for v in st[2:]), st  # arrivals reset
