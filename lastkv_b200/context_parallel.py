@@ -126,6 +126,9 @@ class ContextParallelDecode:
         return st
 
     def check_errors(self):
+        """Raise if a device-side wait gave up (a peer did not push in time).  The ranks'
+        epoch and arrival state is then inconsistent: rebuild this object on every rank
+        (fresh, zeroed state and receive buffers) before the next layer call."""
         for st in self._p2p.values():
             e = st["error"].cpu().tolist()
             if e[0]:
