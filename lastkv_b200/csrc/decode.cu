@@ -209,7 +209,19 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       for (int i = blockIdx.x; ok && i < n_items; i += gridDim.x) {
         const Item w = item_at(i);
         const int32_t* row = p.bt + (int64_t)w.b * p.bt_stride;
+        // Page ids of a stage are loaded together (one L2 round trip, not one per
+        // page), and the next stage's before waiting for a free slot.
+        int ids[NW];
+#pragma unroll
+        for (int k = 0; k < NW; ++k) ids[k] = (w.p0 + k < w.p1) ? __ldg(row + w.p0 + k) : 0;
         for (int it = 0; it < w.n_iter; ++it, ++gs) {
+          const int first = w.p0 + it * NW;
+          const int cnt = min(NW, w.p1 - first);
+          int cur[NW];
+#pragma unroll
+          for (int k = 0; k < NW; ++k) cur[k] = ids[k];
+#pragma unroll
+          for (int k = 0; k < NW; ++k) ids[k] = (first + NW + k < w.p1) ? __ldg(row + first + NW + k) : 0;
           const int s = (int)(gs % STAGES);
           const uint32_t ph = (gs / STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u)) {
@@ -217,12 +229,12 @@ __global__ void __launch_bounds__((NW + 1) * 32)
             ok = false;
             break;
           }
-          const int first = w.p0 + it * NW;
-          const int cnt = min(NW, w.p1 - first);
           mbar_arrive_expect_tx(&full[s], (uint32_t)(cnt * Cfg::PAGE_BYTES));
           uint8_t* dst = smem + s * Cfg::STAGE_BYTES;
-          for (int k = 0; k < cnt; ++k) {
-            const int pid = row[first + k];
+#pragma unroll
+          for (int k = 0; k < NW; ++k) {
+            if (k >= cnt) break;
+            const int pid = cur[k];
             if (pid < 0 || (int64_t)pid >= p.num_pages) report_error(p.err, DEVERR_BAD_PAGE, 1, pid);
             // An out-of-range page reads as zeros (TMA bounds-fills), never faults.
 #pragma unroll
