@@ -45,10 +45,10 @@ def algo_bytes() -> int:
 
 
 # DRAM read + write bytes of one full-size decode_splitkv launch (config 2): reads
-# 268,544,000 per 8 sequences in the small-case capture (x 8 = 2,148,352,000; the
-# full-size one-pass capture reads 2.15 GB), writes 4.95 MB in the full-size capture
+# 268,564,736 per 8 sequences in the small-case capture (x 8 = 2,148,517,888; the
+# full-size one-pass capture reads 2.15 GB), writes 5.18 MB in the full-size capture
 # (the split partials that leave L2 during the launch).
-NCU_FULL_TRAFFIC = 2_148_352_000 + 4_950_000
+NCU_FULL_TRAFFIC = 2_148_517_888 + 5_180_000
 
 
 def traffic_per_launch() -> int:
