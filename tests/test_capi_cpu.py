@@ -45,6 +45,15 @@ def test_host_only_entry_points(lib):
     small = lib.lkv_decode_workspace_bytes(1, 4, 128, 1)
     big = lib.lkv_decode_workspace_bytes(64, 32, 128, 512)
     assert 256 < small < big
+    # context-parallel state: epoch, done counter, one arrival counter per (sequence, KV head)
+    import ctypes
+
+    words = ctypes.c_int64(0)
+    assert lib.lkv_decode_cp_state_words(4, 8, ctypes.byref(words)) == 0 and words.value == 2 + 32
+    assert lib.lkv_decode_cp_state_words(0, 8, ctypes.byref(words)) == 1
+    send, recv = ctypes.c_int64(0), ctypes.c_int64(0)
+    assert lib.lkv_cp_combine_sizes(128, 128, 8, ctypes.byref(send), ctypes.byref(recv)) == 0
+    assert recv.value == 2 * 8 * (128 * 129)  # two epoch slots x ranks x {value, epoch} words per float
 
 
 def test_argument_validation_needs_no_gpu(lib):
@@ -60,6 +69,12 @@ def test_argument_validation_needs_no_gpu(lib):
     # empty batch is a no-op
     assert lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
                                 0, 8, 8, 128, 1, 1.0, None, 0, None) == 0
+    # the fused context-parallel decode needs its peers and state: rejected before any CUDA call
+    assert lib.lkv_decode_paged_cp(None, 0, None, None, 1, None, 0, None, None, 0, None, 2, 8, 8, 128, 1, 1.0,
+                                   None, 0, None, 0, 2, None, None, None) == 1
+    # the key-split prefill validates its shape first (head_dim 96 is unsupported)
+    assert lib.lkv_prefill_paged_split(None, 0, None, None, 1, None, 0, None, None, None, 0, None, None,
+                                       1, 1, 1, 8, 8, 96, 1, 1.0, 2, None, None, None, None) == 2
 
 
 def test_product_package_never_imports_oracle():
