@@ -30,6 +30,7 @@ device buffers only and is CUDA-graph capturable.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -191,6 +192,11 @@ class SharedKVFastPath:
         self.batch = self.tokens = self.max_q = 0
         self.uniform = True
         self.active = False
+        # RMARIN_MERGED_CHECK=1 (the reference's switch, fastpath.py:199-203): recompute every
+        # layer two-pass from the same pool and report the deviation (eager diagnostics only)
+        self.check = os.environ.get("RMARIN_MERGED_CHECK") == "1"
+        self.check_steps = 0
+        self.check_log: list[dict] = []
 
     def register_layers(self, norm_weights, cos_sin_cache: torch.Tensor, eps: float) -> None:
         """Per-layer (q_norm.weight, k_norm.weight) and the bf16 [max_pos, D] cos|sin cache
@@ -331,7 +337,48 @@ class SharedKVFastPath:
             ops.prefill_paged(q, pool.pool_k, pool.pool_v, self.bt_all[layer_index, :B], self.seq_k[:B],
                               self.cu_q[:B + 1], self.max_q, softmax_scale=self.scale, out=out,
                               out_scale=pool.out_scale[layer_index], error_word=self.error_word, max_pages=self.W)
+        if self.check:
+            self.merged_check(layer_index, q, out)
         return output
+
+    def merged_check(self, layer_index: int, q, out) -> dict:
+        """Two-pass recomputation of one layer from the same pool (the reference's
+        _merged_check_impl, fastpath.py:737-766): causal attention over the layer's ring
+        pages, non-causal attention over the older shared pages, LSE merge (x s_l); the
+        relative L2 deviation of the merged single call from it is logged and printed for
+        the first 192 layer calls and whenever it exceeds 0.02."""
+        pool, B, T = self.pool, self.batch, self.tokens
+        bt = self.bt_all[layer_index, :B]
+        nsrc = self.nsrc[:B]
+        seqk = self.seq_k[:B]
+        cu = self.cu_q[:B + 1]
+        idx = (nsrc.unsqueeze(1).long() + torch.arange(pool.ring_pages, device=bt.device).unsqueeze(0)).clamp_(
+            max=self.W - 1)
+        bt_loc = torch.gather(bt, 1, idx).to(torch.int32).contiguous()
+        seq_loc = (seqk - nsrc * PAGE_SIZE).to(torch.int32)
+        seq_src = torch.clamp(nsrc * PAGE_SIZE, min=1).to(torch.int32)
+        lse_loc = torch.empty((T, self.hq), dtype=torch.float32, device=q.device)
+        lse_src = torch.empty_like(lse_loc)
+        lo = ops.prefill_paged(q, pool.pool_k, pool.pool_v, bt_loc, seq_loc, cu, self.max_q, causal=True,
+                               softmax_scale=self.scale, lse=lse_loc, error_word=self.error_word,
+                               max_pages=pool.ring_pages, kv_splits=1)
+        so = ops.prefill_paged(q, pool.pool_k, pool.pool_v, bt.contiguous(), seq_src, cu, self.max_q, causal=False,
+                               softmax_scale=self.scale, lse=lse_src, error_word=self.error_word,
+                               max_pages=self.W, kv_splits=1)
+        # sequences without older shared pages: the source pass saw a placeholder key
+        tok_seq = torch.repeat_interleave(torch.arange(B, device=q.device), (cu[1:] - cu[:-1]).long(),
+                                          output_size=T)
+        lse_src.masked_fill_((nsrc[tok_seq] == 0).unsqueeze(1), float("-inf"))
+        ref = ops.merge_partials(torch.stack([so.float(), lo.float()]), torch.stack([lse_src, lse_loc]),
+                                 out_scale=pool.out_scale[layer_index])
+        diff = float((ref.float() - out.float()).norm() / ref.float().norm().clamp(min=1e-6))
+        self.check_steps += 1
+        rec = {"layer": layer_index, "batch": B, "tokens": T, "rel": round(diff, 5),
+               "out_absmax": round(float(out.float().abs().max()), 2), "ref_absmax": round(float(ref.float().abs().max()), 2)}
+        self.check_log.append(rec)
+        if self.check_steps <= 32 * 6 or diff > 0.02:
+            print({"rmarin_merged_check": rec}, flush=True)
+        return rec
 
     def check_errors(self) -> None:
         e, w = self.error_word.cpu().tolist(), self.workspace.error()

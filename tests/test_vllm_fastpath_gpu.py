@@ -110,3 +110,35 @@ def test_mixed_prefill_decode_schedule_matches_oracle():
         step += 1
     fast.check_errors()
     assert step > 10
+
+
+def test_merged_check_switch_reports_two_pass_agreement(small_d128, monkeypatch, capsys):
+    """RMARIN_MERGED_CHECK=1 (the reference's diagnostic switch): every layer call is recomputed
+    two-pass (ring pages causal + older shared pages non-causal + LSE merge) and the deviation of
+    the merged single call is reported; on the recorded calls it stays at bf16 rounding."""
+    from lastkv_b200.vllm_backend import Span, rope_cos_sin_cache
+
+    monkeypatch.setenv("RMARIN_MERGED_CHECK", "1")
+    data = small_d128
+    L, C = int(data["num_layers"]), int(data["chunk"])
+    hq, hkv, d = int(data["num_heads"]), int(data["num_kv_heads"]), int(data["head_dim"])
+    B, T = data["tokens"].shape
+    pool, fast = _fast(L, B, T, C, hkv, hq, d, np.random.default_rng(3).permutation(B * (-(-T // 16))))
+    assert fast.check
+    pool.bind_parameters(torch.from_numpy(data["alpha_logits"]), torch.from_numpy(data["v_scale"]), hq)
+    fast.register_layers([(torch.from_numpy(data["q_norm_w"][l]).cuda(), torch.from_numpy(data["k_norm_w"][l]).cuda())
+                          for l in range(L)], rope_cos_sin_cache(T, d, float(data["rope_theta"])), float(data["eps"]))
+    for rec in golden_calls(data):
+        layer, start, lq = rec["layer"], rec["start"], rec["lq"]
+        if layer == 0:
+            assert fast.prepare([Span(b, start, lq) for b in range(B)])
+        q = torch.from_numpy(rec["q_proj"].reshape(B * lq, hq * d)).cuda().bfloat16()
+        k = torch.from_numpy(rec["k_proj"].reshape(B * lq, hkv * d)).cuda().bfloat16()
+        v = torch.from_numpy(rec["v_proj"].reshape(B * lq, hkv * d)).cuda().bfloat16()
+        out = torch.empty((B * lq, hq, d), dtype=torch.bfloat16, device="cuda")
+        fast.run_layer(layer, q, k, v, out)
+    fast.check_errors()
+    assert len(fast.check_log) == int(data["calln"])
+    worst = max(r["rel"] for r in fast.check_log)
+    assert worst < 0.02, fast.check_log
+    assert "rmarin_merged_check" in capsys.readouterr().out
