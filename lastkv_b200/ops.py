@@ -9,6 +9,8 @@ the caller passes ``out``/``workspace`` buffers.
 from __future__ import annotations
 
 import ctypes
+import functools
+import os
 
 import torch
 
@@ -27,6 +29,24 @@ def _stream():
 def _require(cond: bool, msg: str) -> None:
     if not cond:
         raise RMarinBackendContractError(msg)
+
+
+# LKV_NVTX=1: every kernel-launching op runs inside an NVTX range "lkv.<op>" (for timeline
+# and ncu --nvtx captures); off by default, so the ops carry no range overhead.
+_NVTX = os.environ.get("LKV_NVTX") == "1"
+
+
+def _traced(fn):
+    if not _NVTX:
+        return fn
+    name = "lkv." + fn.__name__
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        with torch.cuda.nvtx.range(name):
+            return fn(*args, **kwargs)
+
+    return wrapper
 
 
 def _check_pool(pool_k, pool_v):
@@ -65,6 +85,7 @@ class Workspace:
         _capi.check(_capi.lib().lkv_clear_error_word(self.ptr(), _stream()), "lkv_clear_error_word")
 
 
+@_traced
 def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, out=None, lse=None,
                  out_scale=None, workspace: Workspace | None = None, max_pages: int | None = None,
                  partial: bool = False, partial_out=None):
@@ -132,6 +153,7 @@ def prefill_split_plan(batch, max_q, num_q_heads, num_kv_heads, head_dim, max_pa
     return s.value
 
 
+@_traced
 def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, causal=True, softmax_scale=None,
                   out=None, lse=None, out_scale=None, error_word=None, max_pages: int | None = None,
                   kv_splits: int | None = None, partials=None):
@@ -195,6 +217,7 @@ def prefill_paged(q, pool_k, pool_v, block_table, seq_k, cu_q, max_q: int, *, ca
     return out
 
 
+@_traced
 def merge_partials(o_parts, lse_parts, *, out_scale=None, out=None, lse_out=None):
     """LSE-merge P partials: o_parts fp32 [P, T, Hq, D], lse_parts fp32 [P, T, Hq]."""
     P_, T, Hq, D = o_parts.shape
@@ -209,6 +232,7 @@ def merge_partials(o_parts, lse_parts, *, out_scale=None, out=None, lse_out=None
     return out
 
 
+@_traced
 def merge_partials_packed(parts, T: int, Hq: int, D: int, *, out_scale=None, out=None, lse_out=None):
     """LSE-merge parts packed as [P, T*Hq*D (o) | T*Hq (lse) | pad] fp32 rows (one all-gather buffer)."""
     P_ = parts.shape[0]
@@ -225,6 +249,7 @@ def merge_partials_packed(parts, T: int, Hq: int, D: int, *, out_scale=None, out
     return out
 
 
+@_traced
 def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_scale, ring_slot, ring_k, ring_v,
                      src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None, interleaved=False):
     """Fused RoPE -> Q/K RMSNorm -> V/s -> paged append for one layer.
@@ -264,6 +289,7 @@ def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_s
     return q_out
 
 
+@_traced
 def gather_blend(pool_k, pool_v, dst, src_a, src_b, alpha_row, alpha, *, error_word=None):
     """Token-level copy / blend on the flat pool (see lkv_gather_blend).
 
@@ -283,6 +309,7 @@ def gather_blend(pool_k, pool_v, dst, src_a, src_b, alpha_row, alpha, *, error_w
     _capi.check(st, "lkv_gather_blend")
 
 
+@_traced
 def blend_chunk(pool_k, pool_v, raw_pages, ring_pages, ring_layer_stride: int, alpha, *, error_word=None):
     """Commit a finished chunk into every layer ring (K and V/s) in place.
 
@@ -301,6 +328,7 @@ def blend_chunk(pool_k, pool_v, raw_pages, ring_pages, ring_layer_stride: int, a
     _capi.check(st, "lkv_blend_chunk")
 
 
+@_traced
 def build_layer_block_tables(block_table, nsrc, ring_base, out=None):
     """bt_all [L, B, W] from [older | layer-relative ring] rows (fastpath.py:422-424)."""
     B, W = block_table.shape
@@ -322,6 +350,7 @@ def _rows2d(t, name):
     return t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
 
 
+@_traced
 def rmsnorm(x, weight, eps: float, residual=None, *, out=None, residual_out=None):
     """RMSNorm over the last dim, optionally after the residual add h = x + residual.
 
@@ -355,6 +384,7 @@ def rmsnorm(x, weight, eps: float, residual=None, *, out=None, residual_out=None
     return out if residual is None else (residual_out, out)
 
 
+@_traced
 def silu_mul(gate_up, *, out=None):
     """bf16(bf16(silu(gate)) * up) for rows [gate | up] of width 2F; returns [..., F]."""
     F2 = gate_up.shape[-1]
@@ -370,6 +400,7 @@ def silu_mul(gate_up, *, out=None):
     return out
 
 
+@_traced
 def argmax_rows(logits, *, out=None):
     """torch.argmax(logits, -1) for bf16 rows (first index on ties, NaN largest), int64 [rows]."""
     x2 = _rows2d(logits, "logits")
@@ -405,6 +436,7 @@ def decode_gemm_plan(n_rows: int, k: int, silu_mul: bool = False) -> dict:
     return {"tiles": t.value, "splits": s.value, "ctas_per_sm": o.value}
 
 
+@_traced
 def decode_gemm(x, weight, *, silu_mul: bool = False, out=None, error_word=None):
     """``x @ weight.T`` for 1..16 rows of x (decode) on tcgen05, bf16 out.
 
@@ -447,6 +479,7 @@ def decode_cp_state_words(batch: int, num_kv_heads: int) -> int:
     return n.value
 
 
+@_traced
 def decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, recv_ptrs, rank: int, world: int, state, *,
                     softmax_scale=None, out=None, out_scale=None, workspace: Workspace | None = None,
                     max_pages: int | None = None, error_word=None):
@@ -485,6 +518,7 @@ def decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, recv_ptrs, rank: int,
     return out
 
 
+@_traced
 def cp_combine(send, recv_ptrs, rank: int, world: int, state, rows: int, head_dim: int, hq: int, *,
                out_scale=None, out=None, error_word=None):
     """Push this rank's packed partial to every peer over peer memory, wait for theirs,

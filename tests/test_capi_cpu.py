@@ -123,3 +123,22 @@ def test_integration_bindings_match_the_abi():
                 assert len(node.args) == len(_capi._SIGNATURES[name][1]), (name, len(node.args))
                 seen += 1
     assert seen >= 4
+
+
+def test_nvtx_ranges_are_opt_in():
+    """LKV_NVTX=1 wraps every kernel-launching op in an NVTX range; without it the ops are
+    the plain functions (no per-call range overhead)."""
+    import subprocess
+    import sys
+
+    code = ("import lastkv_b200.ops as o; "
+            "names = ['decode_paged', 'prefill_paged', 'rope_norm_append', 'decode_gemm', 'decode_paged_cp']; "
+            "print(sum(hasattr(getattr(o, n), '__wrapped__') for n in names))")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PYTHONPATH=root)
+    env.pop("LKV_NVTX", None)
+    off = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, cwd=root)
+    on = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=dict(env, LKV_NVTX="1"),
+                        cwd=root)
+    assert off.stdout.strip() == "0", off.stderr
+    assert on.stdout.strip() == "5", on.stderr
