@@ -162,9 +162,9 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
-  pdl_wait();  // q, the appended keys and the tables come from the previous kernels
-  // this call's epoch (the combine launch that follows advances the stored one)
-  const uint32_t cp_epoch = p.cp_state ? __ldcg(p.cp_state) + 1u : 0u;
+  // Programmatic dependent launch: q, the epoch and each sequence's newest key
+  // (appended by the previous kernel) are read only after pdl_wait(); the
+  // producer may request the first stages of older pages before it.
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -204,17 +204,60 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
       const uint64_t policy = policy_evict_first();
-      uint32_t gs = 0;
+      // Before waiting for the previous kernel: the first item's first stages
+      // (fresh slots, so no empty-slot wait), as long as a stage holds neither
+      // the sequence's last page - where the previous kernel may just have
+      // appended this step's key - nor a page id that would need an error report
+      // (a global write, which must follow the wait).  The sequence lengths and
+      // block tables are inputs of the step, not outputs of the previous kernel.
+      int pre = 0;
+      if ((int)blockIdx.x < n_items) {
+        const Item w = item_at(blockIdx.x);
+        const int32_t* row = p.bt + (int64_t)w.b * p.bt_stride;
+        const int last_page = min((w.n + PAGE - 1) / PAGE, p.W) - 1;
+        for (; pre < STAGES && pre < w.n_iter; ++pre) {
+          const int first = w.p0 + pre * NW;
+          const int cnt = min(NW, w.p1 - first);
+          if (first + cnt - 1 >= last_page) break;
+          int cur[NW];
+          bool good = true;
+#pragma unroll
+          for (int k = 0; k < NW; ++k) {
+            cur[k] = k < cnt ? __ldg(row + first + k) : 0;
+            good = good && (k >= cnt || (cur[k] >= 0 && (int64_t)cur[k] < p.num_pages));
+          }
+          if (!good) break;
+          mbar_arrive_expect_tx(&full[pre], (uint32_t)(cnt * Cfg::PAGE_BYTES));
+          uint8_t* dst = smem + pre * Cfg::STAGE_BYTES;
+#pragma unroll
+          for (int k = 0; k < NW; ++k) {
+            if (k >= cnt) break;
+#pragma unroll
+            for (int h = 0; h < Cfg::HALVES; ++h) {
+              tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + h * Cfg::TILE_BYTES, &tmk, &full[pre], h * 64, w.hk, 0,
+                               cur[k], policy);
+              tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + (Cfg::HALVES + h) * Cfg::TILE_BYTES, &tmv, &full[pre],
+                               h * 64, w.hk, 0, cur[k], policy);
+            }
+          }
+        }
+      }
+      pdl_wait();
+      uint32_t gs = (uint32_t)pre;
       bool ok = true;
       for (int i = blockIdx.x; ok && i < n_items; i += gridDim.x) {
         const Item w = item_at(i);
         const int32_t* row = p.bt + (int64_t)w.b * p.bt_stride;
+        const int it0 = i == (int)blockIdx.x ? pre : 0;  // stages already requested above
         // Page ids of a stage are loaded together (one L2 round trip, not one per
         // page), and the next stage's before waiting for a free slot.
         int ids[NW];
 #pragma unroll
-        for (int k = 0; k < NW; ++k) ids[k] = (w.p0 + k < w.p1) ? __ldg(row + w.p0 + k) : 0;
-        for (int it = 0; it < w.n_iter; ++it, ++gs) {
+        for (int k = 0; k < NW; ++k) {
+          const int pg = w.p0 + it0 * NW + k;
+          ids[k] = pg < w.p1 ? __ldg(row + pg) : 0;
+        }
+        for (int it = it0; it < w.n_iter; ++it, ++gs) {
           const int first = w.p0 + it * NW;
           const int cnt = min(NW, w.p1 - first);
           int cur[NW];
@@ -252,6 +295,9 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   }
 
   // -------------------------------------------------------------- consumers
+  pdl_wait();
+  // this call's epoch (the combine launch that follows advances the stored one)
+  const uint32_t cp_epoch = p.cp_state ? __ldcg(p.cp_state) + 1u : 0u;
   const int g = lane >> 2, c = lane & 3;
   // ldmatrix source rows/chunks (see the fragment derivation in the header comment)
   const uint32_t k_row = (lane & 7) + ((lane >> 3) & 1) * 8, k_chunk_hi = lane >> 4;
