@@ -76,11 +76,14 @@ int lkv_clear_error_word(int32_t* error_word, void* stream);
  * natural-log LSE [batch, num_q_heads] for a later lkv_merge_partials (the
  * context-parallel combine); `out`, `lse` and `out_scale` are then ignored.
  * Supported: head_dim 64 or 128; num_q_heads / num_kv_heads in {1, 2, 4, 8}.
- * The kernel is launched with programmatic dependent launch and may start
- * reading a sequence's pages before the stream's preceding kernel has
- * finished, all but its last page (where an append kernel just before it puts
- * this step's key); q, seq_k and the block table it reads only after.  So a
- * kernel right before this call may write the last pages, not older ones.
+ * The kernel is launched with programmatic dependent launch: before the
+ * stream's preceding kernel has finished it may already read seq_k, the block
+ * table and every page of a sequence but its last (where an append kernel just
+ * before it puts this step's key); q, the last pages and the workspace it
+ * touches only after.  A kernel right before this call may therefore write q
+ * and the last pages, but seq_k, the block table and older pages must be
+ * complete before it (written by a copy or an ordinary launch, as every
+ * caller in this library does).
  */
 size_t lkv_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int max_pages_per_seq);
 
