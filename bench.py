@@ -133,6 +133,47 @@ def cpu_tokens_per_s(layer_step_s: float, batch: int) -> float:
     return batch / (CFG["layers"] * layer_step_s)
 
 
+# ----------------------------------------------------------------- output check
+
+# bf16 tolerance of the parity tests (attention outputs vs an fp32/float64 recomputation)
+PARITY_TOL = {"max_abs": 2e-2, "rel_l2": 1e-2}
+
+
+def torch_ref_rows(q_rows, pool_k, pool_v, bt_row, n_keys, scale, out_scale=None):
+    """fp32 torch attention of query rows q_rows [R, Hq, D] of one sequence against its
+    paged keys; row r sees keys [0, n_keys[r]) (the bench's own outputs are checked
+    against this after its timed region)."""
+    import torch
+
+    R, Hq, D = q_rows.shape
+    Hkv = pool_k.shape[2]
+    n_max = int(max(n_keys))
+    pages = bt_row[: -(-n_max // 16)].long()
+    k = pool_k[pages].float().reshape(-1, Hkv, D)[:n_max]
+    v = pool_v[pages].float().reshape(-1, Hkv, D)[:n_max]
+    qg = q_rows.float().view(R, Hkv, Hq // Hkv, D)
+    s = torch.einsum("rhgd,khd->rhgk", qg, k) * scale
+    n = torch.as_tensor(list(n_keys), device=s.device).view(R, 1, 1, 1)
+    s = s.masked_fill(torch.arange(n_max, device=s.device).view(1, 1, 1, -1) >= n, float("-inf"))
+    o = torch.einsum("rhgk,khd->rhgd", torch.softmax(s, dim=-1), v).reshape(R, Hq, D)
+    if out_scale is not None:
+        o = o * out_scale.float().view(1, Hq, 1)
+    return o
+
+
+def parity_summary(pairs) -> dict:
+    """max-abs and relative L2 over (got, want) pairs of tensors, against PARITY_TOL."""
+    import torch
+
+    got = torch.cat([g.float().reshape(-1) for g, _ in pairs])
+    want = torch.cat([w.float().reshape(-1) for _, w in pairs])
+    max_abs = float((got - want).abs().max())
+    rel = float((got - want).norm() / want.norm().clamp_min(1e-12))
+    return {"max_abs": max_abs, "rel_l2": rel, "values": int(got.numel()), "tolerance": PARITY_TOL,
+            "pass": bool(max_abs <= PARITY_TOL["max_abs"] and rel <= PARITY_TOL["rel_l2"]),
+            "reference": "torch fp32 recomputation of sampled rows on the same bf16 inputs"}
+
+
 # ----------------------------------------------------------------- clocks
 
 
@@ -153,9 +194,17 @@ class ClockSampler:
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # nvidia-smi takes about a second to print its first sample, as long as a
+        # short timed region: wait for it so the samples cover the region
+        t_end = time.perf_counter() + 5.0
+        while time.perf_counter() < t_end and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -287,6 +336,14 @@ def measure_prefill(device, reps: int = 5, batch: int | None = None):
     last_flops = prefill_flops(N - C, C, B, Hq, D)
     if err.cpu().tolist()[0] != 0:
         raise RuntimeError(f"prefill device error word set: {err.cpu().tolist()}")
+    # out holds the last span (7168 keys of history + 1024 causal queries): sampled tokens
+    toks = torch.tensor([0, 1, 255, 512, C - 1], device=device)
+    pairs = []
+    for b in sorted({0, B - 1}):
+        rows = b * C + toks
+        want = torch_ref_rows(q[rows], pool_k, pool_v, bt[b], (N - C + toks + 1).tolist(), D ** -0.5)
+        pairs.append((out[rows], want))
+    parity = dict(parity_summary(pairs), rows="last span, 2 sequences x 5 tokens, all heads")
     try:
         peak = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["bf16_tflops"])
         src = "measured (burst)"
@@ -297,7 +354,7 @@ def measure_prefill(device, reps: int = 5, batch: int | None = None):
     return {"workload": f"chunked prefill attention, 1 layer, batch {B} x 8192-token prompt as 8 x 1024-token spans, "
                         "32/8 heads, D 128, shuffled pages", "ms_per_layer": ms, "flops_per_layer": flops,
             "tflops": tf, "frac": tf / peak, "last_span_tflops": tf_last, "last_span_frac": tf_last / peak,
-            "peak_tflops": peak, "peak_source": src, "kernel": "prefill_tcgen05_kernel"}
+            "peak_tflops": peak, "peak_source": src, "kernel": "prefill_tcgen05_kernel", "parity": parity}
 
 
 WAN = dict(batch=2, heads=12, head_dim=128, frame_h=30, frame_w=52, frames_per_block=3, max_frames=21,
@@ -360,6 +417,15 @@ def measure_wan(device, reps: int = 5, batch: int | None = None, kv_splits: int 
     cache.check_errors()
     attn_ms = e[0].elapsed_time(e[1]) / reps
     layer_ms = e[1].elapsed_time(e[2]) / reps
+    attn_only()  # out: the timed call's result again (the layer calls above share the cache, not `out`)
+    toks = torch.tensor([0, 1559, 1560, 3000, BT - 1], device=device)
+    pairs = []
+    for b in range(B):
+        rows = b * BT + toks
+        nk = int(m["seq_k"][b])
+        want = torch_ref_rows(qa[rows], cache.pool_k, cache.pool_v, m["bt"][0][b], [nk] * len(toks), D ** -0.5)
+        pairs.append((out[rows], want))
+    parity = dict(parity_summary(pairs), rows=f"{B} sequences x 5 block tokens, all heads, non-causal")
     try:
         peak = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["bf16_tflops"])
         src = "measured (burst)"
@@ -371,7 +437,7 @@ def measure_wan(device, reps: int = 5, batch: int | None = None, kv_splits: int 
             "flops_per_layer": flops, "attn_ms": attn_ms, "tflops": tf, "frac": tf / peak,
             "layer_ms_incl_rope_append": layer_ms, "peak_tflops": peak, "peak_source": src,
             "kernel": "prefill_tcgen05_kernel<128, 1> (non-causal, keys split in one launch) + merge_partials_kernel",
-            "kv_splits": splits}
+            "kv_splits": splits, "parity": parity}
 
 
 def run_ours(args):
@@ -397,8 +463,9 @@ def run_ours(args):
                                                 wl["ws"])
 
     def layer(l):
+        # the tables were built at set-up, before any torch launch of the warm-up: ready
         ops.decode_paged(wl["q"][l], wl["pool_k"], wl["pool_v"], wl["bt_all"][l], wl["seq_k"], out=wl["out"][l],
-                         out_scale=wl["out_scale"][l], workspace=wl["ws"], max_pages=wl["W"])
+                         out_scale=wl["out_scale"][l], workspace=wl["ws"], max_pages=wl["W"], tables_ready=True)
 
     def barrier():
         if world > 1:
@@ -432,6 +499,16 @@ def run_ours(args):
     err = wl["ws"].error()
     if err[0] != 0:
         raise RuntimeError(f"device error word set: {err}")
+    # the timed region's own outputs (its last step), sampled sequences of the first and last layer
+    D = CFG["head_dim"]
+    pairs = []
+    for l in (0, L - 1):
+        for b in sorted({0, B // 3, 2 * B // 3, B - 1}):
+            n = int(wl["seq_k"][b])
+            want = torch_ref_rows(wl["q"][l][b:b + 1], wl["pool_k"], wl["pool_v"], wl["bt_all"][l][b], [n],
+                                  D ** -0.5, wl["out_scale"][l])
+            pairs.append((wl["out"][l][b:b + 1], want))
+    decode_parity = dict(parity_summary(pairs), rows=f"layers 0 and {L - 1}, 4 sequences each, all heads")
 
     # ---- end to end through the public op with host buffers every step
     q_host = torch.empty(wl["q"].shape, dtype=wl["q"].dtype, pin_memory=True)
@@ -465,6 +542,7 @@ def run_ours(args):
         wl["nsrc"].copy_(nsrc_host, non_blocking=True)
         wl["seq_k"].copy_(seqk_host, non_blocking=True)
         ops.build_layer_block_tables(wl["bt"], wl["nsrc"], wl["ring_base"], out=wl["bt_all"])
+        # the tables come from the kernel just launched, in the same PDL chain: not "ready"
         for l in range(L):
             ops.decode_paged(q_dev[k][l], wl["pool_k"], wl["pool_v"], wl["bt_all"][l], wl["seq_k"],
                              out=out_dev[k][l], out_scale=wl["out_scale"][l], workspace=wl["ws"], max_pages=wl["W"])
@@ -520,6 +598,7 @@ def run_ours(args):
                      "traffic": traffic_per_launch(),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch"},
         "attn_hbm_gbs": achieved,
+        "parity": decode_parity,
         "clocks": clk,
         "gpu_launches": int(args.steps * L * launches_per_call),
         "kv_splits": splits,
@@ -540,9 +619,11 @@ def run_ours(args):
                          "prefill_tokens_per_s": e["prefill"]["tokens_per_s"],
                          "gpu_launches": e["gpu_launches"]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
         times, threads = cpu_layer_step_sample(args.cpu_seconds, batch=8)
         med = statistics.median(times)
         line["cpu_baseline"] = {"value": cpu_tokens_per_s(med, 8), "unit": UNIT, "cores": threads,
+                                "cpu_count": os.cpu_count(),
                                 "kind": "port",
                                 "sample": f"reference CPU layer-step (torch.cat history + torch SDPA, bf16) on 8 of "
                                           f"64 sequences, {len(times)} reps, median {med * 1e3:.1f} ms; "
@@ -558,6 +639,12 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
+    import torch
+
+    # torch.distributed.run exports OMP_NUM_THREADS=1 to every rank; rank 0 alone runs
+    # this arm, so give it every host core, as the single-process run has.
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
     batch = 8
     runner = CpuLayerStep(batch)
     threads = runner.threads
@@ -569,7 +656,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "cpu_count": cores, "kind": "port",
                          "sample": f"one layer-step of the reference's CPU attention (torch.cat history + torch SDPA "
                                    f"bf16) on {batch} of 64 sequences per step; tokens/s = {batch} / (32 x median)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -624,7 +711,7 @@ def run_cp(args):
     def step():
         for l in range(L):
             cp.layer(q[l], pool_k, pool_v, bt, seq_k, out_scale=scale, out=out[l], workspace=ws,
-                     max_pages=pages_mine)
+                     max_pages=pages_mine, tables_ready=True)  # static tables, written at set-up
 
     for _ in range(max(args.warmup, 1)):
         step()

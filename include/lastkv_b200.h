@@ -51,7 +51,9 @@ const char* lkv_status_string(int status);
 /* ABI version of this library (major * 100 + minor). */
 int lkv_abi_version(void);
 
-/* LKV_OK if `device` is an sm_100 (B200-class) GPU this library was built for. */
+/* LKV_OK if `device` is an sm_100 (B200-class) GPU this library was built for.
+ * When `device` is the current device it also loads the static scratch of
+ * lkv_decode_paged_noalloc there (see below), so call it at start-up. */
 int lkv_check_device(int device);
 
 /* Copy the int32[4] error word {code, kernel, block, detail} to host memory.
@@ -76,15 +78,26 @@ int lkv_clear_error_word(int32_t* error_word, void* stream);
  * natural-log LSE [batch, num_q_heads] for a later lkv_merge_partials (the
  * context-parallel combine); `out`, `lse` and `out_scale` are then ignored.
  * Supported: head_dim 64 or 128; num_q_heads / num_kv_heads in {1, 2, 4, 8}.
- * The kernel is launched with programmatic dependent launch: before the
- * stream's preceding kernel has finished it may already read seq_k, the block
- * table and every page of a sequence but its last (where an append kernel just
- * before it puts this step's key); q, the last pages and the workspace it
- * touches only after.  A kernel right before this call may therefore write q
- * and the last pages, but seq_k, the block table and older pages must be
- * complete before it (written by a copy or an ordinary launch, as every
- * caller in this library does).
+ *
+ * Programmatic dependent launch (PDL): the kernel may start while the kernels
+ * before it in the stream still run; CUDA makes their writes visible to it
+ * only at its griddepcontrol.wait.  With flags = 0 it reads nothing (q, seq_k,
+ * block table, pages, workspace) before that wait, so any kernel before it may
+ * produce any input.  With LKV_DECODE_TABLES_READY it requests its first pages
+ * before the wait, overlapping the ring fill with the previous kernel's tail;
+ * the caller then guarantees that seq_k, the block table rows and every page
+ * of a sequence but its last (where an append kernel just before the call
+ * puts this step's key) were written before the most recent operation in the
+ * stream that was NOT a PDL kernel launch - a copy, a plain kernel launch
+ * (torch's, or this library's lkv_build_layer_block_tables) or the start of a
+ * graph - since PDL launches chained back to back may all start before that
+ * point, and the first of them before that operation has finished.  Example: a
+ * step that copies its tables in, launches any plain kernel, then runs the
+ * layers' append + decode pairs; not a step that builds its tables with
+ * lkv_build_layer_block_tables right before its first decode.
  */
+#define LKV_DECODE_TABLES_READY 1
+
 size_t lkv_decode_workspace_bytes(int batch, int num_q_heads, int head_dim, int max_pages_per_seq);
 
 int lkv_decode_paged(const void* q, int64_t q_stride_tok,
@@ -95,7 +108,7 @@ int lkv_decode_paged(const void* q, int64_t q_stride_tok,
                      float* partial_o, float* partial_lse,
                      int batch, int num_q_heads, int num_kv_heads, int head_dim,
                      int max_pages_per_seq, float softmax_scale,
-                     void* workspace, size_t workspace_bytes, void* stream);
+                     void* workspace, size_t workspace_bytes, int flags, void* stream);
 
 /* Allocation-free form of lkv_decode_paged.  No counterpart in the reference:
  * it exists for callers that cannot allocate device memory - an engine whose
@@ -103,15 +116,19 @@ int lkv_decode_paged(const void* q, int64_t q_stride_tok,
  * a C-FFI host that can only pass the inputs and outputs it owns, or a loop
  * that cannot afford cudaMalloc's implicit synchronisation.  Instead of a
  * caller workspace it uses one static device array of
- * LKV_NOALLOC_SCRATCH_BYTES inside the library, held on every GPU that loads
- * the library until the process exits.
- *  - Same arguments and result as lkv_decode_paged (final bf16 output only),
- *    without workspace; `error_word` (device int32[4], may be NULL) receives
+ * LKV_NOALLOC_SCRATCH_BYTES inside the library, held on a GPU from the moment
+ * the library's module is loaded there until the process exits.  Module
+ * loading is lazy: it happens at lkv_check_device(d) while d is the current
+ * device, or else at the first no-alloc call on that device - make one of
+ * them before the engine reserves its KV-cache pool.
+ *  - Same arguments and result as lkv_decode_paged (final bf16 output only,
+ *    flags = 0), without workspace; `error_word` (device int32[4], may be NULL) receives
  *    the call's device error word.
  *  - Rejects, with LKV_ERR_WORKSPACE and nothing launched, shapes where
  *    batch * num_q_heads * (head_dim + 1) * 4 + 512 > LKV_NOALLOC_SCRATCH_BYTES.
- *  - The first call on a device looks up the array's address with that device
- *    current; make it before any stream capture.
+ *  - The first of those calls on a device looks up the array's address with
+ *    that device current; make it before any stream capture.  The address is
+ *    cached for the process: do not reset the device's primary context.
  *  - All calls share the array: calls whose GPU work overlaps race; serialise.
  *  - Allocates nothing (no cudaMalloc / cudaFree). */
 #define LKV_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -352,7 +369,8 @@ int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_fl
  * lkv_cp_combine (rows = batch * num_q_heads); `workspace` as for
  * lkv_decode_paged; state: lkv_decode_cp_state_words uint32 of device memory
  * (8-byte aligned, zero before the first call; every completed call leaves it
- * ready for the next; zero it again after a call reports a device error). */
+ * ready for the next; zero it again after a call reports a device error).
+ * flags as for lkv_decode_paged. */
 int lkv_decode_cp_state_words(int batch, int num_kv_heads, int64_t* state_words);
 int lkv_decode_paged_cp(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
                         int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,
@@ -360,7 +378,7 @@ int lkv_decode_paged_cp(const void* q, int64_t q_stride_tok, const void* pool_k,
                         int batch, int num_q_heads, int num_kv_heads, int head_dim, int max_pages_per_seq,
                         float softmax_scale, void* workspace, size_t workspace_bytes,
                         const uint64_t* peer_recv, int rank, int world, uint32_t* state,
-                        int32_t* error_word, void* stream);
+                        int32_t* error_word, int flags, void* stream);
 /* send may be NULL when this rank's rows were already pushed into every receive
  * buffer (lkv_decode_paged_cp's decode kernel); the call then only polls and merges. */
 int lkv_cp_combine(const float* send, const uint64_t* peer_recv, int rank, int world, uint32_t* state,

@@ -35,7 +35,7 @@ _SIGNATURES = {
     "lkv_clear_error_word": (I32, [P, P]),
     "lkv_decode_workspace_bytes": (SZ, [I32, I32, I32, I32]),
     "lkv_decode_paged": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, P, P, P, P,
-                               I32, I32, I32, I32, I32, F32, P, SZ, P]),
+                               I32, I32, I32, I32, I32, F32, P, SZ, I32, P]),
     "lkv_decode_plan": (I32, [I32, I32, I32, I32, I32, SZ, I32, P, P]),
     "lkv_decode_paged_noalloc": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, P, P,
                                        I32, I32, I32, I32, I32, F32, P, P]),
@@ -53,7 +53,7 @@ _SIGNATURES = {
     "lkv_cp_combine": (I32, [P, P, I32, I32, P, I64, I32, I32, P, P, I64, P, P]),
     "lkv_decode_cp_state_words": (I32, [I32, I32, P]),
     "lkv_decode_paged_cp": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, P, I32, I32, I32, I32, I32, F32, P, SZ,
-                                  P, I32, I32, P, P, P]),
+                                  P, I32, I32, P, P, I32, P]),
     "lkv_decode_gemm": (I32, [P, I64, P, I64, P, I64, I32, I64, I64, I32, P, P, P]),
     "lkv_prefill_paged": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
                                 I32, I32, I32, I32, I32, I32, I32, I32, F32, P, P]),

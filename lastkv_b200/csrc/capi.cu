@@ -120,13 +120,21 @@ const char* lkv_status_string(int status) {
   }
 }
 
-int lkv_abi_version(void) { return 100; }
+int lkv_abi_version(void) { return 200; }
 
 int lkv_check_device(int device) {
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) return LKV_ERR_CUDA;
   if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) return LKV_ERR_CUDA;
-  return (major == 10 && minor == 0) ? LKV_OK : LKV_ERR_ARCH;
+  if (major != 10 || minor != 0) return LKV_ERR_ARCH;
+  // Load the allocation-free decode's static scratch now (lazy module loading
+  // would otherwise commit it at the first lkv_decode_paged_noalloc call, which
+  // may come after a KV-cache pool has taken the memory).  Best effort: a
+  // failure here is retried, and reported, by that call.
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur == device) (void)lkv::noalloc_scratch_prepare();
+  (void)cudaGetLastError();
+  return LKV_OK;
 }
 
 int lkv_read_error_word(const int32_t* error_word, int32_t host_out[4], void* stream) {
@@ -153,7 +161,7 @@ int lkv_decode_paged(const void* q, int64_t q_stride_tok, const void* pool_k, co
                      int64_t out_stride_tok, float* lse, const float* out_scale, float* partial_o,
                      float* partial_lse, int batch, int num_q_heads, int num_kv_heads, int head_dim,
                      int max_pages_per_seq, float softmax_scale, void* workspace, size_t workspace_bytes,
-                     void* stream) {
+                     int flags, void* stream) {
   lkv::DecodeArgs a{};
   a.q = q;
   a.q_stride_tok = q_stride_tok;
@@ -178,6 +186,7 @@ int lkv_decode_paged(const void* q, int64_t q_stride_tok, const void* pool_k, co
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.stream = stream;
+  a.flags = flags;
   return lkv::decode_paged(a);
 }
 
@@ -192,7 +201,7 @@ int lkv_decode_paged_cp(const void* q, int64_t q_stride_tok, const void* pool_k,
                         int64_t out_stride_tok, const float* out_scale, int batch, int num_q_heads, int num_kv_heads,
                         int head_dim, int max_pages_per_seq, float softmax_scale, void* workspace,
                         size_t workspace_bytes, const uint64_t* peer_recv, int rank, int world, uint32_t* state,
-                        int32_t* error_word, void* stream) {
+                        int32_t* error_word, int flags, void* stream) {
   lkv::DecodeArgs a{};
   a.q = q;
   a.q_stride_tok = q_stride_tok;
@@ -219,6 +228,7 @@ int lkv_decode_paged_cp(const void* q, int64_t q_stride_tok, const void* pool_k,
   a.cp_world = world;
   a.cp_state = state;
   a.cp_error = error_word;
+  a.flags = flags;
   return lkv::decode_paged_cp(a);
 }
 

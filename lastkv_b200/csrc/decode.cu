@@ -56,6 +56,7 @@ struct DecodeParams {
   int64_t num_pages;
   float scale_log2;  // softmax_scale * log2(e)
   int final_out;     // 1: this kernel writes `out` (S == 1 and not partial mode)
+  int early;         // 1: seq_k, the block table and older pages predate the PDL chain (LKV_DECODE_TABLES_READY)
   // Context parallel: the last CTA to finish a (sequence, KV head) unit merges its
   // split partials and pushes the merged rows to every rank's receive buffer.
   uint64_t* cp_recv[kCpMaxRanks];
@@ -162,9 +163,12 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
-  // Programmatic dependent launch: q, the epoch and each sequence's newest key
-  // (appended by the previous kernel) are read only after pdl_wait(); the
-  // producer may request the first stages of older pages before it.
+  // Programmatic dependent launch: only after pdl_wait() are the writes of the
+  // kernels before this one in the stream guaranteed visible.  Everything is
+  // read after it, except with p.early: the caller then guarantees that seq_k,
+  // the block table and every page but each sequence's last were written
+  // before the most recent launch without the PDL attribute, so the producer
+  // may request the first stages of older pages before the wait.
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -208,10 +212,11 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       // (fresh slots, so no empty-slot wait), as long as a stage holds neither
       // the sequence's last page - where the previous kernel may just have
       // appended this step's key - nor a page id that would need an error report
-      // (a global write, which must follow the wait).  The sequence lengths and
-      // block tables are inputs of the step, not outputs of the previous kernel.
+      // (a global write, which must follow the wait).  Only with p.early: the
+      // sequence lengths and block tables are then inputs of the step that no
+      // kernel of the current PDL chain writes.
       int pre = 0;
-      if ((int)blockIdx.x < n_items) {
+      if (p.early && (int)blockIdx.x < n_items) {
         const Item w = item_at(blockIdx.x);
         const int32_t* row = p.bt + (int64_t)w.b * p.bt_stride;
         const int last_page = min((w.n + PAGE - 1) / PAGE, p.W) - 1;
@@ -687,10 +692,15 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
 
 }  // namespace
 
+// Workspace bytes one KV split takes after the error header: its normalised o
+// [rows, D] and LSE [rows] in fp32, plus 256 bytes for the o area's alignment.
+size_t decode_split_bytes(int64_t rows, int d) { return (size_t)rows * (size_t)(d + 1) * sizeof(float) + 256; }
+
 size_t decode_workspace_bytes(int batch, int hq, int d, int max_pages) {
   const int64_t rows = (int64_t)std::max(batch, 0) * std::max(hq, 0);
   const int s = std::min(kMaxSplits, std::max(1, max_pages / 4));
-  return kWorkspaceHeader + (size_t)rows * s * (size_t)(std::max(d, 64) + 1) * sizeof(float) + 256;
+  // s splits of decode_paged's per-split layout (o and lse of every row + 256 bytes of alignment slack)
+  return kWorkspaceHeader + (size_t)s * decode_split_bytes(rows, std::max(d, 64));
 }
 
 int decode_paged(const DecodeArgs& a) {
@@ -740,12 +750,13 @@ int decode_paged(const DecodeArgs& a) {
   prm.W = a.max_pages_per_seq;
   prm.num_pages = a.num_pages;
   prm.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+  prm.early = (a.flags & LKV_DECODE_TABLES_READY) ? 1 : 0;
 
   // Workspace after the error header: lse [rows * smax] (256-aligned), then o [rows * smax * D].
   uint8_t* ws = static_cast<uint8_t*>(a.workspace) + kWorkspaceHeader;
   const size_t ws_avail = a.workspace_bytes - kWorkspaceHeader;
   const int64_t rows = (int64_t)a.batch * a.num_q_heads;
-  const size_t per_split = (size_t)rows * (a.head_dim + 1) * sizeof(float) + 256;
+  const size_t per_split = decode_split_bytes(rows, a.head_dim);
   const int smax = (int)std::min<size_t>(kMaxSplits, ws_avail / per_split);
   if (smax < 1 && (partial_mode || a.max_pages_per_seq > 0)) return LKV_ERR_WORKSPACE;
   prm.part_lse = reinterpret_cast<float*>(ws);
@@ -832,7 +843,7 @@ int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspa
   if (occ < 0) return LKV_ERR_CUDA;
   const int64_t rows = (int64_t)batch * hq;
   const size_t avail = workspace_bytes > kWorkspaceHeader ? workspace_bytes - kWorkspaceHeader : 0;
-  const int smax = (int)std::min<size_t>(kMaxSplits, avail / ((size_t)rows * (d + 1) * sizeof(float) + 256));
+  const int smax = (int)std::min<size_t>(kMaxSplits, avail / decode_split_bytes(rows, d));
   const int S = std::min(std::max(smax, 1), choose_splits(batch * hkv, max_pages, g_dev[dev].sms * occ));
   *splits = S;
   *launches = (S == 1 && !partial) ? 1 : 2;

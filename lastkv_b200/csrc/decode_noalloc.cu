@@ -12,11 +12,17 @@
 // fixed-size array below, inside the library itself.
 //
 // Rules of use (also stated in include/lastkv_b200.h):
-//  * The array costs LKV_NOALLOC_SCRATCH_BYTES of device memory on every GPU
-//    that loads this library, for the life of the process.
-//  * The first call on each device looks up the array's device address with
-//    that device current (cudaGetSymbolAddress); make that first call before
-//    any CUDA-graph stream capture.
+//  * The array costs LKV_NOALLOC_SCRATCH_BYTES of device memory on a GPU once
+//    this file's module is loaded there, for the life of the process.  CUDA
+//    loads modules lazily, so that happens at lkv_check_device(d) with d the
+//    current device, or else at the first no-alloc call on the device: make
+//    one of them before the engine reserves its KV-cache pool, or the module's
+//    8 MiB may no longer fit.
+//  * The first of those calls on each device looks up the array's device
+//    address with that device current (cudaGetSymbolAddress); make it before
+//    any CUDA-graph stream capture.  The address is cached per device index
+//    for the life of the process: it assumes the device's primary context is
+//    never reset (no cudaDeviceReset between calls).
 //  * Every call shares the one array.  Calls whose GPU work overlaps (other
 //    streams, other host threads, concurrent graph replays) race on it and
 //    corrupt each other's results; serialise them.
@@ -51,7 +57,10 @@ int scratch_address(int dev, void** out) {
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (g_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr) return LKV_ERR_CUDA;
+    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();  // leave no pending error for the caller's next CUDA check
+      return LKV_ERR_CUDA;
+    }
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];
@@ -59,6 +68,22 @@ int scratch_address(int dev, void** out) {
 }
 
 }  // namespace
+
+namespace lkv {
+
+// Called by lkv_check_device for the current device: loads the module (and so
+// commits the array) at start-up, before a KV-cache pool takes the memory.
+int noalloc_scratch_prepare() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return LKV_ERR_CUDA;
+  }
+  void* p = nullptr;
+  return scratch_address(dev, &p);
+}
+
+}  // namespace lkv
 
 extern "C" int lkv_decode_paged_noalloc(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
                                         int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,

@@ -65,6 +65,7 @@ struct DecodeArgs {
   void* workspace;
   size_t workspace_bytes;
   void* stream;
+  int flags = 0;  // LKV_DECODE_TABLES_READY
   // context parallel (decode_paged_cp): every unit's merged partial is pushed to these receive buffers
   const uint64_t* cp_recv = nullptr;  // host array of cp_world device addresses
   int cp_rank = 0, cp_world = 0;
@@ -72,7 +73,11 @@ struct DecodeArgs {
   int32_t* cp_error = nullptr;
 };
 
+size_t decode_split_bytes(int64_t rows, int d);
 size_t decode_workspace_bytes(int batch, int hq, int d, int max_pages);
+// Loads the allocation-free decode's static scratch on the current device (see
+// decode_noalloc.cu); LKV_OK or LKV_ERR_CUDA, with the CUDA error cleared.
+int noalloc_scratch_prepare();
 int decode_paged(const DecodeArgs& a);
 int decode_plan(int batch, int hq, int hkv, int d, int max_pages, size_t workspace_bytes, int partial, int* splits,
                 int* launches);

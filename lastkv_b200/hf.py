@@ -457,7 +457,8 @@ class LastKVAttention(nn.Module):
         bt = meta["bt_all"][self.layer_idx]
         if L == 1:
             out = ops.decode_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], out_scale=out_scale,
-                                   workspace=cache.workspace, max_pages=meta["W"])
+                                   workspace=cache.workspace, max_pages=meta["W"],
+                                   tables_ready=meta.get("tables_ready", False))
         else:
             out = ops.prefill_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], meta["cu_q"], L,
                                     out_scale=out_scale, error_word=cache.error_word, max_pages=meta["W"])

@@ -79,9 +79,15 @@ class GraphDecodeRunner:
 
     def _fresh_meta(self):
         """The span metadata over the static buffers, without the per-span values the
-        layers memoise (so a capture records the kernels that compute them)."""
+        layers memoise (so a capture records the kernels that compute them).
+
+        ``tables_ready``: the block tables and sequence lengths are written before the
+        graph starts (copies + the table kernel in ``_prepare``), and a graph's first
+        kernel waits for all earlier stream work, so every decode in the step may start
+        its page loads before its PDL wait (LKV_DECODE_TABLES_READY)."""
         self.cache._meta = {"n": 1, "W": self.W, "bt_all": self.bt_all, "seq_k": self.seq_k, "cu_q": self.cu_q,
-                            "local_pos": self.local_pos, "ring_tok": self.ring_tok, "src_slot": self.src_slot}
+                            "local_pos": self.local_pos, "ring_tok": self.ring_tok, "src_slot": self.src_slot,
+                            "tables_ready": True}
 
     def _body(self):
         m = self.model.model

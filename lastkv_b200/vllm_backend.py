@@ -186,6 +186,8 @@ class SharedKVFastPath:
         self._h = [{"ring": host(mt, torch.int64), "src": host(mt, torch.int64), "pos": host(mt, torch.int64),
                     "cu": host(mb + 1, torch.int32), "seqk": host(mb, torch.int32), "nsrc": host(mb, torch.int32),
                     "bt": host((mb, self.W), torch.int32)} for _ in range(self.NSETS)]
+        # per set: an event recorded after the last copies that read it (None = never used)
+        self._h_done = [None] * self.NSETS
         self._set = 0
         self.layers = None
         self.cos_sin = None
@@ -279,6 +281,9 @@ class SharedKVFastPath:
         self._commit(plan["commits"])
         self._set = (self._set + 1) % self.NSETS
         h = self._h[self._set]
+        if self._h_done[self._set] is not None:
+            # the non_blocking copies that last read this set must have run before it is refilled
+            self._h_done[self._set].synchronize()
         T, B = plan["tokens"], plan["batch"]
         h["ring"][:T] = torch.from_numpy(plan["ring"])
         h["src"][:T] = torch.from_numpy(plan["src"])
@@ -294,6 +299,9 @@ class SharedKVFastPath:
         self.seq_k[:B].copy_(h["seqk"][:B], non_blocking=True)
         self.nsrc[:B].copy_(h["nsrc"][:B], non_blocking=True)
         self.bt[:B].copy_(h["bt"][:B], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        self._h_done[self._set] = done
         L = self.pool.num_layers
         self.bt_all = self._bt_all_flat[: L * B * self.W].view(L, B, self.W)
         ops.build_layer_block_tables(self.bt[:B], self.nsrc[:B], self.pool.ring_base_dev, out=self.bt_all)

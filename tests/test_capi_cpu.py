@@ -59,19 +59,19 @@ def test_host_only_entry_points(lib):
 def test_argument_validation_needs_no_gpu(lib):
     # unsupported head_dim / GQA group are rejected before any CUDA call
     st = lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
-                              1, 4, 1, 96, 1, 1.0, None, 0, None)
+                              1, 4, 1, 96, 1, 1.0, None, 0, 0, None)
     assert st == 2
     st = lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
-                              1, 12, 1, 128, 1, 1.0, None, 0, None)
+                              1, 12, 1, 128, 1, 1.0, None, 0, 0, None)
     assert st == 2
     assert lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
-                                1, 8, 3, 128, 1, 1.0, None, 0, None) == 1
+                                1, 8, 3, 128, 1, 1.0, None, 0, 0, None) == 1
     # empty batch is a no-op
     assert lib.lkv_decode_paged(None, 0, None, None, 1, None, 0, None, None, 0, None, None, None, None,
-                                0, 8, 8, 128, 1, 1.0, None, 0, None) == 0
+                                0, 8, 8, 128, 1, 1.0, None, 0, 0, None) == 0
     # the fused context-parallel decode needs its peers and state: rejected before any CUDA call
     assert lib.lkv_decode_paged_cp(None, 0, None, None, 1, None, 0, None, None, 0, None, 2, 8, 8, 128, 1, 1.0,
-                                   None, 0, None, 0, 2, None, None, None) == 1
+                                   None, 0, None, 0, 2, None, None, 0, None) == 1
     # the key-split prefill validates its shape first (head_dim 96 is unsupported)
     assert lib.lkv_prefill_paged_split(None, 0, None, None, 1, None, 0, None, None, None, 0, None, None,
                                        1, 1, 1, 8, 8, 96, 1, 1.0, 2, None, None, None, None) == 2
@@ -102,27 +102,23 @@ def test_ops_fail_loudly_without_library(tmp_path, monkeypatch):
         _capi.load(str(tmp_path / "missing.so"))
 
 
-def test_integration_bindings_match_the_abi():
-    """Every lkv_* call in INTEGRATION.md's Python snippets passes as many arguments
-    as the C ABI declares (the snippets are what a maintainer would copy)."""
-    import ast
-    import os
+def test_binding_arities_match_the_header():
+    """Every ctypes signature in ``_capi._SIGNATURES`` passes exactly as many arguments as
+    the function's declaration in include/lastkv_b200.h, and every declared function is
+    bound (the header is the ABI; the bindings are what a caller copies)."""
     import re
 
     from lastkv_b200 import _capi
 
-    text = open(os.path.join(os.path.dirname(__file__), "..", "INTEGRATION.md")).read()
-    blocks = re.findall(r"```python\n(.*?)```", text, flags=re.S)
-    assert blocks
-    seen = 0
-    for block in blocks:
-        for node in ast.walk(ast.parse(block)):
-            if isinstance(node, ast.Call) and isinstance(node.func, ast.Attribute) and node.func.attr.startswith("lkv_"):
-                name = node.func.attr
-                assert name in _capi._SIGNATURES, name
-                assert len(node.args) == len(_capi._SIGNATURES[name][1]), (name, len(node.args))
-                seen += 1
-    assert seen >= 4
+    text = re.sub(r"/\*.*?\*/", "", open(_capi.HEADER).read(), flags=re.S)
+    decls = {}
+    for m in re.finditer(r"\b(lkv_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+        params = m.group(2).strip()
+        decls[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    assert set(decls) == set(_capi.declared_symbols())
+    assert set(decls) == set(_capi._SIGNATURES), set(decls) ^ set(_capi._SIGNATURES)
+    for name, n in decls.items():
+        assert len(_capi._SIGNATURES[name][1]) == n, (name, n, len(_capi._SIGNATURES[name][1]))
 
 
 def test_nvtx_ranges_are_opt_in():
