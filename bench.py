@@ -76,6 +76,8 @@ def parse():
     ap.add_argument("--cp-combine", default="p2p", choices=["p2p", "nccl"],
                     help="cp128k: combine the partials over peer memory (one kernel) or NCCL all-gather + merge")
     ap.add_argument("--cp-eager", action="store_true", help="cp128k: launch per layer instead of a CUDA graph")
+    ap.add_argument("--no-cp", action="store_true",
+                    help="skip the context-parallel 128K decode measurement (config 4) in the default line")
     ap.add_argument("--e2e-layers", type=int, default=None,
                     help="e2e8b with fewer layers (same per-layer shapes), for profiler captures; never a bench line")
     return ap.parse_args()
@@ -609,7 +611,7 @@ def run_ours(args):
         line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1, kv_splits=args.wan_kv_splits)
     if not args.no_e2e8b:
         # config 3 on the same ranks: the 8B architecture end to end (weak scaling, batch 8 per GPU)
-        del wl
+        wl = None
         torch.cuda.empty_cache()
         e = measure_e2e8b(max(E2E8B["decode_tokens"] - 3, 1), 3, world, device)
         line["e2e8b"] = {"metric": e["metric"], "value": e["value"], "unit": e["unit"], "n_gpus": world,
@@ -618,6 +620,15 @@ def run_ours(args):
                          "roofline_frac": e["roofline"]["frac"], "achieved_gbs": e["roofline"]["achieved"],
                          "prefill_tokens_per_s": e["prefill"]["tokens_per_s"],
                          "gpu_launches": e["gpu_launches"]}
+    if not args.no_cp:
+        # config 4 on the same ranks: 128K-context decode sharded over all N GPUs (strong scaling)
+        wl = None
+        torch.cuda.empty_cache()
+        c4 = measure_cp(100, 3, world, rank, device, combine=args.cp_combine, eager=args.cp_eager)
+        line["cp128k"] = {k: c4[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step",
+                                             "scaling", "layer_ms", "hbm_gbs_per_gpu", "hbm_frac_per_gpu",
+                                             "combine_bytes_per_rank_per_layer", "parity")}
+        line["cp128k"]["parallelism"] = c4["config"]["parallelism"]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         times, threads = cpu_layer_step_sample(args.cpu_seconds, batch=8)
@@ -669,20 +680,13 @@ CP = dict(batch=4, q_heads=32, kv_heads=8, head_dim=128, context=131072, window=
 
 
 def run_cp(args):
-    """Config 4: 128K-context decode, sequence-sharded over the ranks (context parallel).
-
-    Each rank holds a contiguous 1/G slice of every sequence's shared pages (the
-    last rank also the 2048-token ring window); per layer the partial decode
-    kernel runs on the slice, the (o, lse) partials are all-gathered over NCCL
-    and merged exactly.  Prints one JSON line (rank 0).
-    """
+    """Config 4 alone (``--workload cp128k``): prints its line (rank 0)."""
     import datetime
 
     import torch
     import torch.distributed as dist
 
-    from lastkv_b200 import _capi, ops
-    from lastkv_b200.context_parallel import ContextParallelDecode, plan_shard
+    from lastkv_b200 import _capi
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -692,77 +696,153 @@ def run_cp(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     _capi.load()
+    line = measure_cp(args.steps, args.warmup, world, rank, device, combine=args.cp_combine, eager=args.cp_eager)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _cp_shard_tensors(rank: int, world: int, device):
+    """Rank ``rank``'s slice of config 4: its pools, shuffled block table and key count
+    (seeded per rank, so any rank can rebuild another's slice for the output check)."""
+    import torch
+
+    from lastkv_b200.context_parallel import plan_shard
+
+    B, H, D, N, Wt = (CP[k] for k in ("batch", "kv_heads", "head_dim", "context", "window"))
+    sp = plan_shard((N - Wt) // 16, Wt, 16, world, rank)
+    pages = (sp.p1 - sp.p0) + sp.ring_pages
+    gen = torch.Generator(device=device).manual_seed(300 + rank)
+    pool_k = torch.randn((B * pages + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    pool_v = torch.randn((B * pages + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
+    bt = torch.randperm(B * pages, generator=gen, device=device).to(torch.int32).view(B, pages)
+    return pool_k, pool_v, bt, sp.seq_k, pages
+
+
+def measure_cp(steps: int, warmup: int, world: int, rank: int, device, combine: str = "p2p",
+               eager: bool = False) -> dict:
+    """Config 4: 128K-context decode, sequence-sharded over the ranks (context parallel).
+
+    Each rank holds a contiguous 1/G slice of every sequence's shared pages (the
+    last rank also the 2048-token ring window).  With one rank a layer is the
+    plain split-KV decode; with more, each layer is ``lkv_decode_paged_cp`` (the
+    decode kernel pushes each unit's merged rows to every rank over peer memory,
+    then one poll-and-merge launch) or, with ``combine="nccl"``, the partial
+    decode + NCCL all-gather + merge.  The queries are the same on every rank (one
+    decode token).  After the timed region rank 0 checks sampled rows of its
+    output against an fp32 recomputation over all ranks' keys (each rank's slice
+    rebuilt from its seed).  All ranks call this together.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from lastkv_b200 import ops
+    from lastkv_b200.context_parallel import ContextParallelDecode
+
     B, Hq, H, D, N, Wt, L = (CP[k] for k in ("batch", "q_heads", "kv_heads", "head_dim", "context", "window",
                                              "layers"))
-    nsrc = (N - Wt) // 16
-    sp = plan_shard(nsrc, Wt, 16, world, rank)
-    pages_mine = (sp.p1 - sp.p0) + sp.ring_pages
-    gen = torch.Generator(device=device).manual_seed(300 + rank)
-    pool_k = torch.randn((B * pages_mine + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
-    pool_v = torch.randn((B * pages_mine + 1, 16, H, D), generator=gen, device=device, dtype=torch.bfloat16)
-    bt = torch.randperm(B * pages_mine, generator=gen, device=device).to(torch.int32).view(B, pages_mine)
-    seq_k = torch.full((B,), sp.seq_k, dtype=torch.int32, device=device)
-    q = torch.randn((L, B, Hq, D), generator=gen, device=device, dtype=torch.bfloat16)
+    pool_k, pool_v, bt, seq_len, pages_mine = _cp_shard_tensors(rank, world, device)
+    seq_k = torch.full((B,), seq_len, dtype=torch.int32, device=device)
+    qgen = torch.Generator(device=device).manual_seed(299)  # one query token, the same on every rank
+    q = torch.randn((L, B, Hq, D), generator=qgen, device=device, dtype=torch.bfloat16)
+    scale = (torch.rand((L, Hq), generator=qgen, device=device) + 0.5).to(torch.bfloat16).float()
     out = torch.empty((L, B, Hq, D), dtype=torch.bfloat16, device=device)
-    scale = torch.ones(Hq, device=device)
     ws = ops.Workspace.for_decode(B, Hq, D, pages_mine, device=device)
-    cp = ContextParallelDecode(combine=args.cp_combine if world > 1 else "nccl")
+    cp = ContextParallelDecode(combine=combine) if world > 1 else None
 
     def step():
         for l in range(L):
-            cp.layer(q[l], pool_k, pool_v, bt, seq_k, out_scale=scale, out=out[l], workspace=ws,
-                     max_pages=pages_mine, tables_ready=True)  # static tables, written at set-up
+            if cp is None:
+                ops.decode_paged(q[l], pool_k, pool_v, bt, seq_k, out=out[l], out_scale=scale[l], workspace=ws,
+                                 max_pages=pages_mine, tables_ready=True)  # static tables, written at set-up
+            else:
+                cp.layer(q[l], pool_k, pool_v, bt, seq_k, out_scale=scale[l], out=out[l], workspace=ws,
+                         max_pages=pages_mine, tables_ready=True)
 
-    for _ in range(max(args.warmup, 1)):
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(warmup, 1)):
         step()
     torch.cuda.synchronize()
     graph = None
-    if not args.cp_eager:
-        # the 32 layer calls of one step (decode with push + combine each) as one CUDA graph
-        if world > 1:
-            dist.barrier()
+    if not eager:
+        # the 32 layer calls of one step as one CUDA graph (the combine's epoch lives on the device)
+        barrier()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step()
         graph.replay()
         torch.cuda.synchronize()
     run = graph.replay if graph is not None else step
-    if world > 1:
-        dist.barrier()
+    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         run()
     e1.record()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    cp.check_errors()
+    barrier()
+    if cp is not None:
+        cp.check_errors()
+    if ws.error()[0] != 0:
+        raise RuntimeError(f"context-parallel decode error word set: {ws.error()}")
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    layer_ms = ms / (args.steps * L)
+    del graph, run  # a graph holding collectives goes before the process group
+    parity = None
+    if rank == 0:
+        # the last layer's output of the last step, sequences 0 and B-1, against all ranks' keys
+        l = L - 1
+        keys = {b: ([], []) for b in (0, B - 1)}
+        for r in range(world):
+            pk, pv, bt_r, n_r, _ = (pool_k, pool_v, bt, seq_len, None) if r == rank else \
+                _cp_shard_tensors(r, world, device)
+            for b in keys:
+                pg = bt_r[b][: -(-n_r // 16)].long()
+                keys[b][0].append(pk[pg].reshape(-1, H, D)[:n_r])
+                keys[b][1].append(pv[pg].reshape(-1, H, D)[:n_r])
+            del pk, pv
+        pairs = []
+        for b, (ks, vs) in keys.items():
+            k, v = torch.cat(ks).float(), torch.cat(vs).float()
+            assert k.shape[0] == N
+            qg = q[l][b].float().view(H, Hq // H, D)
+            p_ = torch.softmax(torch.einsum("hgd,khd->hgk", qg, k) * D ** -0.5, dim=-1)
+            want = torch.einsum("hgk,khd->hgd", p_, v).reshape(Hq, D) * scale[l].view(Hq, 1)
+            pairs.append((out[l][b], want))
+        parity = dict(parity_summary(pairs), rows=f"last layer, sequences 0 and {B - 1}, all heads, over all "
+                                                  f"{world} ranks' keys")
+        del keys
+    layer_ms = ms / (steps * L)
     bytes_layer = 2 * B * H * N * D * 2
+    try:
+        peak = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        peak = 6650.0
+    mode = ("plain split-KV decode (one GPU)" if cp is None else
+            "decode kernel pushes each unit's merged rows over peer memory; one poll + LSE merge launch"
+            if cp.combine == "p2p" else "NCCL all-gather + LSE merge")
     line = {"metric": "context-parallel decode tokens/s (attention only, 32 layers, 128K context)",
-            "value": B * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "value": B * steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "cp128k", "batch": B, "context_tokens": N, "ring_window": Wt, "q_heads": Hq,
                        "kv_heads": H, "head_dim": D, "layers_per_step": L,
-                       "parallelism": f"cp{world} (shared pages sharded; " + (
-                           "decode kernel pushes each unit's merged rows over peer memory; one poll + LSE "
-                           "merge launch)" if cp.combine == "p2p" and world > 1
-                           else "NCCL all-gather + LSE merge)"),
-                       "launch": "eager per layer" if graph is None else "one CUDA graph per step"},
+                       "parallelism": f"cp{world} (shared pages sharded; {mode})",
+                       "launch": "eager per layer" if eager else "one CUDA graph per step"},
             "layer_ms": layer_ms, "attn_bytes_per_layer_total": bytes_layer,
             "hbm_gbs_per_gpu": bytes_layer / world / (layer_ms * 1e-3) / 1e9,
-            "combine_bytes_per_rank_per_layer": B * Hq * (D + 1) * 4}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    del graph, run  # a graph holding collectives goes before the process group
-    if world > 1:
-        dist.destroy_process_group()
+            "hbm_frac_per_gpu": bytes_layer / world / (layer_ms * 1e-3) / 1e9 / peak,
+            "combine_bytes_per_rank_per_layer": B * Hq * (D + 1) * 4 if world > 1 else 0,
+            "parity": parity}
+    del cp, pool_k, pool_v, out, ws
+    torch.cuda.empty_cache()
+    return line
 
 
 E2E8B = dict(layers=32, hidden=4096, q_heads=32, kv_heads=8, head_dim=128, ffn=14336, vocab=128256, chunk=1024,

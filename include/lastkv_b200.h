@@ -238,6 +238,11 @@ int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_par
  * are skipped and recorded in `error_word` (int32[4], may be NULL). */
 #define LKV_ROPE_INTERLEAVED 1 /* rotary pairs (2i, 2i+1) (GPT-J / Wan) instead of (i, i + D/2) */
 #define LKV_ROPE_TABLE_FP32 2  /* cos_sin is fp32 (e.g. per-token 3-D tables) instead of bf16 */
+/* Every tensor fp32 (q, k, v, q_out, pools, q_weight / k_weight, cos_sin): the
+ * reference's fp32 configuration (modeling.py:103-108 in fp32).  RoPE is then
+ * q*cos + rotate_half(q)*sin with two rounded products and a rounded sum, and
+ * RMSNorm w * (x * (1 / sqrt(mean(x^2) + eps))), as the fp32 torch modules. */
+#define LKV_APPEND_FP32 4
 
 int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_row,
                          const void* v, int64_t v_row, const int64_t* positions,
@@ -248,6 +253,28 @@ int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_
                          const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots,
                          int num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
                          int flags, int32_t* error_word, void* stream);
+
+/* ------------------------------------------------------------------ fp32 attention
+ * The merged attention call for fp32 models (the reference's fp32
+ * configuration: LastKVAttention.forward's SDPA over fp32 history,
+ * llm/src/lastkv/llm/modeling.py:109-146, with the s_l of _scale folded into
+ * out_scale as in lkv_decode_paged).  Decode (one token per sequence) and
+ * chunked-prefill spans alike: query i of a span of Lq sees keys
+ * [0, seq_k - Lq + i] when causal (bottom-right), all seq_k keys otherwise.
+ * All tensors fp32 with the bf16 path's layouts: q / out [total_q, Hq, D] rows,
+ * pools [num_pages, 16, Hkv, D] (16-byte aligned), block_table int32 [batch,
+ * >= max_pages_per_seq], seq_k int32 [batch], cu_seqlens_q int32 [batch + 1],
+ * out_scale fp32 [Hq] or NULL, lse fp32 [total_q, Hq] (natural log) or NULL,
+ * error_word (required) device int32[4].  Pages outside the pool are skipped
+ * and recorded.  head_dim 64 or 128, any GQA group.  One launch (PDL). */
+int lkv_attention_paged_f32(const void* q, int64_t q_stride_tok,
+                            const void* pool_k, const void* pool_v, int64_t num_pages,
+                            const int32_t* block_table, int64_t block_table_stride,
+                            const int32_t* seq_k, const int32_t* cu_seqlens_q,
+                            void* out, int64_t out_stride_tok, float* lse, const float* out_scale,
+                            int batch, int total_q, int num_q_heads, int num_kv_heads, int head_dim,
+                            int max_pages_per_seq, int causal, float softmax_scale,
+                            int32_t* error_word, void* stream);
 
 /* ------------------------------------------------------------------ gather / blend
  * Token-level commit for histories whose segments do not start on page
@@ -279,6 +306,14 @@ int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages,
                     const int32_t* raw_pages, const int32_t* ring_pages, int64_t ring_layer_stride_pages,
                     const float* alpha, int num_layers, int num_seqs, int pages_per_chunk,
                     int num_kv_heads, int head_dim, int32_t* error_word, void* stream);
+/* The same commit on fp32 pools (the reference's fp32 configuration): ring =
+ * a*raw + (1-a)*ring in fp32, a*raw and (1-a)*ring each rounded, then their
+ * sum (modeling.py:115-119); alpha fp32 [num_layers, num_kv_heads] holding the
+ * fp32 sigmoid of the logits. */
+int lkv_blend_chunk_f32(void* pool_k, void* pool_v, int64_t num_pages,
+                        const int32_t* raw_pages, const int32_t* ring_pages, int64_t ring_layer_stride_pages,
+                        const float* alpha, int num_layers, int num_seqs, int pages_per_chunk,
+                        int num_kv_heads, int head_dim, int32_t* error_word, void* stream);
 
 /* ------------------------------------------------------------------ block tables
  * Per-layer block tables of the merged pool (fastpath.py:422-424):

@@ -44,6 +44,9 @@ _SIGNATURES = {
                                    P, P, P, I64, P, P, P, I64, I32, I32, I32, I32, I32, P, P]),
     "lkv_gather_blend": (I32, [P, P, I64, P, P, P, P, P, I32, I32, I32, P, P]),
     "lkv_blend_chunk": (I32, [P, P, I64, P, P, I64, P, I32, I32, I32, I32, I32, P, P]),
+    "lkv_blend_chunk_f32": (I32, [P, P, I64, P, P, I64, P, I32, I32, I32, I32, I32, P, P]),
+    "lkv_attention_paged_f32": (I32, [P, I64, P, P, I64, P, I64, P, P, P, I64, P, P,
+                                      I32, I32, I32, I32, I32, I32, I32, F32, P, P]),
     "lkv_build_layer_block_tables": (I32, [P, I64, P, P, I32, I32, I32, P, P]),
     "lkv_rmsnorm": (I32, [P, I64, P, I64, P, I64, P, P, I64, I32, I32, F32, P]),
     "lkv_silu_mul": (I32, [P, I64, P, I64, I64, I32, P]),

@@ -20,7 +20,8 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIBDIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIBDIR, "liblastkv_b200.so")
-SOURCES = ["capi.cu", "decode.cu", "append.cu", "prefill.cu", "decode_noalloc.cu", "dense.cu", "gemm.cu", "cp_combine.cu"]
+SOURCES = ["capi.cu", "decode.cu", "append.cu", "prefill.cu", "decode_noalloc.cu", "dense.cu", "gemm.cu", "cp_combine.cu",
+           "fp32.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

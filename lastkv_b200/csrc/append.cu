@@ -318,6 +318,7 @@ int rope_norm_append(const AppendArgs& a) {
   if ((a.q_weight == nullptr) != (a.k_weight == nullptr)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.src_slot && (!a.src_k || !a.src_v)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.num_tokens > 65535) return LKV_ERR_UNSUPPORTED;  // grid.y limit; callers split larger spans
+  if (a.flags & LKV_APPEND_FP32) return rope_norm_append_f32(a);  // fp32 tensors and table (fp32.cu)
   AppendParams p{};
   p.q = static_cast<const __nv_bfloat16*>(a.q);
   p.q_row = a.q_row;

@@ -317,6 +317,61 @@ int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages, const int32_t
   return lkv::blend_chunk(a);
 }
 
+int lkv_blend_chunk_f32(void* pool_k, void* pool_v, int64_t num_pages, const int32_t* raw_pages,
+                        const int32_t* ring_pages, int64_t ring_layer_stride_pages, const float* alpha,
+                        int num_layers, int num_seqs, int pages_per_chunk, int num_kv_heads, int head_dim,
+                        int32_t* error_word, void* stream) {
+  lkv::BlendArgs a{};
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.raw_pages = raw_pages;
+  a.ring_pages = ring_pages;
+  a.ring_layer_stride_pages = ring_layer_stride_pages;
+  a.alpha = alpha;
+  a.num_layers = num_layers;
+  a.num_seqs = num_seqs;
+  a.pages_per_chunk = pages_per_chunk;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.error_word = error_word;
+  a.stream = stream;
+  return lkv::blend_chunk_f32(a);
+}
+
+int lkv_attention_paged_f32(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
+                            int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,
+                            const int32_t* seq_k, const int32_t* cu_seqlens_q, void* out, int64_t out_stride_tok,
+                            float* lse, const float* out_scale, int batch, int total_q, int num_q_heads,
+                            int num_kv_heads, int head_dim, int max_pages_per_seq, int causal, float softmax_scale,
+                            int32_t* error_word, void* stream) {
+  lkv::AttnF32Args a{};
+  a.q = q;
+  a.q_stride_tok = q_stride_tok;
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.block_table = block_table;
+  a.block_table_stride = block_table_stride;
+  a.seq_k = seq_k;
+  a.cu_seqlens_q = cu_seqlens_q;
+  a.out = out;
+  a.out_stride_tok = out_stride_tok;
+  a.lse = lse;
+  a.out_scale = out_scale;
+  a.batch = batch;
+  a.total_q = total_q;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.max_pages_per_seq = max_pages_per_seq;
+  a.causal = causal;
+  a.softmax_scale = softmax_scale;
+  a.error_word = error_word;
+  a.stream = stream;
+  return lkv::attention_f32(a);
+}
+
 int lkv_prefill_paged(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,
                       int64_t num_pages, const int32_t* block_table, int64_t block_table_stride,
                       const int32_t* seq_k, const int32_t* cu_seqlens_q, void* out, int64_t out_stride_tok,

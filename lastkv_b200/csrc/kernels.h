@@ -116,6 +116,28 @@ struct AppendArgs {
   void* stream;
 };
 int rope_norm_append(const AppendArgs& a);
+int rope_norm_append_f32(const AppendArgs& a);  // LKV_APPEND_FP32 (fp32.cu)
+
+struct AttnF32Args {
+  const void* q;
+  int64_t q_stride_tok;
+  const void* pool_k;
+  const void* pool_v;
+  int64_t num_pages;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  const int32_t* seq_k;
+  const int32_t* cu_seqlens_q;
+  void* out;
+  int64_t out_stride_tok;
+  float* lse;
+  const float* out_scale;
+  int batch, total_q, num_q_heads, num_kv_heads, head_dim, max_pages_per_seq, causal;
+  float softmax_scale;
+  int32_t* error_word;
+  void* stream;
+};
+int attention_f32(const AttnF32Args& a);
 
 int gather_blend(void* pool_k, void* pool_v, int64_t num_slots, const int64_t* dst, const int64_t* src_a,
                  const int64_t* src_b, const int32_t* alpha_row, const float* alpha, int num_tokens,
@@ -134,6 +156,7 @@ struct BlendArgs {
   void* stream;
 };
 int blend_chunk(const BlendArgs& a);
+int blend_chunk_f32(const BlendArgs& a);  // fp32 pools (fp32.cu)
 
 int build_layer_block_tables(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc, const int32_t* ring_base,
                              int num_layers, int batch, int width, int32_t* bt_all, cudaStream_t stream);

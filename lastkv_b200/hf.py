@@ -222,7 +222,11 @@ class PagedLastKVCache:
     reference's meaning (modeling.py:56-67).
     """
 
-    def __init__(self, config: LastKVConfig, batch: int, max_tokens: int, device=None, *, page_order=None):
+    def __init__(self, config: LastKVConfig, batch: int, max_tokens: int, device=None, *, page_order=None,
+                 dtype=torch.bfloat16):
+        if dtype not in (torch.bfloat16, torch.float32):
+            raise RMarinBackendContractError("the paged cache holds bf16 or fp32 keys and values")
+        self.dtype = dtype
         self.num_layers = config.num_hidden_layers
         self.chunk_size = config.chunk_size
         self.batch = batch
@@ -240,8 +244,8 @@ class PagedLastKVCache:
         self.ring_stride = self.ring_pages * batch + 1
         self.num_pages = self.src_pages + self.num_layers * self.ring_stride
         shape = (self.num_pages, PAGE_SIZE, self.hkv, self.d)
-        self.pool_k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
-        self.pool_v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.pool_k = torch.zeros(shape, dtype=dtype, device=device)
+        self.pool_v = torch.zeros(shape, dtype=dtype, device=device)
         order = np.arange(self.src_pages) if page_order is None else np.asarray(page_order)
         if sorted(order.tolist()) != list(range(self.src_pages)):
             raise RMarinBackendContractError("page_order must permute the shared pages")
@@ -250,8 +254,10 @@ class PagedLastKVCache:
         self.ring_base = self.src_pages + np.arange(self.num_layers) * self.ring_stride
         self.ring_base_dev = torch.from_numpy(self.ring_base.astype(np.int32)).to(device)
         self.error_word = torch.zeros(4, dtype=torch.int32, device=device)
+        # the split-KV partials of the bf16 decode (the fp32 attention needs no scratch)
         self.workspace = ops.Workspace.for_decode(batch, config.num_attention_heads, self.d,
-                                                  self.pages_per_seq + self.ring_pages, device=device)
+                                                  self.pages_per_seq + self.ring_pages, device=device) \
+            if dtype == torch.bfloat16 else None
         self._meta = None
 
     # -- reference API
@@ -347,7 +353,7 @@ class PagedLastKVCache:
 
     def check_errors(self):
         e = self.error_word.cpu().tolist()
-        w = self.workspace.error()
+        w = self.workspace.error() if self.workspace is not None else [0, 0, 0, 0]
         if e[0] or w[0]:
             raise RMarinBackendContractError(f"device error word set: append/blend {e}, decode {w}")
 
@@ -389,32 +395,38 @@ class LastKVAttention(nn.Module):
         self._qkv = _fuse_linears([self.q_proj, self.k_proj, self.v_proj])
         return self
 
-    def _layer_constants(self):
-        """(s, 1/s, s per query head, q-norm weight, k-norm weight) for the kernels, rebuilt
-        only when a parameter they derive from changes (in-place loads bump the version)."""
+    def _layer_constants(self, kv_dtype=torch.bfloat16):
+        """(s, 1/s, s per query head, q-norm weight, k-norm weight) for the kernels of a
+        ``kv_dtype`` cache, rebuilt only when a parameter they derive from changes
+        (in-place loads bump the version)."""
         params = [p for p in (getattr(self, "deep_v_scale", None),
                               getattr(getattr(self, "q_norm", None), "weight", None),
                               getattr(getattr(self, "k_norm", None), "weight", None)) if p is not None]
-        key = tuple((p.data_ptr(), p._version, p.dtype) for p in params) + (str(self.q_proj.weight.device),)
+        key = tuple((p.data_ptr(), p._version, p.dtype) for p in params) + (str(self.q_proj.weight.device),
+                                                                             kv_dtype)
         if self._consts[0] != key:
-            s = self.value_scale()
+            s = self.value_scale(kv_dtype)
             qn = getattr(self, "q_norm", None)
             kn = getattr(self, "k_norm", None)
             self._consts = (key, (s, (1.0 / s).contiguous(),
                                   s.repeat_interleave(self.num_heads // self.num_key_value_heads).contiguous(),
-                                  qn.weight.detach().to(torch.bfloat16).contiguous() if qn is not None else None,
-                                  kn.weight.detach().to(torch.bfloat16).contiguous() if kn is not None else None))
+                                  qn.weight.detach().to(kv_dtype).contiguous() if qn is not None else None,
+                                  kn.weight.detach().to(kv_dtype).contiguous() if kn is not None else None))
         return self._consts[1]
 
-    def value_scale(self) -> torch.Tensor:
-        """s_l per KV head as the pool sees it: bf16-exact values (batching.py:1070-1080)."""
+    def value_scale(self, kv_dtype=torch.bfloat16) -> torch.Tensor:
+        """s_l per KV head as the pool sees it, in fp32: bf16-exact values for a bf16 cache
+        (batching.py:1070-1080), the parameter itself for an fp32 one (``_scale``,
+        modeling.py:93-96, in the value dtype)."""
         if not self.config.deep_kv_rescale:
             return torch.ones(self.num_key_value_heads, device=self.q_proj.weight.device)
-        return self.deep_v_scale.detach().to(torch.bfloat16).float()
+        return self.deep_v_scale.detach().to(kv_dtype).float()
 
-    def blend_alpha(self) -> torch.Tensor:
-        """sigmoid of the bf16 logits, rounded to bf16 (batching.py:1067-1079)."""
-        return self.prev_chunk_alphas.detach().to(torch.bfloat16).sigmoid().float()
+    def blend_alpha(self, kv_dtype=torch.bfloat16) -> torch.Tensor:
+        """The blend weight a = sigmoid(prev_chunk_alphas) in the cache's dtype, as fp32:
+        the sigmoid of the bf16 logits rounded to bf16 for a bf16 cache
+        (batching.py:1067-1079), the fp32 sigmoid for an fp32 one (modeling.py:115)."""
+        return self.prev_chunk_alphas.detach().to(kv_dtype).sigmoid().float()
 
     def forward(self, hidden_states, position_embeddings, cache: PagedLastKVCache):
         B, L, _ = hidden_states.shape
@@ -431,18 +443,19 @@ class LastKVAttention(nn.Module):
             q = self.q_proj(hidden_states).reshape(B * L, Hq * D)
             k = self.k_proj(hidden_states).reshape(B * L, Hkv * D)
             v = self.v_proj(hidden_states).reshape(B * L, Hkv * D)
-        if q.dtype != torch.bfloat16:
-            q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+        kv_dtype = cache.dtype  # bf16: the tensor-core kernels; fp32: the fp32 configuration's kernels
+        if q.dtype != kv_dtype:
+            q, k, v = q.to(kv_dtype), k.to(kv_dtype), v.to(kv_dtype)
         cs = None
         if not self.config.use_nope:
             cos, sin = position_embeddings
             # the (cos | sin) table is the same for every layer of a span: build it once
             if meta.get("cs_of") is not cos:
                 meta["cs"] = torch.cat((cos[0, :, : D // 2], sin[0, :, : D // 2]), dim=-1).to(
-                    torch.bfloat16).contiguous()
+                    torch.bfloat16 if kv_dtype == torch.bfloat16 else torch.float32).contiguous()
                 meta["cs_of"] = cos
             cs = meta["cs"]
-        s, inv, out_scale, q_w, k_w = self._layer_constants()
+        s, inv, out_scale, q_w, k_w = self._layer_constants(kv_dtype)
         top = self.layer_idx == cache.num_layers - 1
         flat_k = cache.pool_k.view(-1, Hkv, D)
         flat_v = cache.pool_v.view(-1, Hkv, D)
@@ -455,7 +468,10 @@ class LastKVAttention(nn.Module):
             meta["src_slot"] if top else None, flat_k if top else None, flat_v if top else None,
             error_word=cache.error_word)
         bt = meta["bt_all"][self.layer_idx]
-        if L == 1:
+        if kv_dtype == torch.float32:  # decode and spans alike (lkv_attention_paged_f32)
+            out = ops.attention_paged_f32(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], meta["cu_q"],
+                                          out_scale=out_scale, error_word=cache.error_word, max_pages=meta["W"])
+        elif L == 1:
             out = ops.decode_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], out_scale=out_scale,
                                    workspace=cache.workspace, max_pages=meta["W"],
                                    tables_ready=meta.get("tables_ready", False))
@@ -525,7 +541,7 @@ class LastKVModel(nn.Module):
             outputs.append(self.run_layers(chunk, position_embeddings, cache))
             cache.advance(take)
             if cache.seen_tokens % C == 0:
-                cache.commit(self.blend_alpha())
+                cache.commit(self.blend_alpha(cache.dtype))
             start += take
         return outputs[0] if len(outputs) == 1 else torch.cat(outputs, dim=1)
 
@@ -536,12 +552,14 @@ class LastKVModel(nn.Module):
             residual, delta = layer.forward_residual(residual, delta, position_embeddings, cache)
         return self.norm.fused(residual, delta)[1]
 
-    def blend_alpha(self) -> torch.Tensor:
+    def blend_alpha(self, kv_dtype=torch.bfloat16) -> torch.Tensor:
+        """Every layer's blend weights [L, Hkv] for a ``kv_dtype`` cache (cached; a state-dict
+        load through ``load_reference_state_dict`` resets it)."""
         cached = getattr(self, "_alpha", None)
-        if cached is None:
-            cached = torch.stack([l.self_attn.blend_alpha() for l in self.layers]).contiguous()
+        if cached is None or cached[0] != kv_dtype:
+            cached = (kv_dtype, torch.stack([l.self_attn.blend_alpha(kv_dtype) for l in self.layers]).contiguous())
             self._alpha = cached
-        return cached
+        return cached[1]
 
 
 class LastKVForCausalLM(nn.Module):
@@ -564,6 +582,9 @@ class LastKVForCausalLM(nn.Module):
         return self
 
     def new_cache(self, batch: int, max_tokens: int, **kw) -> PagedLastKVCache:
+        """A paged cache for this model: fp32 keys and values for an fp32 model (the
+        reference's fp32 arithmetic end to end), bf16 otherwise."""
+        kw.setdefault("dtype", torch.float32 if self.lm_head.weight.dtype == torch.float32 else torch.bfloat16)
         return PagedLastKVCache(self.config, batch, max_tokens, device=self.lm_head.weight.device, **kw)
 
     def forward(self, input_ids, past_key_values: PagedLastKVCache, logits_to_keep: int = 0):

@@ -20,6 +20,8 @@ from .contract import PAGE_SIZE, RMarinBackendContractError, require_heads
 
 # lkv_decode_paged / lkv_decode_paged_cp flag (include/lastkv_b200.h): the tables predate the PDL chain
 DECODE_TABLES_READY = 1
+# lkv_rope_norm_append flag: every tensor fp32 (the fp32 model configuration)
+APPEND_FP32 = 4
 
 
 def _ptr(t):
@@ -51,6 +53,14 @@ def _traced(fn):
             return fn(*args, **kwargs)
 
     return wrapper
+
+
+def _check_pool_f32(pool_k, pool_v):
+    _require(pool_k.is_cuda and pool_v.is_cuda, "pools must be CUDA tensors")
+    _require(pool_k.dtype == torch.float32 and pool_v.dtype == torch.float32, "pools must be fp32")
+    _require(pool_k.dim() == 4 and pool_k.shape == pool_v.shape, "pools must be [pages, 16, Hkv, D] and equal")
+    _require(pool_k.shape[1] == PAGE_SIZE, f"page size must be {PAGE_SIZE}")
+    _require(pool_k.is_contiguous() and pool_v.is_contiguous(), "pools must be contiguous")
 
 
 def _check_pool(pool_k, pool_v):
@@ -259,6 +269,46 @@ def merge_partials_packed(parts, T: int, Hq: int, D: int, *, out_scale=None, out
 
 
 @_traced
+def attention_paged_f32(q, pool_k, pool_v, block_table, seq_k, cu_q, *, causal=True, softmax_scale=None,
+                        out=None, lse=None, out_scale=None, error_word=None, max_pages: int | None = None):
+    """The merged attention call for fp32 models (lkv_attention_paged_f32): decode (one
+    token per sequence) or chunked-prefill spans over fp32 pools, bottom-right causal.
+
+    q [T, Hq, D] fp32 rows; pools fp32 [pages, 16, Hkv, D]; block_table int32 [B, W];
+    seq_k int32 [B]; cu_q int32 [B+1]; out_scale fp32 [Hq] or None.  Returns out
+    [T, Hq, D] fp32.
+    """
+    _check_pool_f32(pool_k, pool_v)
+    T, Hq, D = q.shape
+    Hkv = pool_k.shape[2]
+    _require(Hq % Hkv == 0 and D in (64, 128) and pool_k.shape[3] == D, "heads / head_dim")
+    _require(q.dtype == torch.float32 and q.stride(2) == 1 and q.stride(1) == D, "q must be fp32 [T, Hq, D] rows")
+    _require(block_table.dtype == torch.int32 and block_table.stride(1) == 1, "block_table must be int32 [B, W]")
+    _require(cu_q.dtype == torch.int32 and seq_k.dtype == torch.int32, "cu_q / seq_k must be int32")
+    B = cu_q.numel() - 1
+    W = int(max_pages if max_pages is not None else block_table.shape[1])
+    _require(W <= block_table.shape[1], "max_pages exceeds block_table width")
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.float32, device=q.device)
+    _require(out.dtype == torch.float32 and out.stride(2) == 1 and out.stride(1) == D, "out layout")
+    if error_word is None:
+        error_word = torch.zeros(4, dtype=torch.int32, device=q.device)
+    if out_scale is not None:
+        _require(out_scale.dtype == torch.float32 and out_scale.numel() == Hq, "out_scale must be fp32 [Hq]")
+    if lse is not None:
+        _require(lse.dtype == torch.float32 and lse.is_contiguous() and lse.numel() == T * Hq, "lse [T, Hq] fp32")
+    st = _capi.lib().lkv_attention_paged_f32(
+        q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
+        block_table.stride(0), seq_k.data_ptr(), cu_q.data_ptr(), out.data_ptr(), out.stride(0), _ptr(lse),
+        _ptr(out_scale), B, T, Hq, Hkv, D, W, int(bool(causal)), float(softmax_scale), error_word.data_ptr(),
+        _stream())
+    _capi.check(st, "lkv_attention_paged_f32")
+    return out
+
+
+@_traced
 def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_scale, ring_slot, ring_k, ring_v,
                      src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None, interleaved=False):
     """Fused RoPE -> Q/K RMSNorm -> V/s -> paged append for one layer.
@@ -272,19 +322,28 @@ def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_s
     D = ring_k.shape[-1]
     Hq, Hkv = q.shape[-1] // D, k.shape[-1] // D
     require_heads(Hq, Hkv, D)
+    # bf16 everywhere, or fp32 everywhere (LKV_APPEND_FP32: the fp32 model configuration)
+    dt = ring_k.dtype
+    _require(dt in (torch.bfloat16, torch.float32) and ring_v.dtype == dt, "ring views must be bf16 or fp32")
     for name, t in (("q", q), ("k", k), ("v", v)):
-        _require(t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1, f"{name} must be bf16 [T, H*D] rows")
+        _require(t.dtype == dt and t.dim() == 2 and t.stride(1) == 1, f"{name} must be {dt} [T, H*D] rows")
     _require(ring_slot.dtype == torch.int64, "slots must be int64")
     if cos_sin is not None:  # None: use_nope (no rotary)
         _require(positions.dtype == torch.int64, "positions must be int64")
         _require(cos_sin.dtype in (torch.bfloat16, torch.float32) and cos_sin.stride(1) == 1
                  and cos_sin.shape[-1] == D, "cos_sin must be bf16 or fp32 [max_pos, D]")
+        _require(dt == torch.bfloat16 or cos_sin.dtype == torch.float32, "the fp32 append takes an fp32 table")
     flags = (1 if interleaved else 0) | (2 if cos_sin is not None and cos_sin.dtype == torch.float32 else 0)
+    if dt == torch.float32:
+        flags |= APPEND_FP32
     _require((q_weight is None) == (k_weight is None), "q/k norm weights come together (None: use_qk_norm=False)")
     if q_weight is not None:
-        _require(q_weight.dtype == torch.bfloat16 and k_weight.dtype == torch.bfloat16, "norm weights must be bf16")
+        _require(q_weight.dtype == dt and k_weight.dtype == dt, f"norm weights must be {dt}")
+    if src_k is not None:
+        _require(src_k.dtype == dt and src_v.dtype == dt, "shared-history views must match the rings' dtype")
     if q_out is None:
-        q_out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
+        q_out = torch.empty((T, Hq, D), dtype=dt, device=q.device)
+    _require(q_out.dtype == dt, "q_out dtype")
     top = src_slot is not None
     st = _capi.lib().lkv_rope_norm_append(
         q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), _ptr(positions),
@@ -322,18 +381,23 @@ def gather_blend(pool_k, pool_v, dst, src_a, src_b, alpha_row, alpha, *, error_w
 def blend_chunk(pool_k, pool_v, raw_pages, ring_pages, ring_layer_stride: int, alpha, *, error_word=None):
     """Commit a finished chunk into every layer ring (K and V/s) in place.
 
-    raw_pages / ring_pages int32 [S, C/16]; alpha fp32 [L, Hkv] (bf16-exact).
+    raw_pages / ring_pages int32 [S, C/16]; alpha fp32 [L, Hkv] (bf16-exact for
+    bf16 pools; the fp32 sigmoid for fp32 pools, which take lkv_blend_chunk_f32).
     """
-    _check_pool(pool_k, pool_v)
+    fn = _capi.lib().lkv_blend_chunk
+    if pool_k.dtype == torch.float32:
+        _check_pool_f32(pool_k, pool_v)
+        fn = _capi.lib().lkv_blend_chunk_f32
+    else:
+        _check_pool(pool_k, pool_v)
     S, ppc = raw_pages.shape
     L, Hkv = alpha.shape
     _require(ring_pages.shape == raw_pages.shape, "ring_pages must match raw_pages")
     _require(raw_pages.dtype == torch.int32 and ring_pages.dtype == torch.int32, "page lists must be int32")
     _require(alpha.dtype == torch.float32 and alpha.is_contiguous(), "alpha must be fp32 [L, Hkv]")
-    st = _capi.lib().lkv_blend_chunk(pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0],
-                                     raw_pages.contiguous().data_ptr(), ring_pages.contiguous().data_ptr(),
-                                     int(ring_layer_stride), alpha.data_ptr(), L, S, ppc, Hkv, pool_k.shape[3],
-                                     _ptr(error_word), _stream())
+    st = fn(pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], raw_pages.contiguous().data_ptr(),
+            ring_pages.contiguous().data_ptr(), int(ring_layer_stride), alpha.data_ptr(), L, S, ppc, Hkv,
+            pool_k.shape[3], _ptr(error_word), _stream())
     _capi.check(st, "lkv_blend_chunk")
 
 

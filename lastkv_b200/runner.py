@@ -48,7 +48,7 @@ class GraphDecodeRunner:
                     "done": None} for _ in range(self.NSETS)]
         self._set = 0
         self.graph = None
-        self.alpha = model.model.blend_alpha()
+        self.alpha = model.model.blend_alpha(cache.dtype)
 
     def _prepare(self):
         """Host plan of the next token -> static device buffers (stream-ordered copies)."""

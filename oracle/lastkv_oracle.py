@@ -159,6 +159,33 @@ def blend_chunk(ring, raw, alpha) -> np.ndarray:
     return bf16_round(t1 + t3)
 
 
+def rope_hf_f32(x, cos, sin) -> np.ndarray:
+    """fp32 ``apply_rotary_pos_emb`` as the HF module evaluates it (modeling.py:105):
+    ``x*cos + rotate_half(x)*sin``, each product and the sum rounded to fp32.
+    ``cos``/``sin`` hold the D/2 distinct frequencies."""
+    x = _f32(x)
+    half = x.shape[-1] // 2
+    xf, yf = x[..., :half], x[..., half:]
+    c, s = _f32(cos), _f32(sin)
+    return np.concatenate([xf * c + (-yf) * s, yf * c + xf * s], axis=-1).astype(np.float32)
+
+
+def rms_norm_hf_f32(x, weight, eps: float) -> np.ndarray:
+    """fp32 ``LlamaRMSNorm`` (modeling.py:90-91, 106): ``w * (x * (1/sqrt(mean(x^2) + eps)))``
+    in fp32 (the mean summed in float64 here; the kernel's fp32 order differs by an ulp)."""
+    x = _f32(x)
+    var = ((x.astype(np.float64) ** 2).sum(-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
+    return (_f32(weight) * (x * inv)).astype(np.float32)
+
+
+def blend_chunk_f32(ring, raw, alpha) -> np.ndarray:
+    """fp32 recent-chunk blend ``a*top + (1-a)*layer`` (modeling.py:115-119 in fp32): the two
+    products and their sum each rounded to fp32.  ring [L, C, H, D], raw [C, H, D], alpha [L, H]."""
+    a = _f32(alpha)[:, None, :, None]
+    return (a * _f32(raw)[None] + (np.float32(1.0) - a) * _f32(ring)).astype(np.float32)
+
+
 def alpha_from_logits(logits) -> np.ndarray:
     """``sigmoid`` evaluated on bf16 logits and rounded to bf16 (batching.py:1067-1079)."""
     x = bf16_round(logits).astype(np.float64)
