@@ -232,6 +232,7 @@ class PagedLastKVCache:
         self.batch = batch
         self.max_tokens = max_tokens
         self.hkv, self.d = config.num_key_value_heads, config.head_dim
+        self._hq = config.num_attention_heads
         self.seen_tokens = 0
         self.committed = 0
         device = torch.device(device or "cuda")
@@ -258,6 +259,44 @@ class PagedLastKVCache:
         self.workspace = ops.Workspace.for_decode(batch, config.num_attention_heads, self.d,
                                                   self.pages_per_seq + self.ring_pages, device=device) \
             if dtype == torch.bfloat16 else None
+        self._meta = None
+
+    # -- capacity
+    def reserve(self, max_tokens: int) -> None:
+        """Grow the cache to hold ``max_tokens`` tokens per sequence, keeping its contents:
+        a new pool with ``ceil(max_tokens / 16)`` shared pages per sequence (in sequence
+        order), the old shared pages and every layer ring copied over (for callers that
+        do not know the final length up front, such as ``generate``).  Allocates; not
+        for use inside a CUDA-graph capture."""
+        if max_tokens <= self.max_tokens:
+            return
+        B, L, P = self.batch, self.num_layers, PAGE_SIZE
+        pps = -(-max_tokens // P)
+        src_pages = B * pps
+        num_pages = src_pages + L * self.ring_stride
+        table = np.arange(src_pages, dtype=np.int32).reshape(B, pps)
+        ring_base = src_pages + np.arange(L) * self.ring_stride
+        old_idx = [self.src_table.reshape(-1)] + [self.ring_base[l] + np.arange(self.ring_stride) for l in range(L)]
+        new_idx = [table[:, : self.pages_per_seq].reshape(-1)] + [ring_base[l] + np.arange(self.ring_stride)
+                                                                   for l in range(L)]
+        o = torch.from_numpy(np.concatenate(old_idx).astype(np.int64)).to(self.device)
+        n = torch.from_numpy(np.concatenate(new_idx).astype(np.int64)).to(self.device)
+        shape = (num_pages, P, self.hkv, self.d)
+        for name in ("pool_k", "pool_v"):
+            old = getattr(self, name)
+            new = torch.zeros(shape, dtype=self.dtype, device=self.device)
+            new[n] = old.index_select(0, o)
+            setattr(self, name, new)
+        self.max_tokens = max_tokens
+        self.pages_per_seq = pps
+        self.src_pages = src_pages
+        self.num_pages = num_pages
+        self.src_table = table
+        self.src_table_dev = torch.from_numpy(table).to(self.device)
+        self.ring_base = ring_base
+        self.ring_base_dev = torch.from_numpy(ring_base.astype(np.int32)).to(self.device)
+        if self.workspace is not None:
+            self.workspace = ops.Workspace.for_decode(B, self._hq, self.d, pps + self.ring_pages, device=self.device)
         self._meta = None
 
     # -- reference API
@@ -521,21 +560,33 @@ class LastKVModel(nn.Module):
         self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.rotary_emb = RotaryEmbedding(config)
 
-    def forward(self, input_ids, cache: PagedLastKVCache):
-        """Chunk loop of modeling.py:194-208: split at chunk boundaries, commit after all layers."""
-        hidden = self.embed_tokens(input_ids)
+    def forward(self, input_ids, cache: PagedLastKVCache, *, inputs_embeds=None, position_ids=None):
+        """Chunk loop of modeling.py:194-208: split at chunk boundaries, commit after all layers.
+        ``position_ids`` [1 or B, length] (default: the cache positions) drive the rotary
+        tables only, as in the reference (modeling.py:188-195)."""
+        hidden = self.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
         B, length, _ = hidden.shape
         if not length:
             raise ValueError("At least one new token is required")
         if cache.chunk_size != self.config.chunk_size or cache.num_layers != len(self.layers):
             raise ValueError("Cache architecture does not match this model")
+        if position_ids is not None:
+            position_ids = position_ids[None, :] if position_ids.ndim == 1 else position_ids
+            if position_ids.shape[-1] != length or position_ids.shape[0] not in (1, B):
+                raise ValueError("position_ids must describe the new input tokens")
+            if position_ids.shape[0] != 1 and not bool((position_ids == position_ids[:1]).all()):
+                raise RMarinBackendContractError("the paged cache advances all sequences together: "
+                                                 "position_ids must be equal across the batch")
         C = self.config.chunk_size
         outputs = []
         start = 0
         while start < length:
             take = min(length - start, C - cache.seen_tokens % C)
             chunk = hidden[:, start:start + take]
-            pos = torch.arange(cache.seen_tokens, cache.seen_tokens + take, device=hidden.device)[None]
+            if position_ids is None:
+                pos = torch.arange(cache.seen_tokens, cache.seen_tokens + take, device=hidden.device)[None]
+            else:
+                pos = position_ids[:1, start:start + take].to(hidden.device)
             position_embeddings = self.rotary_emb(chunk, pos)
             cache.plan(take)
             outputs.append(self.run_layers(chunk, position_embeddings, cache))

@@ -270,9 +270,15 @@ class SharedKVFastPath:
         return {"uniform": uniform, "batch": batch, "tokens": tok, "max_q": max_q, "ring": ring, "src": src,
                 "pos": pos, "cu": cu, "seqk": seqk, "nsrc": nsrc, "bt": bt, "commits": commits}
 
-    def prepare(self, spans: list[Span], num_reqs_padded: int | None = None) -> bool:
+    def prepare_dummy(self, num_reqs: int) -> bool:
+        """A uniform decode step whose rows all read and write the scratch pages
+        (``prepare_dummy``, fastpath.py:584-600): vLLM's warm-up and CUDA-graph
+        capture runs, which have no real requests."""
+        return self.prepare([], max(1, int(num_reqs)), dummy=True)
+
+    def prepare(self, spans: list[Span], num_reqs_padded: int | None = None, *, dummy: bool = False) -> bool:
         """Host prologue of one step (``prepare_real``, fastpath.py:456-582)."""
-        if not spans:
+        if not spans and not dummy:
             self.active = False
             return False
         if self.pool.alpha is None or self.layers is None:

@@ -142,3 +142,50 @@ def test_merged_check_switch_reports_two_pass_agreement(small_d128, monkeypatch,
     worst = max(r["rel"] for r in fast.check_log)
     assert worst < 0.02, fast.check_log
     assert "rmarin_merged_check" in capsys.readouterr().out
+
+
+def test_plugin_backend_reproduces_reference_calls(small_d128):
+    """The same recorded calls through the reference's backend surface: the lean metadata
+    builder (vLLM's per-step build -> host prologue) and RMarinFlashInferImpl.forward
+    (vLLM's per-layer call) of ``lastkv_b200.vllm_plugin``, with vLLM's modules faked at the
+    pinned signatures and the real fast path and kernels underneath."""
+    import types
+
+    from lastkv_b200 import vllm_plugin
+    from lastkv_b200.vllm_backend import rope_cos_sin_cache
+    from tests.test_vllm_plugin_cpu import _fake_runtime, _metadata, _versions
+
+    data = small_d128
+    L, C = int(data["num_layers"]), int(data["chunk"])
+    hq, hkv, d = int(data["num_heads"]), int(data["num_kv_heads"]), int(data["head_dim"])
+    B, T = data["tokens"].shape
+    pool, fast = _fast(L, B, T, C, hkv, hq, d, np.random.default_rng(3).permutation(B * (-(-T // 16))))
+    pool.bind_parameters(torch.from_numpy(data["alpha_logits"]), torch.from_numpy(data["v_scale"]), hq)
+    fast.register_layers([(torch.from_numpy(data["q_norm_w"][l]).cuda(), torch.from_numpy(data["k_norm_w"][l]).cuda())
+                          for l in range(L)], rope_cos_sin_cache(T, d, float(data["rope_theta"])), float(data["eps"]))
+    vllm_plugin._LEAN_BUILDER = None
+    cfg = types.SimpleNamespace(model_config=types.SimpleNamespace(hf_config=types.SimpleNamespace(chunk_size=C)))
+    importer, _ = _fake_runtime(config=cfg)
+    backend, impl_cls = vllm_plugin.build_vllm_backend_types(importer=importer, version_getter=_versions())
+    vllm_plugin.install_fast_path(fast)
+    try:
+        builder = backend.get_builder_cls()(None, [f"l{l}" for l in range(L)], cfg, "cuda")
+        impl = impl_cls(hq, d, d ** -0.5, hkv, None, None, "auto", None, "decoder", None, None)
+        md = None
+        for rec in golden_calls(data):
+            layer, start, lq = rec["layer"], rec["start"], rec["lq"]
+            if layer == 0:
+                md = builder.build(0, _metadata([lq] * B, [start + lq] * B))
+            q = torch.from_numpy(rec["q_proj"].reshape(B * lq, hq * d)).cuda().bfloat16()
+            k = torch.from_numpy(rec["k_proj"].reshape(B * lq, hkv * d)).cuda().bfloat16()
+            v = torch.from_numpy(rec["v_proj"].reshape(B * lq, hkv * d)).cuda().bfloat16()
+            out = torch.full((B * lq + 3, hq * d), float("nan"), dtype=torch.bfloat16, device="cuda")  # padded
+            impl.forward(types.SimpleNamespace(rmarin_layer_index=layer), q, k, v, None, md, out)
+            exp = rec["out"].transpose(0, 2, 1, 3).reshape(B * lq, hq, d)
+            assert_close_bf16(out[: B * lq].view(-1, hq, d).float().cpu().numpy(), exp,
+                              what=f"plugin layer {layer} @ {start} x {lq}")
+            assert bool((out[B * lq:] == 0).all())
+        fast.check_errors()
+    finally:
+        vllm_plugin.uninstall_fast_path()
+        vllm_plugin._LEAN_BUILDER = None
