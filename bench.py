@@ -525,21 +525,25 @@ def run_ours(args):
     # A serving loop: each step's queries are uploaded and its outputs downloaded on a copy
     # stream, overlapping the neighbouring steps' attention (double-buffered q and out);
     # the small per-step tables go in-line on the compute stream.
-    copy = torch.cuda.Stream(device=device)
+    # Uploads and downloads go on two streams of their own: on one, the next step's upload
+    # would queue behind this step's download, which waits for this step to finish.
+    up_stream, down_stream = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
     q_dev = [wl["q"], torch.empty_like(wl["q"])]
     out_dev = [wl["out"], torch.empty_like(wl["out"])]
     ev_h2d = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_d2h = [torch.cuda.Event(), torch.cuda.Event()]
     ev_done = [torch.cuda.Event(), torch.cuda.Event()]
 
     def upload(k):
-        with torch.cuda.stream(copy):
-            copy.wait_event(ev_done[k])  # the step that last read q_dev[k] has finished
+        with torch.cuda.stream(up_stream):
+            up_stream.wait_event(ev_done[k])  # the step that last read q_dev[k] has finished
             q_dev[k].copy_(q_host, non_blocking=True)
-            ev_h2d[k].record(copy)
+            ev_h2d[k].record(up_stream)
 
     def e2e_step(i, n):
         k = i % 2
         stream.wait_event(ev_h2d[k])
+        stream.wait_event(ev_d2h[k])  # the download that last read out_dev[k] has finished
         wl["bt"].copy_(bt_host, non_blocking=True)
         wl["nsrc"].copy_(nsrc_host, non_blocking=True)
         wl["seq_k"].copy_(seqk_host, non_blocking=True)
@@ -549,9 +553,10 @@ def run_ours(args):
             ops.decode_paged(q_dev[k][l], wl["pool_k"], wl["pool_v"], wl["bt_all"][l], wl["seq_k"],
                              out=out_dev[k][l], out_scale=wl["out_scale"][l], workspace=wl["ws"], max_pages=wl["W"])
         ev_done[k].record(stream)
-        with torch.cuda.stream(copy):
-            copy.wait_event(ev_done[k])
+        with torch.cuda.stream(down_stream):
+            down_stream.wait_event(ev_done[k])
             out_host.copy_(out_dev[k], non_blocking=True)  # this step's result to the host
+            ev_d2h[k].record(down_stream)
         if i + 1 < n:
             upload(1 - k)                                   # the next step's queries
 
@@ -559,14 +564,15 @@ def run_ours(args):
         upload(0)
         for i in range(n):
             e2e_step(i, n)
-        stream.wait_stream(copy)  # the last download is part of the run
+        stream.wait_stream(down_stream)  # the last download is part of the run
 
     e2e_run(max(args.warmup, 1))
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    copy.wait_event(e0)  # the first upload starts inside the timed region
+    up_stream.wait_event(e0)  # the first upload starts inside the timed region
+    down_stream.wait_event(e0)
     e2e_run(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
