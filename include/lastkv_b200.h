@@ -397,10 +397,15 @@ int lkv_cp_combine_sizes(int64_t rows, int head_dim, int world, int64_t* send_fl
  * kernel, as each (sequence, KV head) finishes, merges that unit's splits and
  * pushes the merged rows to every rank's receive buffer (the same {value,
  * epoch} words lkv_cp_combine pushes, so the transfer overlaps the rest of the
- * decode), then lkv_cp_combine with send = NULL polls and merges the `world`
- * ranks' rows in rank order into `out` (x out_scale).  Two launches, no merge
- * launch and no collective call; the result equals lkv_decode_paged (partial)
- * + all-gather + lkv_merge_partials bit for bit.  peer_recv / recv sizes as for
+ * decode), then the `world` ranks' rows are polled and merged in rank order
+ * into `out` (x out_scale).  When no CTA of the decode's persistent grid takes
+ * more than 32 work items (every shape of the 128K configuration), that poll
+ * and merge runs inside the decode kernel itself: the CTA that pushed a
+ * (sequence, KV head) unit, once its own items are done, polls that unit's rows
+ * from every rank and writes them - one launch per call.  Otherwise a
+ * lkv_cp_combine launch with send = NULL does it - two launches.  No merge
+ * launch and no collective call either way; the result equals
+ * lkv_decode_paged (partial) + all-gather + lkv_merge_partials bit for bit.  peer_recv / recv sizes as for
  * lkv_cp_combine (rows = batch * num_q_heads); `workspace` as for
  * lkv_decode_paged; state: lkv_decode_cp_state_words uint32 of device memory
  * (8-byte aligned, zero before the first call; every completed call leaves it

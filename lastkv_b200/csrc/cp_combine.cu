@@ -29,6 +29,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "cp_words.cuh"
 #include "kernels.h"
 #include "launch.cuh"
 
@@ -56,34 +57,9 @@ struct CpParams {
   int* err;
 };
 
-__device__ __forceinline__ uint64_t ll_word(float v, uint32_t epoch) {
-  return ((uint64_t)epoch << 32) | (uint64_t)__float_as_uint(v);
-}
-
-__device__ __forceinline__ void st_ll2(uint64_t* dst, uint64_t a, uint64_t b) {
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
-}
-
-__device__ __forceinline__ uint64_t ld_ll(const uint64_t* src) {
-  uint64_t v;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
-  return v;
-}
-
-// Poll one word until it carries `epoch` (or the wall-time limit passes: then `fail` is set).
-__device__ __forceinline__ float ll_take(const uint64_t* src, uint32_t epoch, uint64_t start, bool& fail) {
-  uint64_t w = ld_ll(src);
-  for (uint32_t it = 1; (uint32_t)(w >> 32) != epoch && !fail; ++it) {
-    if ((it & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) fail = true;
-    w = ld_ll(src);
-  }
-  return __uint_as_float((uint32_t)w);
-}
-
 template <int D>
 __global__ void __launch_bounds__(kCpThreads)
     cp_combine_kernel(const __grid_constant__ CpPeers peers, const __grid_constant__ CpParams p) {
-  constexpr int PER = D / 32;
   pdl_launch_dependents();
   pdl_wait();  // the partial comes from the decode kernel (and the previous call's epoch update)
   // This call's epoch: one more than the previous call's.  Every CTA reads it
@@ -116,47 +92,9 @@ __global__ void __launch_bounds__(kCpThreads)
   const uint64_t* slot_base = peers.recv[p.rank] + (int64_t)slot * p.world * p.part_words;
   const uint64_t start = global_timer_ns();
   bool fail = false;
-  constexpr float to2 = 1.4426950408889634f;
-  for (int64_t row = r0 + warp; row < r1; row += kCpThreads / 32) {
-    auto lse_of = [&](int s) -> float {
-      return (s == p.rank && p.send) ? p.send[lse_off + row]
-                                     : ll_take(slot_base + (int64_t)s * p.part_words + lse_off + row, epoch, start, fail);
-    };
-    float M = -INFINITY;
-    for (int s = lane; s < p.world; s += 32) M = fmaxf(M, lse_of(s) * to2);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float acc[PER];
-#pragma unroll
-    for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-    float L = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < p.world; ++s) {
-        const float ls = lse_of(s) * to2;
-        if (ls == -INFINITY) continue;
-        const float w = exp2f(ls - M);
-        L += w;
-        float v[PER];
-        if (s == p.rank && p.send) {
-#pragma unroll
-          for (int e = 0; e < PER; ++e) v[e] = p.send[row * D + lane * PER + e];
-        } else {
-          const uint64_t* src = slot_base + (int64_t)s * p.part_words + row * D + lane * PER;
-#pragma unroll
-          for (int e = 0; e < PER; ++e) v[e] = ll_take(src + e, epoch, start, fail);
-        }
-#pragma unroll
-        for (int e = 0; e < PER; ++e) acc[e] += w * v[e];
-      }
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int h = (int)(row % p.Hq);
-    const int64_t tok = row / p.Hq;
-    const float sc = (p.out_scale ? p.out_scale[h] : 1.f) * inv;
-    __nv_bfloat16* dst = p.out + tok * p.out_stride_tok + (int64_t)h * D + lane * PER;
-#pragma unroll
-    for (int e = 0; e < PER; e += 2) *reinterpret_cast<uint32_t*>(dst + e) = pack_bf16(acc[e] * sc, acc[e + 1] * sc);
-  }
+  for (int64_t row = r0 + warp; row < r1; row += kCpThreads / 32)
+    cp_merge_row<D>(slot_base, p.part_words, p.world, p.rank, p.send, p.rows, row, p.Hq, p.out_scale, p.out,
+                    p.out_stride_tok, epoch, start, fail, lane);
   if (fail) report_error(p.err, DEVERR_WAIT_TIMEOUT, kCpKernelId, (int)r0);
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(p.state + 1, 1u) == gridDim.x - 1) {

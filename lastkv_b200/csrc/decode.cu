@@ -32,6 +32,7 @@
 #include <climits>
 
 #include "common.cuh"
+#include "cp_words.cuh"
 #include "kernels.h"
 #include "launch.cuh"
 
@@ -60,10 +61,20 @@ struct DecodeParams {
   // Context parallel: the last CTA to finish a (sequence, KV head) unit merges its
   // split partials and pushes the merged rows to every rank's receive buffer.
   uint64_t* cp_recv[kCpMaxRanks];
-  uint32_t* cp_state;      // [0] epoch of the previous call, [2 + unit] arrivals (null: no push)
+  uint32_t* cp_state;      // [0] epoch of the previous call, [1] CTAs done, [2 + unit] arrivals (null: no push)
   int64_t cp_part_words;   // words per rank partial in a receive slot
   int cp_rank, cp_world;
+  // Fused exchange: after its own items, a CTA counts its units' arrivals once; the
+  // last CTA of a unit pushes the unit's merged rows to every rank, then polls the
+  // unit's rows from every rank, merges them in rank order and writes `out` (x
+  // out_scale); the last CTA to finish advances the epoch.  No combine launch.
+  int cp_fused;
+  int* cp_err;
 };
+
+// Items a CTA may complete after its item loop in the fused context-parallel
+// exchange; the host uses that form only when no CTA takes more items than this.
+constexpr int kMaxTouched = 32;
 
 // Exact LSE merge of one row's S partials (S <= 32): lane s holds part s's LSE,
 // so the accumulation loop has no load-dependent branch and its part loads are
@@ -117,6 +128,32 @@ __device__ __forceinline__ void merge_row_parts(const float* o_base, int64_t o_s
   lse2 = L > 0.f ? M + log2f(L) : -INFINITY;
 }
 
+// Context parallel: merge one row's S split partials (merge_partials_kernel's
+// arithmetic) and push it as {value, epoch} words into every rank's receive slot
+// [epoch & 1][this rank] - the words cp_combine_kernel's push writes.  One warp.
+template <int D>
+__device__ __forceinline__ void cp_push_row(const DecodeParams& p, int64_t row, uint32_t epoch, int lane) {
+  constexpr int PER = D / 32;
+  float acc[PER];
+  float inv, lse2;
+  merge_row_parts<D>(p.part_o + row * p.S * D, D, p.part_lse + row * p.S, 1, p.S, 1.f, lane, acc, inv, lse2);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) acc[e] = acc[e] * inv;  // as merge_partials_kernel's fp32 output
+  const float lse_e = lse2 * 0.6931471805599453f;
+  const int64_t rows = (int64_t)p.B * p.Hq;
+  const int slot = (int)(epoch & 1u);
+  for (int r = 0; r < p.cp_world; ++r) {
+    uint64_t* dst = p.cp_recv[r] + ((int64_t)slot * p.cp_world + p.cp_rank) * p.cp_part_words;
+    uint64_t* od = dst + row * D + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) st_ll2(od + e, ll_word(acc[e], epoch), ll_word(acc[e + 1], epoch));
+    if (lane == 0) {
+      const uint64_t wl = ll_word(lse_e, epoch);
+      asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst + rows * D + row), "l"(wl) : "memory");
+    }
+  }
+}
+
 template <int D, int NW, int STAGES>
 struct DecodeCfg {
   static constexpr int HALVES = D / 64;
@@ -127,7 +164,8 @@ struct DecodeCfg {
   static constexpr int DATA_BYTES = STAGES * STAGE_BYTES;
   // merge area after the ring: o [NW][4 heads][OSTRIDE], then m and l [NW][8]
   static constexpr int MERGE_BYTES = NW * 4 * OSTRIDE * 4 + 2 * NW * 8 * 4;
-  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + MERGE_BYTES + 2 * STAGES * 8 + 16;  // + failure / last flags
+  // + failure / last flags, the completion count, unit list and last flags
+  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + MERGE_BYTES + 2 * STAGES * 8 + 32 + 2 * kMaxTouched * 4;
 };
 
 __device__ __forceinline__ float warp_max_g(float v) {
@@ -160,6 +198,10 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   uint64_t* empty = full + STAGES;
   volatile int* fail_flag = reinterpret_cast<volatile int*>(empty + STAGES);
   volatile int* last_flag = fail_flag + 1;
+  // fused exchange: the units of this CTA's items and which of them it completes
+  volatile int* n_touched = fail_flag + 4;
+  volatile int* touched = n_touched + 4;
+  volatile int* last_of = touched + kMaxTouched;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
@@ -176,6 +218,7 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       mbar_init(&empty[s], NW);
     }
     *fail_flag = 0;
+    *n_touched = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -463,11 +506,14 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       // the area (and mm / ml) is rewritten by the next chunk or item
       asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
     }
-    if (p.cp_state) {
-      // Context parallel: count this split; the unit's last CTA merges the S
-      // partials (merge_partials_kernel's arithmetic) and pushes the merged rows
-      // as {value, epoch} words into every rank's receive slot, as
-      // cp_combine_kernel's push would.
+    if (p.cp_fused) {
+      // completion after the item loop: remember the unit (the barrier above has
+      // ordered this CTA's partial writes; the list is read after the next barrier)
+      if (threadIdx.x == 0) touched[(*n_touched)++] = b * p.Hkv + hk;
+    } else if (p.cp_state) {
+      // Context parallel, more items per CTA than the list holds: count this split
+      // now; the unit's last CTA merges the S partials (merge_partials_kernel's
+      // arithmetic) and pushes the merged rows, and a cp_combine launch follows.
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
       uint32_t* arrivals = p.cp_state + 2 + (int64_t)b * p.Hkv + hk;
@@ -475,35 +521,59 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
       if (*last_flag) {
         __threadfence();
-        const int64_t rows = (int64_t)p.B * p.Hq;
-        const int slot = (int)(cp_epoch & 1u);
-        for (int h = warp; h < GROUP; h += NW) {
-          const int64_t row = (int64_t)b * p.Hq + hk * GROUP + h;
-          float acc[D / 32];
-          float inv, lse2;
-          merge_row_parts<D>(p.part_o + row * p.S * D, D, p.part_lse + row * p.S, 1, p.S, 1.f, lane, acc, inv, lse2);
-#pragma unroll
-          for (int e = 0; e < D / 32; ++e) acc[e] = acc[e] * inv;  // as merge_partials_kernel's fp32 output
-          const float lse_e = lse2 * 0.6931471805599453f;
-          for (int r = 0; r < p.cp_world; ++r) {
-            uint64_t* dst = p.cp_recv[r] + ((int64_t)slot * p.cp_world + p.cp_rank) * p.cp_part_words;
-            uint64_t* od = dst + row * D + lane * (D / 32);
-#pragma unroll
-            for (int e = 0; e < D / 32; e += 2) {
-              const uint64_t w0 = ((uint64_t)cp_epoch << 32) | (uint64_t)__float_as_uint(acc[e]);
-              const uint64_t w1 = ((uint64_t)cp_epoch << 32) | (uint64_t)__float_as_uint(acc[e + 1]);
-              asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(od + e), "l"(w0), "l"(w1) : "memory");
-            }
-            if (lane == 0) {
-              const uint64_t wl = ((uint64_t)cp_epoch << 32) | (uint64_t)__float_as_uint(lse_e);
-              asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst + rows * D + row), "l"(wl) : "memory");
-            }
-          }
-        }
+        for (int h = warp; h < GROUP; h += NW) cp_push_row<D>(p, (int64_t)b * p.Hq + hk * GROUP + h, cp_epoch, lane);
         asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
         if (threadIdx.x == 0) *arrivals = 0u;  // every split has arrived: ready for the next call
       }
     }
+  }
+  if (!p.cp_fused) return;
+
+  // ---------------------------------------------------------------- fused exchange
+  // One fence and one round of arrival counting per CTA, after all its items (a
+  // fence and two barriers per item stall the consumers while the ring waits).
+  // The last CTA to count a unit merges the unit's S split partials
+  // (merge_partials_kernel's arithmetic) and pushes the merged rows to every
+  // rank; then it polls the unit's rows from every rank and merges them in rank
+  // order into `out`.  A CTA polls only after all its items and pushes are done,
+  // and only for pushes other GPUs' CTAs make without waiting: no wait cycle.
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  const int n_items_cta = *n_touched;
+  __threadfence();  // this CTA's partials, before the counting makes them another CTA's input
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  uint32_t* counters = p.cp_state + 2;
+  if (threadIdx.x == 0)
+    for (int k = 0; k < n_items_cta; ++k) last_of[k] = atomicAdd(counters + touched[k], 1u) == (uint32_t)(p.S - 1);
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  __threadfence();  // the other CTAs' partials of the units this CTA completes
+  for (int k = 0; k < n_items_cta; ++k) {
+    if (!last_of[k]) continue;
+    const int unit = touched[k];
+    const int b = unit / p.Hkv, hk = unit % p.Hkv;
+    for (int h = warp; h < GROUP; h += NW) cp_push_row<D>(p, (int64_t)b * p.Hq + hk * GROUP + h, cp_epoch, lane);
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  if (threadIdx.x == 0)
+    for (int k = 0; k < n_items_cta; ++k)
+      if (last_of[k]) counters[touched[k]] = 0u;  // every split has arrived: ready for the next call
+  const int64_t rows = (int64_t)p.B * p.Hq;
+  const uint64_t* slot_base = p.cp_recv[p.cp_rank] + (int64_t)(cp_epoch & 1u) * p.cp_world * p.cp_part_words;
+  const uint64_t start = global_timer_ns();
+  bool fail = false;
+  for (int k = 0; k < n_items_cta; ++k) {
+    if (!last_of[k]) continue;
+    const int unit = touched[k];
+    const int b = unit / p.Hkv, hk = unit % p.Hkv;
+    for (int h = warp; h < GROUP; h += NW)
+      cp_merge_row<D>(slot_base, p.cp_part_words, p.cp_world, p.cp_rank, nullptr, rows,
+                      (int64_t)b * p.Hq + hk * GROUP + h, p.Hq, p.out_scale, p.out, p.out_stride_tok, cp_epoch, start,
+                      fail, lane);
+  }
+  if (fail && lane == 0) report_error(p.cp_err, DEVERR_WAIT_TIMEOUT, 1, 2000000 + (int)blockIdx.x);
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  if (threadIdx.x == 0 && atomicAdd(p.cp_state + 1, 1u) == gridDim.x - 1) {
+    p.cp_state[1] = 0u;        // every CTA has read the epoch and counted itself
+    p.cp_state[0] = cp_epoch;  // the next call (stream-ordered after this one) uses the next epoch
   }
 }
 
@@ -661,10 +731,13 @@ int launch_group(const CUtensorMap& tmk, const CUtensorMap& tmv, DecodeParams pr
   const int64_t items = (int64_t)S * prm.Hkv * prm.B;
   if (items > INT_MAX) return LKV_ERR_UNSUPPORTED;
   dim3 grid((unsigned)std::min<int64_t>(items, slots));
+  // context parallel: fuse the exchange into this launch when no CTA takes more items than it can list
+  prm.cp_fused = (cp && (items + grid.x - 1) / grid.x <= kMaxTouched) ? 1 : 0;
+  prm.cp_err = cp ? cp->cp_error : nullptr;
   if (launch_pdl(decode_splitkv_kernel<D, GROUP, kNW, STAGES>, grid, dim3((kNW + 1) * 32), Cfg::SMEM_BYTES, stream,
                  tmk, tmv, prm) != cudaSuccess)
     return LKV_ERR_CUDA;
-  if (prm.final_out) return LKV_OK;
+  if (prm.final_out || prm.cp_fused) return LKV_OK;
   if (cp)  // every rank's merged rows are pushed: poll them and merge in rank order
     return cp_combine(nullptr, cp->cp_recv, cp->cp_rank, cp->cp_world, cp->cp_state, rows, D, prm.Hq,
                       cp->out_scale, cp->out, cp->out_stride_tok, cp->cp_error, stream);

@@ -99,3 +99,33 @@ def test_fused_decode_push_equals_partial_merge_path():
         torch.testing.assert_close(got.view(B, Hq, D), ref.view(B, Hq, D), rtol=0, atol=0)
         st = state.cpu().tolist()
         assert st[0] == call + 1 and st[1] == 0 and all(v == 0 for v in st[2:]), st  # arrivals reset
+
+
+def test_fused_exchange_missing_peer_times_out_into_error_word():
+    """lkv_decode_paged_cp with the exchange fused into the decode kernel (no combine launch):
+    a second "rank" whose receive buffer nobody fills makes every unit's bounded poll give
+    up (~2 s) into the error word, and the context stays usable."""
+    from lastkv_b200 import ops
+    from tests.gpu_helpers import make_paged_case
+
+    B, Hq, Hkv, D = 2, 8, 2, 128
+    t, _ = make_paged_case(41, B, Hq, Hkv, D, [500, 70])
+    rows = B * Hq
+    sizes = ops.cp_combine_sizes(rows, D, 2)
+    mine = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
+    peer = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")  # rank 1 never runs
+    state = torch.zeros(ops.decode_cp_state_words(B, Hkv), dtype=torch.int32, device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws = ops.Workspace.for_decode(B, Hq, D, t["bt"].shape[1], device="cuda")
+    t0 = time.time()
+    ops.decode_paged_cp(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], [mine.data_ptr(), peer.data_ptr()],
+                        0, 2, state, workspace=ws, error_word=err)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    e = err.cpu().tolist()
+    assert e[0] == 1 and e[1] == 1 and e[3] >= 2000000, e  # wait timeout, reported by the decode kernel
+    assert 1.0 < waited < 30.0, waited
+    # this rank's rows reached the "peer" buffer with epoch 1
+    words = peer.view(2, 2, -1)[1, 0, : rows * D].cpu().numpy().astype(np.uint64)
+    assert np.all((words >> np.uint64(32)) == 1)
+    assert float(torch.ones(4, device="cuda").sum()) == 4.0

@@ -180,3 +180,24 @@ def test_decode_reference_golden_calls(small_d128):
             for b in range(B):
                 state.commit_if_boundary(b, start + lq)
     assert checked == 27 * L
+
+
+def test_one_workspace_serves_split_decodes_of_any_batch():
+    """A workspace sized for the largest batch serves split decodes of different batch
+    sizes in any order (the split layout follows each call's rows): each matches the oracle."""
+    from lastkv_b200 import ops
+
+    Hq, Hkv, D = 32, 8, 128
+    ws = ops.Workspace.for_decode(48, Hq, D, 256, device="cuda")
+    for seed, B in ((60, 8), (61, 48), (62, 3), (63, 48), (64, 8)):
+        lens = list(np.random.default_rng(seed).integers(1500, 4000, B))
+        t, n = make_paged_case(seed, B, Hq, Hkv, D, lens)
+        splits, launches = ops.decode_plan(B, Hq, Hkv, D, t["bt"].shape[1], ws)
+        assert splits > 1 and launches == 2, (splits, launches)
+        lse = torch.empty((B, Hq), dtype=torch.float32, device="cuda")
+        out = ops.decode_paged(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], lse=lse, workspace=ws)
+        ref, ref_lse = O.paged_attention(n["q"], n["pool_k"], n["pool_v"], n["bt"], n["seq_k"], n["cu"],
+                                         scale=D ** -0.5)
+        assert_close_bf16(out.float().cpu().numpy(), ref, what=f"batch {B}")
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, rtol=1e-4, atol=1e-3)
+    assert ws.error()[0] == 0
