@@ -44,15 +44,17 @@ def algo_bytes() -> int:
     return 2 * CFG["batch"] * CFG["kv_heads"] * CFG["context"] * CFG["head_dim"] * 2
 
 
-# DRAM read + write bytes of one full-size decode_splitkv launch (config 2): reads
-# 268,564,736 per 8 sequences in the small-case capture (x 8 = 2,148,517,888; the
-# full-size one-pass capture reads 2.15 GB), writes 5.18 MB in the full-size capture
-# (the split partials that leave L2 during the launch).
-NCU_FULL_TRAFFIC = 2_148_517_888 + 5_180_000
+# DRAM read + write bytes of one decode_splitkv launch, from the small-case ncu capture
+# (8 sequences, 2 layers; profiles/decode_splitkv_config2.txt): the mean of two launches,
+# 268,590,080 read + 1,920,896 written (split partials leaving L2), scaled by the
+# sequences a launch processes (x 8 for config 2's 64); the read bytes scale with the
+# sequences, the writes only roughly.
+NCU_SMALL_TRAFFIC = 268_590_080 + 1_920_896
+NCU_SMALL_BATCH = 8
 
 
 def traffic_per_launch() -> int:
-    return NCU_FULL_TRAFFIC * CFG["batch"] // 64
+    return NCU_SMALL_TRAFFIC * CFG["batch"] // NCU_SMALL_BATCH
 
 
 def parse():
@@ -604,7 +606,8 @@ def run_ours(args):
                      "kernel": "decode op = decode_splitkv_kernel + merge_partials_kernel",
                      "algorithmic_bytes_per_launch": algo_bytes(), "avg_launch_ms": avg_op_ms,
                      "traffic": traffic_per_launch(),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch"},
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the small case "
+                                       "(8 sequences), scaled by the sequences per launch"},
         "attn_hbm_gbs": achieved,
         "parity": decode_parity,
         "clocks": clk,
