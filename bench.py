@@ -636,7 +636,7 @@ def run_ours(args):
         c4 = measure_cp(100, 3, world, rank, device, combine=args.cp_combine, eager=args.cp_eager)
         line["cp128k"] = {k: c4[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step",
                                              "scaling", "layer_ms", "hbm_gbs_per_gpu", "hbm_frac_per_gpu",
-                                             "combine_bytes_per_rank_per_layer", "parity")}
+                                             "combine_bytes_per_rank_per_layer", "parity", "error") if k in c4}
         line["cp128k"]["parallelism"] = c4["config"]["parallelism"]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
@@ -794,17 +794,18 @@ def measure_cp(steps: int, warmup: int, world: int, rank: int, device, combine: 
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    if cp is not None:
-        cp.check_errors()
-    if ws.error()[0] != 0:
-        raise RuntimeError(f"context-parallel decode error word set: {ws.error()}")
-    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    # device errors travel with the timing in one all-reduce, so every rank takes the same
+    # collective steps whatever happened on one of them
+    err_words = [ws.error()] + ([st["error"].cpu().tolist() for st in cp._p2p.values()] if cp is not None else [])
+    failed = next((w for w in err_words if w[0] != 0), None)
+    t = torch.tensor([e0.elapsed_time(e1), 1.0 if failed else 0.0], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = float(t[0].item())
+    any_failed = bool(t[1].item())
     del graph, run  # a graph holding collectives goes before the process group
     parity = None
-    if rank == 0:
+    if rank == 0 and not any_failed:
         # the last layer's output of the last step, sequences 0 and B-1, against all ranks' keys
         l = L - 1
         keys = {b: ([], []) for b in (0, B - 1)}
@@ -849,6 +850,8 @@ def measure_cp(steps: int, warmup: int, world: int, rank: int, device, combine: 
             "hbm_frac_per_gpu": bytes_layer / world / (layer_ms * 1e-3) / 1e9 / peak,
             "combine_bytes_per_rank_per_layer": B * Hq * (D + 1) * 4 if world > 1 else 0,
             "parity": parity}
+    if any_failed:
+        line["error"] = f"a rank's device error word was set (this rank: {failed})"
     del cp, pool_k, pool_v, out, ws
     torch.cuda.empty_cache()
     return line
