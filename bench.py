@@ -444,6 +444,106 @@ def measure_wan(device, reps: int = 5, batch: int | None = None, kv_splits: int 
             "kv_splits": splits, "parity": parity}
 
 
+def measure_commit(device, reps: int = 5):
+    """Config 3's chunk-boundary commit (8B shapes: 32 layers, 8 KV heads x 128, chunk 1024,
+    batch 8): the step after the boundary's first-layer append with the blend of every
+    layer's finished chunk fused in (lkv_rope_norm_append_commit), against the append and
+    lkv_blend_chunk as two launches.  The blend is HBM-bound: per page of K or V it reads
+    the shared raw page and the ring page and writes the ring page; the raw pages of one
+    chunk (a few tens of MB) stay in L2 across the layers."""
+    import torch
+
+    from lastkv_b200 import ops
+
+    L, Hq, Hkv, D, C, B = (E2E8B[k] for k in ("layers", "q_heads", "kv_heads", "head_dim", "chunk", "batch"))
+    ppc = C // 16
+    ring_stride = B * 2 * ppc + 1
+    src = B * 2 * ppc
+    total = src + L * ring_stride
+    gen = torch.Generator(device=device).manual_seed(77)
+    pool_k = torch.randn((total, 16, Hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    pool_v = torch.randn((total, 16, Hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    raw = torch.arange(B * ppc, dtype=torch.int32, device=device).view(B, ppc)
+    ring = (src + torch.arange(B, device=device)[:, None] * 2 * ppc
+            + torch.arange(ppc, device=device)[None, :]).to(torch.int32).contiguous()
+    alpha = torch.rand((L, Hkv), generator=gen, device=device).to(torch.bfloat16).float()
+    q = torch.randn((B, Hq * D), generator=gen, device=device).to(torch.bfloat16)
+    k = torch.randn((B, Hkv * D), generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn((B, Hkv * D), generator=gen, device=device).to(torch.bfloat16)
+    pos = torch.full((B,), C, dtype=torch.int64, device=device)
+    cs = torch.randn((C + 1, D), generator=gen, device=device).to(torch.bfloat16)
+    w = torch.ones(D, dtype=torch.bfloat16, device=device)
+    inv = torch.ones(Hkv, dtype=torch.float32, device=device)
+    slot = ((src + torch.arange(B, device=device) * 2 * ppc + ppc) * 16).to(torch.int64)  # second ring half
+    flat_k, flat_v = pool_k.view(-1, Hkv, D), pool_v.view(-1, Hkv, D)
+    err = torch.zeros(4, dtype=torch.int32, device=device)
+    commit = ops.Commit(pool_k, pool_v, raw, ring, ring_stride, alpha)
+
+    def append(c=None):
+        ops.rope_norm_append(q, k, v, pos, cs, w, w, 1e-6, inv, slot, flat_k, flat_v, error_word=err, commit=c)
+
+    def separate():
+        append()
+        ops.blend_chunk(pool_k, pool_v, raw, ring, ring_stride, alpha, error_word=err)
+
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    count = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def timed(fn, n=reps):
+        """Device ms per call: n calls captured in one CUDA graph (no host launch cost), replayed."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(n):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) / n
+
+    sep_ms = timed(separate)
+    fused_ms = timed(lambda: append(commit))
+    # the device-count form a captured step carries every step: its cost without a boundary
+    # (count 0) and its blend time with one (count = batch), at 2 and 8 commit blocks per SM
+    plain_us = timed(append, 50) * 1e3
+    dev_count = {}
+    for per_sm in (2, 8):
+        c = commit._replace(count=count, blocks=per_sm * sms)
+        count.fill_(0)
+        idle_us = timed(lambda: append(c), 50) * 1e3
+        count.fill_(B)
+        dev_count[f"{per_sm}_per_sm"] = {"no_boundary_us": idle_us, "no_boundary_extra_us": idle_us - plain_us,
+                                         "boundary_ms": timed(lambda: append(c))}
+    if int(err[0]):
+        raise RuntimeError(f"commit bench: device error word {err.tolist()}")
+    page_bytes = 16 * Hkv * D * 2
+    # K and V: every layer's ring page read and written, each raw page read once (the other
+    # layers' reads of the chunk's 2 x B x ppc raw pages hit L2)
+    nbytes = B * ppc * L * 2 * 2 * page_bytes + B * ppc * 2 * page_bytes
+    gbs = nbytes / (fused_ms * 1e-3) / 1e9
+    try:
+        peak = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        src_peak = "measured"
+    except (OSError, KeyError, ValueError):
+        peak, src_peak = 6650.0, "fallback"
+    return {"workload": f"boundary commit, 8B shapes: {L} layers x {B} sequences x {ppc} pages of K and V, "
+                        f"fused into the next step's layer-0 append of {B} tokens",
+            "fused_ms": fused_ms, "separate_ms": sep_ms, "saved_us": (sep_ms - fused_ms) * 1e3,
+            "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak,
+            "peak_source": src_peak, "l2": f"{nbytes / 1e9:.1f} GB per launch (larger than L2); no flush",
+            "append_alone_us": plain_us, "device_count": dev_count,
+            "kernel": "append_commit_kernel<128> (vs rope_norm_append_kernel<128> + blend_chunk_kernel)"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -618,6 +718,8 @@ def run_ours(args):
         # the small case (profiler captures) runs the same spans with 2 sequences
         line["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
         line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1, kv_splits=args.wan_kv_splits)
+        line["commit"] = measure_commit(device)
+        torch.cuda.empty_cache()
     if not args.no_e2e8b:
         # config 3 on the same ranks: the 8B architecture end to end (weak scaling, batch 8 per GPU)
         wl = None

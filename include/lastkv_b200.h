@@ -254,6 +254,39 @@ int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_
                          int num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
                          int flags, int32_t* error_word, void* stream);
 
+/* The append of one layer together with the boundary commit of the chunks
+ * that the previous step finished, in one launch (the commit the reference
+ * runs lazily when the next step starts, batching.py:1099-1144, with the
+ * blend_chunk_ arithmetic of fused_qkv.py:158-201; lkv_blend_chunk below
+ * gives its exact form).  The append arguments are lkv_rope_norm_append's
+ * (bf16 only); then the commit of lkv_blend_chunk over rows
+ * [0, num_commit_rows) of raw_pages / ring_pages [num_commit_rows,
+ * pages_per_chunk], or over rows [0, *commit_count) when commit_count (device
+ * int32) is not NULL - so one captured launch serves steps with and without
+ * a boundary (a count above num_commit_rows or below 0 commits nothing and is
+ * recorded in error_word).  commit_blocks = the launch's blocks for the commit,
+ * which stride over the (page, row, layer) items; 0 = one block per item when
+ * commit_count is NULL, else one wave of 8 per SM.
+ * Call it for the first layer of the step after the boundary: every layer's
+ * attention over the unblended chunk has run, and the append writes the other
+ * half of each 2C ring, so no address is both read and written by the launch.
+ * It rewrites pages of every layer's ring as a PDL launch: the decodes of that
+ * step must not pass LKV_DECODE_TABLES_READY (their pages would no longer
+ * predate the last non-PDL operation). */
+int lkv_rope_norm_append_commit(const void* q, int64_t q_row, const void* k, int64_t k_row,
+                                const void* v, int64_t v_row, const int64_t* positions,
+                                const void* cos_sin, int64_t cos_sin_row, int64_t max_position,
+                                const void* q_weight, const void* k_weight, float eps,
+                                const float* inv_scale, void* q_out, int64_t q_out_row,
+                                const int64_t* ring_slot, void* ring_k, void* ring_v, int64_t ring_slots,
+                                const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots,
+                                int num_tokens, int num_q_heads, int num_kv_heads, int head_dim, int flags,
+                                void* pool_k, void* pool_v, int64_t num_pages,
+                                const int32_t* raw_pages, const int32_t* ring_pages,
+                                int64_t ring_layer_stride_pages, const float* alpha, int num_layers,
+                                int num_commit_rows, int pages_per_chunk, const int32_t* commit_count,
+                                int commit_blocks, int32_t* error_word, void* stream);
+
 /* ------------------------------------------------------------------ fp32 attention
  * The merged attention call for fp32 models (the reference's fp32
  * configuration: LastKVAttention.forward's SDPA over fp32 history,

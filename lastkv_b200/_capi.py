@@ -42,6 +42,9 @@ _SIGNATURES = {
     "lkv_merge_partials": (I32, [P, P, I32, I64, I32, I32, I64, I64, P, P, P, P]),
     "lkv_rope_norm_append": (I32, [P, I64, P, I64, P, I64, P, P, I64, I64, P, P, F32, P, P, I64,
                                    P, P, P, I64, P, P, P, I64, I32, I32, I32, I32, I32, P, P]),
+    "lkv_rope_norm_append_commit": (I32, [P, I64, P, I64, P, I64, P, P, I64, I64, P, P, F32, P, P, I64,
+                                          P, P, P, I64, P, P, P, I64, I32, I32, I32, I32, I32,
+                                          P, P, I64, P, P, I64, P, I32, I32, I32, P, I32, P, P]),
     "lkv_gather_blend": (I32, [P, P, I64, P, P, P, P, P, I32, I32, I32, P, P]),
     "lkv_blend_chunk": (I32, [P, P, I64, P, P, I64, P, I32, I32, I32, I32, I32, P, P]),
     "lkv_blend_chunk_f32": (I32, [P, P, I64, P, P, I64, P, I32, I32, I32, I32, I32, P, P]),

@@ -56,15 +56,13 @@ struct AppendParams {
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// One 256-thread block of the append: head group `hg` (8 heads, one per warp) of token `t`.
 template <int D>
-__global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParams p) {
-  pdl_launch_dependents();
-  pdl_wait();  // q/k/v come from the projection GEMM
+__device__ __forceinline__ void append_block(const AppendParams& p, int hg, int t) {
   constexpr int HALF = D / 2;
   constexpr int E = HALF / 32;  // rotary pairs per lane (2 for D=128, 1 for D=64)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x * 8 + warp;
-  const int t = blockIdx.y;
+  const int h = hg * 8 + warp;
   if (h >= p.Hq + p.Hkv) return;
   const bool is_q = h < p.Hq;
   const int j = h - p.Hq;  // kv head
@@ -169,6 +167,13 @@ __global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParam
   }
 }
 
+template <int D>
+__global__ void __launch_bounds__(256) rope_norm_append_kernel(const AppendParams p) {
+  pdl_launch_dependents();
+  pdl_wait();  // q/k/v come from the projection GEMM
+  append_block<D>(p, blockIdx.x, blockIdx.y);
+}
+
 struct BlendParams {
   __nv_bfloat16* pool_k;
   __nv_bfloat16* pool_v;
@@ -177,13 +182,13 @@ struct BlendParams {
   const int32_t* ring_pages;
   int64_t ring_stride;
   const float* alpha;
-  int ppc, Hkv, D;
+  int ppc, S, L, Hkv, D;
+  const int32_t* count;  // append_commit_kernel: device count of rows of raw/ring to commit (NULL = S)
   int* err;
 };
 
-// grid (pages_per_chunk, num_seqs, num_layers); one CTA blends one page of one layer.
-__global__ void __launch_bounds__(256) blend_chunk_kernel(const BlendParams p) {
-  const int jp = blockIdx.x, seq = blockIdx.y, layer = blockIdx.z;
+// One 256-thread block of the commit: page `jp` of sequence `seq`'s finished chunk in layer `layer`'s ring.
+__device__ __forceinline__ void blend_block(const BlendParams& p, int jp, int seq, int layer) {
   const int64_t raw = p.raw_pages[(int64_t)seq * p.ppc + jp];
   const int64_t ring = (int64_t)p.ring_pages[(int64_t)seq * p.ppc + jp] + (int64_t)layer * p.ring_stride;
   if (raw < 0 || raw >= p.num_pages || ring < 0 || ring >= p.num_pages) {
@@ -192,14 +197,21 @@ __global__ void __launch_bounds__(256) blend_chunk_kernel(const BlendParams p) {
   }
   const int64_t page_elems = (int64_t)16 * p.Hkv * p.D;
   const int vecs = (int)(page_elems / 8);
+  // the head of vector vi is (8 vi / D) mod Hkv; D divides the 2048 elements a block
+  // covers per iteration (D is 64 or 128), so the head advances by a constant step
+  const int head0 = (int)((threadIdx.x * 8) / p.D) % p.Hkv;
+  const int hstep = (int)((blockDim.x * 8) / p.D) % p.Hkv;
+  const float* alpha = p.alpha + layer * p.Hkv;
 #pragma unroll 1
   for (int which = 0; which < 2; ++which) {
     __nv_bfloat16* pool = which ? p.pool_v : p.pool_k;
     const uint4* src = reinterpret_cast<const uint4*>(pool + raw * page_elems);
     uint4* dst = reinterpret_cast<uint4*>(pool + ring * page_elems);
+    int head = head0;
     for (int vi = threadIdx.x; vi < vecs; vi += blockDim.x) {
-      const int head = (int)(((int64_t)vi * 8 / p.D) % p.Hkv);
-      const float a = p.alpha[layer * p.Hkv + head];
+      const float a = alpha[head];
+      head += hstep;
+      if (head >= p.Hkv) head -= p.Hkv;
       const float ia = bf16r(__fsub_rn(1.f, a));
       uint4 rv = src[vi], gv = dst[vi];
       uint32_t* r = reinterpret_cast<uint32_t*>(&rv);
@@ -212,6 +224,50 @@ __global__ void __launch_bounds__(256) blend_chunk_kernel(const BlendParams p) {
       }
       dst[vi] = gv;
     }
+  }
+}
+
+// grid (pages_per_chunk, num_seqs, num_layers); one CTA blends one page of one layer.
+__global__ void __launch_bounds__(256) blend_chunk_kernel(const BlendParams p) {
+  blend_block(p, blockIdx.x, blockIdx.y, blockIdx.z);
+}
+
+// The append of the first layer of a step and the commit of the chunks the
+// previous step finished, in one launch (the reference commits lazily at the
+// next step's start too, batching.py:1099-1144).  Blocks [0, n_append) append
+// (head group i % groups, token i / groups); the other gridDim.x - n_append
+// blocks stride over the (page, row, layer) items of the commit, whose row
+// count is read on the device when `count` is set, so one captured launch
+// serves steps with and without a boundary.  Disjoint addresses: the append
+// writes this step's slot of each ring, in the other half of the 2C ring from
+// the finished chunk the blend rewrites, and the blend's raw pages belong to
+// that finished chunk.
+template <int D>
+__global__ void __launch_bounds__(256, 8) append_commit_kernel(const AppendParams pa, const BlendParams pb,
+                                                               int groups, int n_append) {
+  pdl_launch_dependents();
+  pdl_wait();  // q/k/v come from the projection GEMM; the rings and the commit count from earlier work
+  const int i = blockIdx.x;
+  if (i < n_append) {
+    append_block<D>(pa, i % groups, i / groups);
+    return;
+  }
+  int rows = pb.S;
+  if (pb.count) {
+    const int c = *pb.count;
+    if (c < 0 || c > pb.S) {
+      if (i == n_append && threadIdx.x == 0) report_error(pb.err, DEVERR_BAD_SLOT, 3, c);
+      return;
+    }
+    rows = c;
+  }
+  const int64_t per_layer = (int64_t)pb.ppc * rows;
+  const int64_t items = per_layer * pb.L;
+  const int nb = gridDim.x - n_append;
+  for (int64_t j = i - n_append; j < items; j += nb) {
+    const int layer = (int)(j / per_layer);
+    const int64_t r = j - layer * per_layer;
+    blend_block(pb, (int)(r % pb.ppc), (int)(r / pb.ppc), layer);
   }
 }
 
@@ -309,7 +365,8 @@ __global__ void build_block_tables_kernel(const int32_t* bt, int64_t bt_stride, 
   }
 }
 
-int rope_norm_append(const AppendArgs& a) {
+// Host-side checks of an append call; LKV_OK when the bf16 kernel may run.
+static int check_append(const AppendArgs& a) {
   if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
   if (a.num_tokens < 0 || a.num_q_heads < 1 || a.num_kv_heads < 1) return LKV_ERR_INVALID_ARGUMENT;
   if (a.num_tokens == 0) return LKV_OK;
@@ -318,7 +375,10 @@ int rope_norm_append(const AppendArgs& a) {
   if ((a.q_weight == nullptr) != (a.k_weight == nullptr)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.src_slot && (!a.src_k || !a.src_v)) return LKV_ERR_INVALID_ARGUMENT;
   if (a.num_tokens > 65535) return LKV_ERR_UNSUPPORTED;  // grid.y limit; callers split larger spans
-  if (a.flags & LKV_APPEND_FP32) return rope_norm_append_f32(a);  // fp32 tensors and table (fp32.cu)
+  return LKV_OK;
+}
+
+static AppendParams append_params(const AppendArgs& a) {
   AppendParams p{};
   p.q = static_cast<const __nv_bfloat16*>(a.q);
   p.q_row = a.q_row;
@@ -350,6 +410,14 @@ int rope_norm_append(const AppendArgs& a) {
   p.Hq = a.num_q_heads;
   p.Hkv = a.num_kv_heads;
   p.err = a.error_word;
+  return p;
+}
+
+int rope_norm_append(const AppendArgs& a) {
+  const int st = check_append(a);
+  if (st != LKV_OK || a.num_tokens == 0) return st;
+  if (a.flags & LKV_APPEND_FP32) return rope_norm_append_f32(a);  // fp32 tensors and table (fp32.cu)
+  const AppendParams p = append_params(a);
   dim3 grid((a.num_q_heads + a.num_kv_heads + 7) / 8, a.num_tokens);
   cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
   const cudaError_t e = a.head_dim == 128 ? launch_pdl(rope_norm_append_kernel<128>, grid, dim3(256), 0, stream, p)
@@ -357,7 +425,8 @@ int rope_norm_append(const AppendArgs& a) {
   return e == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
 }
 
-int blend_chunk(const BlendArgs& a) {
+// Host-side checks of a commit call; LKV_OK when the kernel may run.
+static int check_blend(const BlendArgs& a) {
   if (a.head_dim != 64 && a.head_dim != 128) return LKV_ERR_UNSUPPORTED;
   if (a.num_layers < 0 || a.num_seqs < 0 || a.pages_per_chunk < 0 || a.num_kv_heads < 1)
     return LKV_ERR_INVALID_ARGUMENT;
@@ -366,6 +435,10 @@ int blend_chunk(const BlendArgs& a) {
   if ((reinterpret_cast<uintptr_t>(a.pool_k) & 15) || (reinterpret_cast<uintptr_t>(a.pool_v) & 15))
     return LKV_ERR_INVALID_ARGUMENT;
   if (a.num_seqs > 65535 || a.num_layers > 65535) return LKV_ERR_UNSUPPORTED;
+  return LKV_OK;
+}
+
+static BlendParams blend_params(const BlendArgs& a) {
   BlendParams p{};
   p.pool_k = static_cast<__nv_bfloat16*>(a.pool_k);
   p.pool_v = static_cast<__nv_bfloat16*>(a.pool_v);
@@ -375,12 +448,64 @@ int blend_chunk(const BlendArgs& a) {
   p.ring_stride = a.ring_layer_stride_pages;
   p.alpha = a.alpha;
   p.ppc = a.pages_per_chunk;
+  p.S = a.num_seqs;
+  p.L = a.num_layers;
   p.Hkv = a.num_kv_heads;
   p.D = a.head_dim;
   p.err = a.error_word;
+  return p;
+}
+
+int blend_chunk(const BlendArgs& a) {
+  const int st = check_blend(a);
+  if (st != LKV_OK || a.num_layers == 0 || a.num_seqs == 0 || a.pages_per_chunk == 0) return st;
+  const BlendParams p = blend_params(a);
   dim3 grid(a.pages_per_chunk, a.num_seqs, a.num_layers);
   blend_chunk_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(a.stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
+}
+
+int rope_norm_append_commit(const AppendArgs& a, const BlendArgs& b, const int32_t* commit_count,
+                            int commit_blocks) {
+  int st = check_append(a);
+  if (st != LKV_OK) return st;
+  st = check_blend(b);
+  if (st != LKV_OK) return st;
+  if (a.flags & LKV_APPEND_FP32) return LKV_ERR_UNSUPPORTED;  // fp32 pools: append, then lkv_blend_chunk_f32
+  if (a.head_dim != b.head_dim || a.num_kv_heads != b.num_kv_heads || commit_blocks < 0)
+    return LKV_ERR_INVALID_ARGUMENT;
+  const int groups = (a.num_q_heads + a.num_kv_heads + 7) / 8;
+  const int64_t n_append = (int64_t)groups * a.num_tokens;
+  const int64_t items = (int64_t)b.pages_per_chunk * b.num_seqs * b.num_layers;
+  // commit blocks: by default one per page item when the host knows the rows (as
+  // blend_chunk_kernel), else one full wave (8 resident 256-thread blocks per SM at
+  // <= 32 registers) striding over the items; an explicit count is capped at the items
+  int64_t nb = 0;
+  if (items > 0) {
+    if (commit_blocks > 0) {
+      nb = commit_count ? commit_blocks : std::min<int64_t>(items, commit_blocks);
+    } else if (!commit_count) {
+      nb = items;
+    } else {
+      int dev = 0, sms = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return LKV_ERR_CUDA;
+      nb = 8 * sms;
+    }
+  }
+  if (n_append + nb > 0x7fffffffLL) return LKV_ERR_UNSUPPORTED;
+  if (n_append + nb == 0) return LKV_OK;
+  const AppendParams pa = append_params(a);
+  BlendParams pb = blend_params(b);
+  pb.count = commit_count;
+  cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
+  const dim3 grid((unsigned)(n_append + nb));
+  const cudaError_t e =
+      a.head_dim == 128
+          ? launch_pdl(append_commit_kernel<128>, grid, dim3(256), 0, stream, pa, pb, groups, (int)n_append)
+          : launch_pdl(append_commit_kernel<64>, grid, dim3(256), 0, stream, pa, pb, groups, (int)n_append);
+  return e == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
 }
 
 int build_layer_block_tables(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc, const int32_t* ring_base,

@@ -120,7 +120,7 @@ const char* lkv_status_string(int status) {
   }
 }
 
-int lkv_abi_version(void) { return 200; }
+int lkv_abi_version(void) { return 201; }
 
 int lkv_check_device(int device) {
   int major = 0, minor = 0;
@@ -245,13 +245,19 @@ int lkv_merge_partials(const float* o_parts, const float* lse_parts, int num_par
                              lse_part_stride, out_scale, out, lse_out, static_cast<cudaStream_t>(stream));
 }
 
-int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_row, const void* v, int64_t v_row,
-                         const int64_t* positions, const void* cos_sin, int64_t cos_sin_row, int64_t max_position,
-                         const void* q_weight, const void* k_weight, float eps, const float* inv_scale, void* q_out,
-                         int64_t q_out_row, const int64_t* ring_slot, void* ring_k, void* ring_v, int64_t ring_slots,
-                         const int64_t* src_slot, void* src_k, void* src_v, int64_t src_slots, int num_tokens,
-                         int num_q_heads, int num_kv_heads, int head_dim, int flags, int32_t* error_word,
-                         void* stream) {
+#define LKV_APPEND_PARAMS                                                                                     \
+  const void *q, int64_t q_row, const void *k, int64_t k_row, const void *v, int64_t v_row,                    \
+      const int64_t *positions, const void *cos_sin, int64_t cos_sin_row, int64_t max_position,                \
+      const void *q_weight, const void *k_weight, float eps, const float *inv_scale, void *q_out,              \
+      int64_t q_out_row, const int64_t *ring_slot, void *ring_k, void *ring_v, int64_t ring_slots,             \
+      const int64_t *src_slot, void *src_k, void *src_v, int64_t src_slots, int num_tokens, int num_q_heads,   \
+      int num_kv_heads, int head_dim, int flags
+#define LKV_APPEND_ARGS                                                                                         \
+  q, q_row, k, k_row, v, v_row, positions, cos_sin, cos_sin_row, max_position, q_weight, k_weight, eps,        \
+      inv_scale, q_out, q_out_row, ring_slot, ring_k, ring_v, ring_slots, src_slot, src_k, src_v, src_slots,   \
+      num_tokens, num_q_heads, num_kv_heads, head_dim, flags
+
+static lkv::AppendArgs append_args(LKV_APPEND_PARAMS, int32_t* error_word, void* stream) {
   lkv::AppendArgs a{};
   a.q = q;
   a.q_row = q_row;
@@ -284,7 +290,44 @@ int lkv_rope_norm_append(const void* q, int64_t q_row, const void* k, int64_t k_
   a.flags = flags;
   a.error_word = error_word;
   a.stream = stream;
-  return lkv::rope_norm_append(a);
+  return a;
+}
+
+static lkv::BlendArgs blend_args(void* pool_k, void* pool_v, int64_t num_pages, const int32_t* raw_pages,
+                                 const int32_t* ring_pages, int64_t ring_layer_stride_pages, const float* alpha,
+                                 int num_layers, int num_seqs, int pages_per_chunk, int num_kv_heads, int head_dim,
+                                 int32_t* error_word, void* stream) {
+  lkv::BlendArgs a{};
+  a.pool_k = pool_k;
+  a.pool_v = pool_v;
+  a.num_pages = num_pages;
+  a.raw_pages = raw_pages;
+  a.ring_pages = ring_pages;
+  a.ring_layer_stride_pages = ring_layer_stride_pages;
+  a.alpha = alpha;
+  a.num_layers = num_layers;
+  a.num_seqs = num_seqs;
+  a.pages_per_chunk = pages_per_chunk;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.error_word = error_word;
+  a.stream = stream;
+  return a;
+}
+
+int lkv_rope_norm_append(LKV_APPEND_PARAMS, int32_t* error_word, void* stream) {
+  return lkv::rope_norm_append(append_args(LKV_APPEND_ARGS, error_word, stream));
+}
+
+int lkv_rope_norm_append_commit(LKV_APPEND_PARAMS, void* pool_k, void* pool_v, int64_t num_pages,
+                                const int32_t* raw_pages, const int32_t* ring_pages, int64_t ring_layer_stride_pages,
+                                const float* alpha, int num_layers, int num_commit_rows, int pages_per_chunk,
+                                const int32_t* commit_count, int commit_blocks, int32_t* error_word, void* stream) {
+  return lkv::rope_norm_append_commit(
+      append_args(LKV_APPEND_ARGS, error_word, stream),
+      blend_args(pool_k, pool_v, num_pages, raw_pages, ring_pages, ring_layer_stride_pages, alpha, num_layers,
+                 num_commit_rows, pages_per_chunk, num_kv_heads, head_dim, error_word, stream),
+      commit_count, commit_blocks);
 }
 
 int lkv_gather_blend(void* pool_k, void* pool_v, int64_t num_slots, const int64_t* dst_slot,
@@ -299,44 +342,18 @@ int lkv_blend_chunk(void* pool_k, void* pool_v, int64_t num_pages, const int32_t
                     const int32_t* ring_pages, int64_t ring_layer_stride_pages, const float* alpha, int num_layers,
                     int num_seqs, int pages_per_chunk, int num_kv_heads, int head_dim, int32_t* error_word,
                     void* stream) {
-  lkv::BlendArgs a{};
-  a.pool_k = pool_k;
-  a.pool_v = pool_v;
-  a.num_pages = num_pages;
-  a.raw_pages = raw_pages;
-  a.ring_pages = ring_pages;
-  a.ring_layer_stride_pages = ring_layer_stride_pages;
-  a.alpha = alpha;
-  a.num_layers = num_layers;
-  a.num_seqs = num_seqs;
-  a.pages_per_chunk = pages_per_chunk;
-  a.num_kv_heads = num_kv_heads;
-  a.head_dim = head_dim;
-  a.error_word = error_word;
-  a.stream = stream;
-  return lkv::blend_chunk(a);
+  return lkv::blend_chunk(blend_args(pool_k, pool_v, num_pages, raw_pages, ring_pages, ring_layer_stride_pages, alpha,
+                                     num_layers, num_seqs, pages_per_chunk, num_kv_heads, head_dim, error_word,
+                                     stream));
 }
 
 int lkv_blend_chunk_f32(void* pool_k, void* pool_v, int64_t num_pages, const int32_t* raw_pages,
                         const int32_t* ring_pages, int64_t ring_layer_stride_pages, const float* alpha,
                         int num_layers, int num_seqs, int pages_per_chunk, int num_kv_heads, int head_dim,
                         int32_t* error_word, void* stream) {
-  lkv::BlendArgs a{};
-  a.pool_k = pool_k;
-  a.pool_v = pool_v;
-  a.num_pages = num_pages;
-  a.raw_pages = raw_pages;
-  a.ring_pages = ring_pages;
-  a.ring_layer_stride_pages = ring_layer_stride_pages;
-  a.alpha = alpha;
-  a.num_layers = num_layers;
-  a.num_seqs = num_seqs;
-  a.pages_per_chunk = pages_per_chunk;
-  a.num_kv_heads = num_kv_heads;
-  a.head_dim = head_dim;
-  a.error_word = error_word;
-  a.stream = stream;
-  return lkv::blend_chunk_f32(a);
+  return lkv::blend_chunk_f32(blend_args(pool_k, pool_v, num_pages, raw_pages, ring_pages, ring_layer_stride_pages,
+                                         alpha, num_layers, num_seqs, pages_per_chunk, num_kv_heads, head_dim,
+                                         error_word, stream));
 }
 
 int lkv_attention_paged_f32(const void* q, int64_t q_stride_tok, const void* pool_k, const void* pool_v,

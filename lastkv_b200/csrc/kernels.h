@@ -156,6 +156,8 @@ struct BlendArgs {
   void* stream;
 };
 int blend_chunk(const BlendArgs& a);
+// the append and the previous step's boundary commit in one launch (commit_count: device row count or NULL)
+int rope_norm_append_commit(const AppendArgs& a, const BlendArgs& b, const int32_t* commit_count, int commit_blocks);
 int blend_chunk_f32(const BlendArgs& a);  // fp32 pools (fp32.cu)
 
 int build_layer_block_tables(const int32_t* bt, int64_t bt_stride, const int32_t* nsrc, const int32_t* ring_base,

@@ -260,6 +260,10 @@ class PagedLastKVCache:
                                                   self.pages_per_seq + self.ring_pages, device=device) \
             if dtype == torch.bfloat16 else None
         self._meta = None
+        # bf16: a boundary commit waits for the next span's first-layer append and runs inside
+        # that launch (lkv_rope_norm_append_commit); False: one blend launch at the boundary
+        self.fuse_commit = dtype == torch.bfloat16
+        self._pending = None
 
     # -- capacity
     def reserve(self, max_tokens: int) -> None:
@@ -270,6 +274,7 @@ class PagedLastKVCache:
         for use inside a CUDA-graph capture."""
         if max_tokens <= self.max_tokens:
             return
+        self.flush_commit()
         B, L, P = self.batch, self.num_layers, PAGE_SIZE
         pps = -(-max_tokens // P)
         src_pages = B * pps
@@ -305,6 +310,7 @@ class PagedLastKVCache:
 
     def reorder_cache(self, beam_idx):
         """Reorder sequences (beam search): gather shared pages and rings by beam index."""
+        self.flush_commit()
         idx = beam_idx.to("cpu").long().numpy()
         src_old = self.src_table[idx].reshape(-1)
         src_new = self.src_table.reshape(-1)
@@ -373,7 +379,11 @@ class PagedLastKVCache:
         self._meta = None
 
     def commit(self, alpha: torch.Tensor):
-        """Blend the chunk that just completed into every layer ring (modeling.py:203-207)."""
+        """Blend the chunk that just completed into every layer ring (modeling.py:203-207).
+
+        With ``fuse_commit`` the blend is queued and runs inside the next span's
+        first-layer append (the next attention to read a ring comes after it);
+        ``flush_commit`` runs a queued blend on its own."""
         C, P = self.chunk_size, PAGE_SIZE
         end = self.seen_tokens
         if end % C or end == self.committed:
@@ -385,10 +395,27 @@ class PagedLastKVCache:
         ring_first = ((end - C) % self.ring_tokens) // P
         ring = (self.ring_base[0] + np.arange(self.batch)[:, None] * self.ring_pages
                 + ring_first + np.arange(C // P)[None, :])
-        ops.blend_chunk(self.pool_k, self.pool_v, torch.from_numpy(raw.astype(np.int32)).to(self.device),
-                        torch.from_numpy(ring.astype(np.int32)).to(self.device), self.ring_stride, alpha,
-                        error_word=self.error_word)
+        raw_d = torch.from_numpy(np.ascontiguousarray(raw, dtype=np.int32)).to(self.device)
+        ring_d = torch.from_numpy(np.ascontiguousarray(ring, dtype=np.int32)).to(self.device)
+        self.flush_commit()
+        if self.fuse_commit:
+            self._pending = ops.Commit(self.pool_k, self.pool_v, raw_d, ring_d, self.ring_stride, alpha)
+        else:
+            ops.blend_chunk(self.pool_k, self.pool_v, raw_d, ring_d, self.ring_stride, alpha,
+                            error_word=self.error_word)
         self.committed = end
+
+    def take_commit(self):
+        """The queued boundary commit (an ``ops.Commit``) for the caller's append, or None."""
+        c, self._pending = self._pending, None
+        return c
+
+    def flush_commit(self) -> None:
+        """Run a queued boundary commit now (before the pools are read or moved outside a span)."""
+        c = self.take_commit()
+        if c is not None:
+            ops.blend_chunk(c.pool_k, c.pool_v, c.raw_pages, c.ring_pages, c.ring_layer_stride, c.alpha,
+                            error_word=self.error_word)
 
     def check_errors(self):
         e = self.error_word.cpu().tolist()
@@ -505,7 +532,7 @@ class LastKVAttention(nn.Module):
             q, k, v, meta["local_pos"], cs, q_w, k_w,
             self.config.rms_norm_eps, inv, ring_slot, flat_k, flat_v,
             meta["src_slot"] if top else None, flat_k if top else None, flat_v if top else None,
-            error_word=cache.error_word)
+            error_word=cache.error_word, commit=cache.take_commit() if self.layer_idx == 0 else None)
         bt = meta["bt_all"][self.layer_idx]
         if kv_dtype == torch.float32:  # decode and spans alike (lkv_attention_paged_f32)
             out = ops.attention_paged_f32(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], meta["cu_q"],

@@ -11,6 +11,7 @@ from __future__ import annotations
 import ctypes
 import functools
 import os
+from typing import NamedTuple, Optional
 
 import torch
 
@@ -308,15 +309,49 @@ def attention_paged_f32(q, pool_k, pool_v, block_table, seq_k, cu_q, *, causal=T
     return out
 
 
+class Commit(NamedTuple):
+    """A chunk-boundary commit (the ``blend_chunk`` arguments) to run inside the next
+    append launch (``rope_norm_append(..., commit=)``, lkv_rope_norm_append_commit).
+
+    ``count`` (device int32 [1], optional) holds how many rows of raw/ring_pages to
+    commit, read on the device, so a captured launch can carry a commit or none;
+    ``blocks`` is the launch's block count for the commit (0: one per page item
+    without ``count``, one wave of 8 per SM with it)."""
+
+    pool_k: torch.Tensor
+    pool_v: torch.Tensor
+    raw_pages: torch.Tensor
+    ring_pages: torch.Tensor
+    ring_layer_stride: int
+    alpha: torch.Tensor
+    count: Optional[torch.Tensor] = None
+    blocks: int = 0
+
+
+def _check_commit(c: Commit):
+    _check_pool(c.pool_k, c.pool_v)
+    _require(c.raw_pages.dim() == 2 and c.ring_pages.shape == c.raw_pages.shape, "ring_pages must match raw_pages")
+    _require(c.raw_pages.dtype == torch.int32 and c.ring_pages.dtype == torch.int32, "page lists must be int32")
+    _require(c.raw_pages.is_contiguous() and c.ring_pages.is_contiguous(), "page lists must be contiguous")
+    _require(c.alpha.dtype == torch.float32 and c.alpha.is_contiguous() and c.alpha.dim() == 2,
+             "alpha must be fp32 [L, Hkv]")
+    if c.count is not None:
+        _require(c.count.dtype == torch.int32 and c.count.numel() >= 1, "commit count must be device int32 [1]")
+    _require(c.blocks >= 0, "commit blocks must be >= 0")
+
+
 @_traced
 def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_scale, ring_slot, ring_k, ring_v,
-                     src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None, interleaved=False):
+                     src_slot=None, src_k=None, src_v=None, q_out=None, error_word=None, interleaved=False,
+                     commit: Optional[Commit] = None):
     """Fused RoPE -> Q/K RMSNorm -> V/s -> paged append for one layer.
 
     q [T, Hq*D], k/v [T, Hkv*D] bf16 (row-strided views allowed); positions
     int64 [T]; cos_sin bf16 or fp32 [max_pos, D] (cos | sin halves) or None;
     ``interleaved`` rotates pairs (2i, 2i+1) instead of (i, i + D/2); ring_* /
     src_* flat token views [slots, Hkv, D] of the pools.  Returns q_out [T, Hq, D].
+    ``commit`` (bf16 only) runs the previous boundary's chunk blend in the same
+    launch; pass it to the first layer of the step after the boundary.
     """
     T = q.shape[0]
     D = ring_k.shape[-1]
@@ -345,15 +380,28 @@ def rope_norm_append(q, k, v, positions, cos_sin, q_weight, k_weight, eps, inv_s
         q_out = torch.empty((T, Hq, D), dtype=dt, device=q.device)
     _require(q_out.dtype == dt, "q_out dtype")
     top = src_slot is not None
-    st = _capi.lib().lkv_rope_norm_append(
-        q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), _ptr(positions),
-        _ptr(cos_sin), cos_sin.stride(0) if cos_sin is not None else 0,
-        cos_sin.shape[0] if cos_sin is not None else 0, _ptr(q_weight), _ptr(k_weight),
-        float(eps), _ptr(inv_scale), q_out.data_ptr(), q_out.stride(0), ring_slot.data_ptr(),
-        ring_k.data_ptr(), ring_v.data_ptr(), ring_k.shape[0],
-        _ptr(src_slot), _ptr(src_k) if top else None, _ptr(src_v) if top else None,
-        src_k.shape[0] if top else 0, T, Hq, Hkv, D, flags, _ptr(error_word), _stream())
-    _capi.check(st, "lkv_rope_norm_append")
+    args = (q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), _ptr(positions),
+            _ptr(cos_sin), cos_sin.stride(0) if cos_sin is not None else 0,
+            cos_sin.shape[0] if cos_sin is not None else 0, _ptr(q_weight), _ptr(k_weight),
+            float(eps), _ptr(inv_scale), q_out.data_ptr(), q_out.stride(0), ring_slot.data_ptr(),
+            ring_k.data_ptr(), ring_v.data_ptr(), ring_k.shape[0],
+            _ptr(src_slot), _ptr(src_k) if top else None, _ptr(src_v) if top else None,
+            src_k.shape[0] if top else 0, T, Hq, Hkv, D, flags)
+    if commit is None:
+        st = _capi.lib().lkv_rope_norm_append(*args, _ptr(error_word), _stream())
+        _capi.check(st, "lkv_rope_norm_append")
+        return q_out
+    _require(dt == torch.bfloat16, "the fused commit takes bf16 pools (fp32: append, then blend_chunk)")
+    _check_commit(commit)
+    S, ppc = commit.raw_pages.shape
+    L, hkv = commit.alpha.shape
+    _require(hkv == Hkv and commit.pool_k.shape[2] == Hkv and commit.pool_k.shape[3] == D,
+             "commit pools must match the append's heads")
+    st = _capi.lib().lkv_rope_norm_append_commit(
+        *args, commit.pool_k.data_ptr(), commit.pool_v.data_ptr(), commit.pool_k.shape[0],
+        commit.raw_pages.data_ptr(), commit.ring_pages.data_ptr(), int(commit.ring_layer_stride),
+        commit.alpha.data_ptr(), L, S, ppc, _ptr(commit.count), int(commit.blocks), _ptr(error_word), _stream())
+    _capi.check(st, "lkv_rope_norm_append_commit")
     return q_out
 
 

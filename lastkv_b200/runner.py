@@ -7,8 +7,10 @@ CUDA graph over static buffers.  Before each replay the host prologue
 ``prepare_real``, vllm/src/lastkv/vllm/backends/rmarin_flashinfer/fastpath.py:456-582)
 fills pinned staging buffers that are copied to the static device buffers on
 the same stream; the argmax of a step feeds the next step on the device.  The
-chunk-boundary commit (one blend launch) runs between replays.  All sequences
-of the batch advance together (equal positions), as in ``generate``.
+chunk-boundary commit runs inside the first layer's append of the next step:
+a second graph, captured with that fused launch over static page lists,
+replays for the step after each boundary.  All sequences of the batch advance
+together (equal positions), as in ``generate``.
 """
 
 from __future__ import annotations
@@ -16,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import ops
-from .contract import RMarinBackendContractError
+from .contract import PAGE_SIZE, RMarinBackendContractError
 from .hf import LastKVForCausalLM, PagedLastKVCache
 
 
@@ -48,7 +50,11 @@ class GraphDecodeRunner:
                     "done": None} for _ in range(self.NSETS)]
         self._set = 0
         self.graph = None
+        self.graph_commit = None  # the step after a chunk boundary (bf16 caches)
         self.alpha = model.model.blend_alpha(cache.dtype)
+        ppc = cache.chunk_size // PAGE_SIZE
+        self.c_raw = torch.zeros((B, ppc), dtype=torch.int32, device=dev)
+        self.c_ring = torch.zeros((B, ppc), dtype=torch.int32, device=dev)
 
     def _prepare(self):
         """Host plan of the next token -> static device buffers (stream-ordered copies)."""
@@ -77,17 +83,19 @@ class GraphDecodeRunner:
         ops.build_layer_block_tables(self.bt, self.nsrc, cache.ring_base_dev, out=self.bt_all)
         self._fresh_meta()
 
-    def _fresh_meta(self):
+    def _fresh_meta(self, tables_ready=True):
         """The span metadata over the static buffers, without the per-span values the
         layers memoise (so a capture records the kernels that compute them).
 
         ``tables_ready``: the block tables and sequence lengths are written before the
         graph starts (copies + the table kernel in ``_prepare``), and a graph's first
         kernel waits for all earlier stream work, so every decode in the step may start
-        its page loads before its PDL wait (LKV_DECODE_TABLES_READY)."""
+        its page loads before its PDL wait (LKV_DECODE_TABLES_READY).  Not in the step
+        after a boundary: its first append launch rewrites the finished chunk's ring
+        pages of every layer, so those decodes load pages after their wait."""
         self.cache._meta = {"n": 1, "W": self.W, "bt_all": self.bt_all, "seq_k": self.seq_k, "cu_q": self.cu_q,
                             "local_pos": self.local_pos, "ring_tok": self.ring_tok, "src_slot": self.src_slot,
-                            "tables_ready": True}
+                            "tables_ready": tables_ready}
 
     def _body(self):
         m = self.model.model
@@ -100,15 +108,23 @@ class GraphDecodeRunner:
             self.ids.copy_(logits.float().argmax(-1, keepdim=True))
 
     def capture(self):
-        """Capture one decode step at the current position (the warm-up runs do not advance)."""
+        """Capture one decode step at the current position (the warm-up runs do not advance),
+        and for bf16 caches the same step with a boundary commit fused into layer 0's append."""
+        cache = self.cache
+        cache.flush_commit()
         saved = self.ids.clone()
         self._prepare()
+        fused = cache.fuse_commit
+        empty = torch.zeros((0, self.c_raw.shape[1]), dtype=torch.int32, device=self.ids.device)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            for _ in range(2):
+            for i in range(3 if fused else 2):
                 self.ids.copy_(saved)
                 self._fresh_meta()
+                if i == 2:  # loads the fused append kernel before its capture; commits nothing
+                    cache._pending = ops.Commit(cache.pool_k, cache.pool_v, empty, empty, cache.ring_stride,
+                                                self.alpha)
                 self._body()
         torch.cuda.current_stream().wait_stream(s)
         self.ids.copy_(saved)
@@ -117,6 +133,17 @@ class GraphDecodeRunner:
         with torch.cuda.graph(g):
             self._body()
         self.graph = g
+        if fused:
+            self._fresh_meta(tables_ready=False)
+            cache._pending = ops.Commit(cache.pool_k, cache.pool_v, self.c_raw, self.c_ring, cache.ring_stride,
+                                        self.alpha)
+            gc = torch.cuda.CUDAGraph()
+            try:
+                with torch.cuda.graph(gc, pool=g.pool()):
+                    self._body()
+            finally:
+                cache._pending = None
+            self.graph_commit = gc
         self.ids.copy_(saved)
 
     def step(self):
@@ -124,8 +151,20 @@ class GraphDecodeRunner:
         if self.graph is None:
             raise RMarinBackendContractError("capture() must run before step()")
         cache = self.cache
+        pending = cache.take_commit()
+        if pending is not None and (self.graph_commit is None or pending.pool_k is not cache.pool_k
+                                    or pending.alpha is not self.alpha
+                                    or pending.raw_pages.shape != self.c_raw.shape):
+            cache._pending = pending  # not the captured form: run it on its own
+            cache.flush_commit()
+            pending = None
         self._prepare()
-        self.graph.replay()
+        if pending is not None:
+            self.c_raw.copy_(pending.raw_pages)
+            self.c_ring.copy_(pending.ring_pages)
+            self.graph_commit.replay()
+        else:
+            self.graph.replay()
         cache.seen_tokens += 1
         cache._meta = None
         if cache.seen_tokens % cache.chunk_size == 0:

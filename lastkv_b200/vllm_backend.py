@@ -178,6 +178,17 @@ class SharedKVFastPath:
         self.bt_all = self._bt_all_flat.view(pool.num_layers, mb, self.W)
         self.q_out = torch.empty((mt, num_q_heads, pool.d), dtype=torch.bfloat16, device=dev)
         self.error_word = torch.zeros(4, dtype=torch.int32, device=dev)
+        # boundary commits of a step: page lists + a device row count read by layer 0's fused
+        # append (lkv_rope_norm_append_commit), so captured decode graphs carry them too.
+        # fuse_commit False: one blend launch in prepare instead.
+        ppc = pool.chunk_size // PAGE_SIZE
+        self.c_raw = torch.zeros((mb, ppc), dtype=torch.int32, device=dev)
+        self.c_ring = torch.zeros((mb, ppc), dtype=torch.int32, device=dev)
+        self.c_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.fuse_commit = True
+        # commit blocks in the fused launch: 0 = one wave of 8 per SM striding over the page
+        # items (a step without a boundary pays well under a microsecond for them)
+        self.commit_blocks = 0
         self.workspace = ops.Workspace.for_decode(mb, num_q_heads, pool.d, self.W, device=dev)
         pin = torch.cuda.is_available() and dev.type == "cuda"
         def host(shape, dtype):
@@ -185,7 +196,9 @@ class SharedKVFastPath:
             return t.pin_memory() if pin else t
         self._h = [{"ring": host(mt, torch.int64), "src": host(mt, torch.int64), "pos": host(mt, torch.int64),
                     "cu": host(mb + 1, torch.int32), "seqk": host(mb, torch.int32), "nsrc": host(mb, torch.int32),
-                    "bt": host((mb, self.W), torch.int32)} for _ in range(self.NSETS)]
+                    "bt": host((mb, self.W), torch.int32), "craw": host((mb, ppc), torch.int32),
+                    "cring": host((mb, ppc), torch.int32), "ccount": host(1, torch.int32)}
+                   for _ in range(self.NSETS)]
         # per set: an event recorded after the last copies that read it (None = never used)
         self._h_done = [None] * self.NSETS
         self._set = 0
@@ -284,7 +297,8 @@ class SharedKVFastPath:
         if self.pool.alpha is None or self.layers is None:
             raise RMarinBackendContractError("bind_parameters and register_layers must run before prepare")
         plan = self.plan_rows(spans, num_reqs_padded)
-        self._commit(plan["commits"])
+        if not self.fuse_commit:
+            self._commit(plan["commits"])
         self._set = (self._set + 1) % self.NSETS
         h = self._h[self._set]
         if self._h_done[self._set] is not None:
@@ -305,6 +319,12 @@ class SharedKVFastPath:
         self.seq_k[:B].copy_(h["seqk"][:B], non_blocking=True)
         self.nsrc[:B].copy_(h["nsrc"][:B], non_blocking=True)
         self.bt[:B].copy_(h["bt"][:B], non_blocking=True)
+        if self.fuse_commit:
+            k = self._stage_commits(plan["commits"], h)
+            if k:
+                self.c_raw[:k].copy_(h["craw"][:k], non_blocking=True)
+                self.c_ring[:k].copy_(h["cring"][:k], non_blocking=True)
+            self.c_count.copy_(h["ccount"], non_blocking=True)
         done = torch.cuda.Event()
         done.record()
         self._h_done[self._set] = done
@@ -315,20 +335,39 @@ class SharedKVFastPath:
         self.active = True
         return True
 
-    def _commit(self, commits) -> None:
-        """Blend finished chunks into every layer ring in one launch (batching.py:1099-1144)."""
-        if not commits:
-            return
+    def _commit_pages(self, commits):
+        """Shared pages and layer-0 ring pages [commits, C/16] of each finished chunk."""
         pool = self.pool
         C, P = pool.chunk_size, PAGE_SIZE
         raw = np.stack([pool.src_table[s, (end - C) // P:end // P] for s, end in commits]).astype(np.int32)
         ring = np.stack([pool.ring_base(0) + s * pool.ring_pages + ((end - C) % pool.ring_tokens) // P
                          + np.arange(C // P) for s, end in commits]).astype(np.int32)
+        return raw, ring
+
+    def _commit(self, commits) -> None:
+        """Blend finished chunks into every layer ring in one launch (batching.py:1099-1144)."""
+        if not commits:
+            return
+        pool = self.pool
+        raw, ring = self._commit_pages(commits)
         ops.blend_chunk(pool.pool_k, pool.pool_v, torch.from_numpy(raw).to(pool.device),
                         torch.from_numpy(ring).to(pool.device), pool.ring_stride, pool.alpha,
                         error_word=self.error_word)
         for s, end in commits:
             pool.committed[s] = end
+
+    def _stage_commits(self, commits, h) -> int:
+        """The step's commits into staging set ``h`` for layer 0's fused append; returns their count.
+        The commits count as done here: every later step's attention runs after that append."""
+        k = len(commits)
+        if k:
+            raw, ring = self._commit_pages(commits)
+            h["craw"][:k] = torch.from_numpy(raw)
+            h["cring"][:k] = torch.from_numpy(ring)
+            for s, end in commits:
+                self.pool.committed[s] = end
+        h["ccount"][0] = k
+        return k
 
     # ------------------------------------------------------------------ per-layer ops
     def run_layer(self, layer_index: int, query, key, value, output):
@@ -341,7 +380,10 @@ class SharedKVFastPath:
             self.cos_sin, qw, kw, self.eps, pool.inv_scale[layer_index], self.ring_idx[:T],
             pool.layer_ring_view(pool.pool_k, layer_index), pool.layer_ring_view(pool.pool_v, layer_index),
             self.src_idx[:T] if top else None, pool.src_view(pool.pool_k) if top else None,
-            pool.src_view(pool.pool_v) if top else None, q_out=self.q_out[:T], error_word=self.error_word)
+            pool.src_view(pool.pool_v) if top else None, q_out=self.q_out[:T], error_word=self.error_word,
+            commit=ops.Commit(pool.pool_k, pool.pool_v, self.c_raw, self.c_ring, pool.ring_stride, pool.alpha,
+                              count=self.c_count, blocks=self.commit_blocks)
+            if layer_index == 0 and self.fuse_commit else None)
         out = output[:T]
         if self.uniform:
             ops.decode_paged(q, pool.pool_k, pool.pool_v, self.bt_all[layer_index, :B], self.seq_k[:B],

@@ -93,7 +93,8 @@ def test_append_rejects_out_of_range_slot_without_fault():
     assert _ulp_diff(rk.float().cpu().numpy(), nrk).max() <= 1
 
 
-@pytest.mark.parametrize("L,S,ppc,Hkv,D", [(3, 2, 4, 8, 128), (32, 1, 64, 8, 128), (2, 3, 1, 12, 64)])
+@pytest.mark.parametrize("L,S,ppc,Hkv,D", [(3, 2, 4, 8, 128), (32, 1, 64, 8, 128), (2, 3, 1, 12, 64),
+                                           (2, 2, 2, 5, 128), (3, 1, 3, 3, 64)])
 def test_blend_chunk_bit_exact(L, S, ppc, Hkv, D):
     from lastkv_b200 import ops
 
