@@ -876,10 +876,10 @@ def measure_cp(steps: int, warmup: int, world: int, rank: int, device, combine: 
         for l in range(L):
             if cp is None:
                 ops.decode_paged(q[l], pool_k, pool_v, bt, seq_k, out=out[l], out_scale=scale[l], workspace=ws,
-                                 max_pages=pages_mine, tables_ready=True)  # static tables, written at set-up
+                                 max_pages=pages_mine, tables_ready=True, l2_keep=True)  # tables written at set-up
             else:
                 cp.layer(q[l], pool_k, pool_v, bt, seq_k, out_scale=scale[l], out=out[l], workspace=ws,
-                         max_pages=pages_mine, tables_ready=True)
+                         max_pages=pages_mine, tables_ready=True, l2_keep=True)
 
     def barrier():
         if world > 1:

@@ -149,9 +149,9 @@ class ContextParallelDecode:
         return self._bufs[key]
 
     def layer(self, q, pool_k, pool_v, block_table, seq_k, *, out_scale=None, out=None, workspace=None,
-              max_pages=None, tables_ready=False):
+              max_pages=None, tables_ready=False, l2_keep=False):
         """One layer: local partial over this rank's keys, all-gather, exact merge.
-        ``tables_ready`` as for ``ops.decode_paged`` (the tables predate the PDL chain)."""
+        ``tables_ready`` and ``l2_keep`` as for ``ops.decode_paged``."""
         if self.injected:
             return self._layer_generic(q, pool_k, pool_v, block_table, seq_k, out_scale, out, workspace, max_pages)
         B, Hq, D = q.shape
@@ -160,7 +160,8 @@ class ContextParallelDecode:
             st = self._p2p_state(B, Hq, D, q.device, pool_k.shape[2])
             return ops.decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, st["recv_ptrs"], self.rank, self.world,
                                        st["cp_state"], out=out, out_scale=out_scale, workspace=workspace,
-                                       max_pages=max_pages, error_word=st["error"], tables_ready=tables_ready)
+                                       max_pages=max_pages, error_word=st["error"], tables_ready=tables_ready,
+                                       l2_keep=l2_keep)
         n = -(-(B * Hq * (D + 1)) // 4) * 4  # o | lse | pad to a multiple of 4 floats (float4 reads)
         send, recv = self._buffers(("packed", n, str(q.device)), lambda: (
             torch.empty(n, dtype=torch.float32, device=q.device),
@@ -168,7 +169,7 @@ class ContextParallelDecode:
         o_view = send[: B * Hq * D].view(B, Hq, D)
         l_view = send[B * Hq * D: B * Hq * (D + 1)].view(B, Hq)
         ops.decode_paged(q, pool_k, pool_v, block_table, seq_k, workspace=workspace, max_pages=max_pages,
-                         partial=True, partial_out=(o_view, l_view), tables_ready=tables_ready)
+                         partial=True, partial_out=(o_view, l_view), tables_ready=tables_ready, l2_keep=l2_keep)
         if self.world == 1:
             parts = send.view(1, n)
         else:

@@ -58,6 +58,7 @@ struct DecodeParams {
   float scale_log2;  // softmax_scale * log2(e)
   int final_out;     // 1: this kernel writes `out` (S == 1 and not partial mode)
   int early;         // 1: seq_k, the block table and older pages predate the PDL chain (LKV_DECODE_TABLES_READY)
+  int keep_pages;    // block-table columns [0, keep_pages) load with L2 evict_last (LKV_DECODE_L2_KEEP), else evict_first
   // Context parallel: the last CTA to finish a (sequence, KV head) unit merges its
   // split partials and pushes the merged rows to every rank's receive buffer.
   uint64_t* cp_recv[kCpMaxRanks];
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__((NW + 1) * 32)
     if (lane == 0) {
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      const uint64_t policy = policy_evict_first();
+      const uint64_t pol_first = policy_evict_first(), pol_last = policy_evict_last();
       // Before waiting for the previous kernel: the first item's first stages
       // (fresh slots, so no empty-slot wait), as long as a stage holds neither
       // the sequence's last page - where the previous kernel may just have
@@ -282,10 +283,11 @@ __global__ void __launch_bounds__((NW + 1) * 32)
             if (k >= cnt) break;
 #pragma unroll
             for (int h = 0; h < Cfg::HALVES; ++h) {
+              const uint64_t pol = first + k < p.keep_pages ? pol_last : pol_first;
               tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + h * Cfg::TILE_BYTES, &tmk, &full[pre], h * 64, w.hk, 0,
-                               cur[k], policy);
+                               cur[k], pol);
               tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + (Cfg::HALVES + h) * Cfg::TILE_BYTES, &tmv, &full[pre],
-                               h * 64, w.hk, 0, cur[k], policy);
+                               h * 64, w.hk, 0, cur[k], pol);
             }
           }
         }
@@ -330,10 +332,11 @@ __global__ void __launch_bounds__((NW + 1) * 32)
             // An out-of-range page reads as zeros (TMA bounds-fills), never faults.
 #pragma unroll
             for (int h = 0; h < Cfg::HALVES; ++h) {
+              const uint64_t pol = first + k < p.keep_pages ? pol_last : pol_first;
               tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + h * Cfg::TILE_BYTES, &tmk, &full[s], h * 64, w.hk, 0, pid,
-                               policy);
+                               pol);
               tma_load_4d_hint(dst + k * Cfg::PAGE_BYTES + (Cfg::HALVES + h) * Cfg::TILE_BYTES, &tmv, &full[s],
-                               h * 64, w.hk, 0, pid, policy);
+                               h * 64, w.hk, 0, pid, pol);
             }
           }
         }
@@ -668,8 +671,26 @@ namespace {
 constexpr int kNW = 4;
 constexpr int kMaxSplits = 32;
 
+// LKV_DECODE_L2_KEEP: how many leading block-table columns of every sequence load
+// with the L2 evict_last policy - the oldest pages, which in the merged pool are
+// shared final-layer pages that every layer of a step reads again - so that
+// they fill a quarter of L2 and later calls over the same history hit them.
+// Measured on the 8B decode step (batch 8, 8200 keys): a quarter 1850-1857
+// tokens/s, 0.15 1832, a half 1826, 0.7 1782, none 1819; more than a quarter
+// crowds out the streamed weights and pages.
+// At batch 64 (config 2) the same quarter is 3 % of a call's pages and measured
+// 0.5 % slower, so only batches up to 16 keep pages.
+constexpr double kL2KeepFraction = 0.25;
+constexpr int kL2KeepMaxBatch = 16;
+int l2_keep_pages(int l2_bytes, int batch, int hkv, int d, int width) {
+  const double page_bytes = 16.0 * hkv * d * 2 * 2;  // K and V of one page, all heads
+  const double keep = kL2KeepFraction * l2_bytes / (page_bytes * std::max(batch, 1));
+  return (int)std::min<double>(width, std::max(0.0, keep));
+}
+
 struct DevInfo {
   int sms = 0;
+  int l2_bytes = 0;
   int occ[2][4] = {{0}};  // [D==128][log2 GROUP]
   bool attr_done[2][4] = {{false}};
 };
@@ -824,6 +845,14 @@ int decode_paged(const DecodeArgs& a) {
   prm.num_pages = a.num_pages;
   prm.scale_log2 = a.softmax_scale * 1.4426950408889634f;
   prm.early = (a.flags & LKV_DECODE_TABLES_READY) ? 1 : 0;
+  if ((a.flags & LKV_DECODE_L2_KEEP) && a.batch <= kL2KeepMaxBatch) {
+    if (g_dev[dev].l2_bytes == 0) {
+      int l2 = 0;
+      if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev) != cudaSuccess) return LKV_ERR_CUDA;
+      g_dev[dev].l2_bytes = l2 > 0 ? l2 : 1;
+    }
+    prm.keep_pages = l2_keep_pages(g_dev[dev].l2_bytes, a.batch, a.num_kv_heads, a.head_dim, a.max_pages_per_seq);
+  }
 
   // Workspace after the error header: lse [rows * smax] (256-aligned), then o [rows * smax * D].
   uint8_t* ws = static_cast<uint8_t*>(a.workspace) + kWorkspaceHeader;

@@ -540,7 +540,7 @@ class LastKVAttention(nn.Module):
         elif L == 1:
             out = ops.decode_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], out_scale=out_scale,
                                    workspace=cache.workspace, max_pages=meta["W"],
-                                   tables_ready=meta.get("tables_ready", False))
+                                   tables_ready=meta.get("tables_ready", False), l2_keep=True)
         else:
             out = ops.prefill_paged(q_out, cache.pool_k, cache.pool_v, bt, meta["seq_k"], meta["cu_q"], L,
                                     out_scale=out_scale, error_word=cache.error_word, max_pages=meta["W"])

@@ -19,8 +19,10 @@ from . import _capi
 from .contract import PAGE_SIZE, RMarinBackendContractError, require_heads
 
 
-# lkv_decode_paged / lkv_decode_paged_cp flag (include/lastkv_b200.h): the tables predate the PDL chain
+# lkv_decode_paged / lkv_decode_paged_cp flags (include/lastkv_b200.h): the tables predate the PDL chain;
+# the oldest pages of each sequence stay in L2 for the next call over the same history
 DECODE_TABLES_READY = 1
+DECODE_L2_KEEP = 2
 # lkv_rope_norm_append flag: every tensor fp32 (the fp32 model configuration)
 APPEND_FP32 = 4
 
@@ -103,7 +105,7 @@ class Workspace:
 @_traced
 def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, out=None, lse=None,
                  out_scale=None, workspace: Workspace | None = None, max_pages: int | None = None,
-                 partial: bool = False, partial_out=None, tables_ready: bool = False):
+                 partial: bool = False, partial_out=None, tables_ready: bool = False, l2_keep: bool = False):
     """One query token per sequence against its paged history.
 
     q [B, Hq, D] bf16 (row-strided views allowed); block_table int32 [B, W];
@@ -113,7 +115,9 @@ def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, o
     that seq_k, the block table and all but each sequence's last page were
     written before the stream's most recent non-PDL operation (a copy, a torch
     kernel, a graph start), so the kernel may start loading pages before the
-    preceding kernel finishes.
+    preceding kernel finishes.  ``l2_keep=True`` (LKV_DECODE_L2_KEEP): the call is
+    one of several over the same history (a step's layers), so the oldest pages
+    of each sequence, a quarter of the L2 in all, are loaded to stay in L2.
     """
     _check_pool(pool_k, pool_v)
     B, Hq, D = q.shape
@@ -151,7 +155,7 @@ def decode_paged(q, pool_k, pool_v, block_table, seq_k, *, softmax_scale=None, o
         block_table.data_ptr(), block_table.stride(0), seq_k.data_ptr(),
         _ptr(out), out.stride(0) if out is not None else 0, _ptr(lse), _ptr(out_scale), _ptr(po), _ptr(pl),
         B, Hq, Hkv, D, W, float(softmax_scale), workspace.ptr(), workspace.nbytes,
-        DECODE_TABLES_READY if tables_ready else 0, _stream())
+        (DECODE_TABLES_READY if tables_ready else 0) | (DECODE_L2_KEEP if l2_keep else 0), _stream())
     _capi.check(st, "lkv_decode_paged")
     return (po, pl) if partial else out
 
@@ -603,7 +607,8 @@ def decode_cp_state_words(batch: int, num_kv_heads: int) -> int:
 @_traced
 def decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, recv_ptrs, rank: int, world: int, state, *,
                     softmax_scale=None, out=None, out_scale=None, workspace: Workspace | None = None,
-                    max_pages: int | None = None, error_word=None, tables_ready: bool = False):
+                    max_pages: int | None = None, error_word=None, tables_ready: bool = False,
+                    l2_keep: bool = False):
     """Sequence-sharded decode with the exchange fused into the decode kernel (lkv_decode_paged_cp):
     this rank's slice of the keys, every unit's merged rows pushed to every rank's receive
     buffer as the unit finishes, then the poll-and-merge launch.  state: int32 device tensor
@@ -634,7 +639,8 @@ def decode_paged_cp(q, pool_k, pool_v, block_table, seq_k, recv_ptrs, rank: int,
         q.data_ptr(), q.stride(0), pool_k.data_ptr(), pool_v.data_ptr(), pool_k.shape[0], block_table.data_ptr(),
         block_table.stride(0), seq_k.data_ptr(), out.data_ptr(), out.stride(0), _ptr(out_scale), B, Hq, Hkv, D, W,
         float(softmax_scale), workspace.ptr(), workspace.nbytes, rp, rank, world, state.data_ptr(),
-        _ptr(error_word), DECODE_TABLES_READY if tables_ready else 0, _stream())
+        _ptr(error_word), (DECODE_TABLES_READY if tables_ready else 0) | (DECODE_L2_KEEP if l2_keep else 0),
+        _stream())
     _capi.check(st, "lkv_decode_paged_cp")
     return out
 

@@ -388,7 +388,7 @@ class SharedKVFastPath:
         if self.uniform:
             ops.decode_paged(q, pool.pool_k, pool.pool_v, self.bt_all[layer_index, :B], self.seq_k[:B],
                              softmax_scale=self.scale, out=out, out_scale=pool.out_scale[layer_index],
-                             workspace=self.workspace, max_pages=self.W)
+                             workspace=self.workspace, max_pages=self.W, l2_keep=True)
         else:
             ops.prefill_paged(q, pool.pool_k, pool.pool_v, self.bt_all[layer_index, :B], self.seq_k[:B],
                               self.cu_q[:B + 1], self.max_q, softmax_scale=self.scale, out=out,

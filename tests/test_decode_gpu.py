@@ -201,3 +201,20 @@ def test_one_workspace_serves_split_decodes_of_any_batch():
         assert_close_bf16(out.float().cpu().numpy(), ref, what=f"batch {B}")
         np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, rtol=1e-4, atol=1e-3)
     assert ws.error()[0] == 0
+
+
+@pytest.mark.parametrize("case", [CASES[2], CASES[4], CASES[6]], ids=["B4", "B5_ragged", "B64"])
+def test_l2_keep_changes_no_result(case):
+    """LKV_DECODE_L2_KEEP only changes the L2 eviction hint of the page loads (batches up
+    to 16 keep the oldest pages; larger ones ignore it): outputs and LSE bit-identical."""
+    from lastkv_b200 import ops
+
+    seed, B, Hq, Hkv, D, lens = case
+    t, _ = make_paged_case(seed, B, Hq, Hkv, D, lens)
+    res = []
+    for keep in (False, True, True):
+        lse = torch.empty((B, Hq), dtype=torch.float32, device="cuda")
+        out = ops.decode_paged(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], lse=lse, l2_keep=keep)
+        res.append((out.cpu(), lse.cpu()))
+    for o, l in res[1:]:
+        assert torch.equal(o, res[0][0]) and torch.equal(l, res[0][1])
