@@ -76,6 +76,13 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // the caller records the error and leaves its loop.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Atomic add with acquire-release semantics at GPU scope (returns the old value).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t start = global_timer_ns();

@@ -347,8 +347,28 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 
   // -------------------------------------------------------------- consumers
   pdl_wait();
-  // this call's epoch (the combine launch that follows advances the stored one)
-  const uint32_t cp_epoch = p.cp_state ? __ldcg(p.cp_state) + 1u : 0u;
+  // This call's epoch.  Unfused, the combine launch that follows advances the
+  // stored one.  Fused, thread 0 reads it once for the CTA and counts the CTA in;
+  // the last CTA to count stores it for the next call (stream-ordered after this
+  // one): every CTA has read it by then, and no CTA's tail waits on the count.
+  uint32_t cp_epoch = 0u;
+  if (p.cp_state) {
+    if (p.cp_fused) {
+      volatile uint32_t* s_epoch = reinterpret_cast<volatile uint32_t*>(n_touched + 1);
+      if (threadIdx.x == 0) {
+        const uint32_t e = __ldcg(p.cp_state) + 1u;
+        *s_epoch = e;
+        if (atom_add_acq_rel_gpu(p.cp_state + 1, 1u) == gridDim.x - 1) {
+          p.cp_state[1] = 0u;
+          p.cp_state[0] = e;
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+      cp_epoch = *s_epoch;
+    } else {
+      cp_epoch = __ldcg(p.cp_state) + 1u;
+    }
+  }
   const int g = lane >> 2, c = lane & 3;
   // ldmatrix source rows/chunks (see the fragment derivation in the header comment)
   const uint32_t k_row = (lane & 7) + ((lane >> 3) & 1) * 8, k_chunk_hi = lane >> 4;
@@ -540,15 +560,16 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   // rank; then it polls the unit's rows from every rank and merges them in rank
   // order into `out`.  A CTA polls only after all its items and pushes are done,
   // and only for pushes other GPUs' CTAs make without waiting: no wait cycle.
-  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));  // this CTA's partial writes are done
   const int n_items_cta = *n_touched;
-  __threadfence();  // this CTA's partials, before the counting makes them another CTA's input
-  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
   uint32_t* counters = p.cp_state + 2;
+  // Thread 0's acquire-release counting publishes the CTA's partials (ordered
+  // before it by the barrier above) and, for a unit it completes, makes the other
+  // CTAs' partials visible to the whole CTA through the barrier below.
   if (threadIdx.x == 0)
-    for (int k = 0; k < n_items_cta; ++k) last_of[k] = atomicAdd(counters + touched[k], 1u) == (uint32_t)(p.S - 1);
+    for (int k = 0; k < n_items_cta; ++k)
+      last_of[k] = atom_add_acq_rel_gpu(counters + touched[k], 1u) == (uint32_t)(p.S - 1);
   asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
-  __threadfence();  // the other CTAs' partials of the units this CTA completes
   for (int k = 0; k < n_items_cta; ++k) {
     if (!last_of[k]) continue;
     const int unit = touched[k];
@@ -573,11 +594,6 @@ __global__ void __launch_bounds__((NW + 1) * 32)
                       fail, lane);
   }
   if (fail && lane == 0) report_error(p.cp_err, DEVERR_WAIT_TIMEOUT, 1, 2000000 + (int)blockIdx.x);
-  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32));
-  if (threadIdx.x == 0 && atomicAdd(p.cp_state + 1, 1u) == gridDim.x - 1) {
-    p.cp_state[1] = 0u;        // every CTA has read the epoch and counted itself
-    p.cp_state[0] = cp_epoch;  // the next call (stream-ordered after this one) uses the next epoch
-  }
 }
 
 // ------------------------------------------------------------------ merge
