@@ -45,10 +45,10 @@ __device__ __forceinline__ float ll_take(const uint64_t* src, uint32_t epoch, ui
 // fp32 sums, one 1/L), scales by out_scale[head] and writes bf16.  Rank s's
 // partial comes from slot_base + s * part_words, polled for `epoch`, except
 // that `own` (this rank's packed partial o | lse, or null) replaces the rank
-// `rank` entry when given.  The words are requested together - every rank's
-// LSE at once (lane s reads rank s), then the o words of four ranks at a time -
-// and only a word that has not arrived yet is polled again, so a row costs a
-// few memory round trips rather than one per word.
+// `rank` entry when given.  The words are requested together - the o words of
+// the first four ranks with every rank's LSE (lane s reads rank s), then four
+// ranks at a time - and only a word that has not arrived yet is polled again,
+// so a row costs a few memory round trips rather than one per word.
 template <int D>
 __device__ __forceinline__ void cp_merge_row(const uint64_t* slot_base, int64_t part_words, int world, int rank,
                                              const float* own, int64_t rows, int64_t row, int Hq,
@@ -58,6 +58,21 @@ __device__ __forceinline__ void cp_merge_row(const uint64_t* slot_base, int64_t 
   constexpr int G = 4;  // ranks whose o words are in flight together
   constexpr float to2 = 1.4426950408889634f;
   const int64_t lse_off = rows * D;
+  uint64_t wv[G][PER];
+  auto load_words = [&](int s0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int s = s0 + g;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) wv[g][e] = 0;
+      if (s < world && !(s == rank && own)) {
+        const uint64_t* src = slot_base + (int64_t)s * part_words + row * D + lane * PER;
+#pragma unroll
+        for (int e = 0; e < PER; e += 2) ld_ll2(src + e, wv[g][e], wv[g][e + 1]);
+      }
+    }
+  };
+  load_words(0);            // requested together with the LSE words below
   float my_ls = -INFINITY;  // lane s < world: rank s's LSE in log2 units
   if (lane < world)
     my_ls = ((lane == rank && own) ? own[lse_off + row]
@@ -73,18 +88,7 @@ __device__ __forceinline__ void cp_merge_row(const uint64_t* slot_base, int64_t 
   float L = 0.f;
   if (M != -INFINITY) {
     for (int s0 = 0; s0 < world; s0 += G) {
-      uint64_t wv[G][PER];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const int s = s0 + g;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) wv[g][e] = 0;
-        if (s < world && !(s == rank && own)) {
-          const uint64_t* src = slot_base + (int64_t)s * part_words + row * D + lane * PER;
-#pragma unroll
-          for (int e = 0; e < PER; e += 2) ld_ll2(src + e, wv[g][e], wv[g][e + 1]);
-        }
-      }
+      if (s0 > 0) load_words(s0);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const int s = s0 + g;

@@ -90,6 +90,29 @@ __device__ __forceinline__ void merge_row_parts(const float* o_base, int64_t o_s
                                                 int64_t lse_step, int S, float to2, int lane,
                                                 float (&acc)[D / 32], float& inv, float& lse2) {
   constexpr int PER = D / 32;
+  constexpr int C = 8;  // parts whose o rows are requested together
+  float v[C][PER];
+  auto load_parts = [&](int s0) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int s = s0 + c;
+      const float* src = o_base + s * o_step + lane * PER;
+      if (s >= S) {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) v[c][e] = 0.f;
+      } else if constexpr (PER == 4) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
+        v[c][0] = t.x;
+        v[c][1] = t.y;
+        v[c][2] = t.z;
+        v[c][3] = t.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) v[c][e] = __ldcg(src + e);
+      }
+    }
+  };
+  load_parts(0);  // in flight together with the LSE loads: no dependency between them
   const float my_ls = lane < S ? __ldcg(lse_base + lane * lse_step) * to2 : -INFINITY;
   float M = my_ls;
 #pragma unroll
@@ -99,29 +122,22 @@ __device__ __forceinline__ void merge_row_parts(const float* o_base, int64_t o_s
   float L = 0.f;
   if (M != -INFINITY) {
     const float my_w = my_ls == -INFINITY ? 0.f : exp2f(my_ls - M);
-#pragma unroll 4
-    for (int s = 0; s < S; ++s) {
-      const float w = __shfl_sync(0xffffffffu, my_w, s);
-      const float* src = o_base + s * o_step + lane * PER;
-      float v[PER];
-      if constexpr (PER == 4) {
-        const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
-        v[0] = t.x;
-        v[1] = t.y;
-        v[2] = t.z;
-        v[3] = t.w;
-      } else {
+    for (int s0 = 0; s0 < S; s0 += C) {
+      if (s0 > 0) load_parts(s0);
 #pragma unroll
-        for (int e = 0; e < PER; ++e) v[e] = __ldcg(src + e);
-      }
-      // a part with -inf LSE (w == 0) leaves L and acc untouched, whatever its o holds
-      const bool use = w != 0.f;
-      const float Ln = L + w;
-      L = use ? Ln : L;
+      for (int c = 0; c < C; ++c) {
+        const int s = s0 + c;
+        if (s >= S) break;
+        const float w = __shfl_sync(0xffffffffu, my_w, s);
+        // a part with -inf LSE (w == 0) leaves L and acc untouched, whatever its o holds
+        const bool use = w != 0.f;
+        const float Ln = L + w;
+        L = use ? Ln : L;
 #pragma unroll
-      for (int e = 0; e < PER; ++e) {
-        const float an = acc[e] + w * v[e];
-        acc[e] = use ? an : acc[e];
+        for (int e = 0; e < PER; ++e) {
+          const float an = acc[e] + w * v[c][e];
+          acc[e] = use ? an : acc[e];
+        }
       }
     }
   }
