@@ -849,7 +849,8 @@ def measure_cp(steps: int, warmup: int, world: int, rank: int, device, combine: 
     last rank also the 2048-token ring window).  With one rank a layer is the
     plain split-KV decode; with more, each layer is ``lkv_decode_paged_cp`` (the
     decode kernel pushes each unit's merged rows to every rank over peer memory,
-    then one poll-and-merge launch) or, with ``combine="nccl"``, the partial
+    then polls and merges every rank's rows in the same launch) or, with
+    ``combine="nccl"``, the partial
     decode + NCCL all-gather + merge.  The queries are the same on every rank (one
     decode token).  After the timed region rank 0 checks sampled rows of its
     output against an fp32 recomputation over all ranks' keys (each rank's slice
@@ -947,7 +948,8 @@ def measure_cp(steps: int, warmup: int, world: int, rank: int, device, combine: 
     except (OSError, KeyError, ValueError):
         peak = 6650.0
     mode = ("plain split-KV decode (one GPU)" if cp is None else
-            "decode kernel pushes each unit's merged rows over peer memory; one poll + LSE merge launch"
+            "one decode launch per layer: pushes each unit's merged rows over peer memory, then polls and "
+            "LSE-merges every rank's rows"
             if cp.combine == "p2p" else "NCCL all-gather + LSE merge")
     line = {"metric": "context-parallel decode tokens/s (attention only, 32 layers, 128K context)",
             "value": B * steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
