@@ -575,13 +575,28 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    side = {}
+    if not args.no_prefill:
+        # The tensor-core legs first, before the HBM-bound decode loop has run the GPU
+        # into its power cap: each is a short burst, set against the burst GEMM peak,
+        # with the SM clocks sampled around the two of them.
+        pclk = ClockSampler(uuid)
+        pclk.start()
+        # the small case (profiler captures) runs the same spans with 2 sequences
+        side["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
+        side["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1, kv_splits=args.wan_kv_splits)
+        tc_clk = pclk.stop()
+        side["prefill"]["clocks"] = side["wan"]["clocks"] = tc_clk
+        side["commit"] = measure_commit(device)
+        torch.cuda.empty_cache()
+
     stream = torch.cuda.current_stream()
     for _ in range(max(args.warmup, 0)):
         for l in range(L):
             layer(l)
     torch.cuda.synchronize()
 
-    uuid = str(torch.cuda.get_device_properties(device).uuid)
     clocks = ClockSampler(uuid)
     # The layer calls go back to back (no events between them, which would cut the
     # programmatic-dependent-launch overlap of consecutive kernels, as a real decode
@@ -714,12 +729,7 @@ def run_ours(args):
         "gpu_launches": int(args.steps * L * launches_per_call),
         "kv_splits": splits,
     }
-    if not args.no_prefill:
-        # the small case (profiler captures) runs the same spans with 2 sequences
-        line["prefill"] = measure_prefill(device, batch=None if args.case == "config2" else 2)
-        line["wan"] = measure_wan(device, batch=None if args.case == "config2" else 1, kv_splits=args.wan_kv_splits)
-        line["commit"] = measure_commit(device)
-        torch.cuda.empty_cache()
+    line.update(side)
     if not args.no_e2e8b:
         # config 3 on the same ranks: the 8B architecture end to end (weak scaling, batch 8 per GPU)
         wl = None
