@@ -207,7 +207,7 @@ __device__ __forceinline__ float fmax3f(float a, float b, float c) {
 // 1.5 * 2^23 rounds x to an integer held in the low mantissa bits of t; then
 // 2^f by a degree-3 polynomial and j added into the exponent field.  The
 // coefficients are a minimax fit of the relative error of 2^f on [-0.5, 0.5]
-// (Remez exchange, exp2_poly_fit.py beside this file): max relative error
+// (Remez exchange, restated in tests/test_exp2_poly_cpu.py): max relative error
 // 7.5e-5, far below the bf16 rounding (2^-9) applied to softmax weights.
 // Inputs are clamped at -125 (2^-125 instead of the SFU's flush to zero; a
 // masked -inf therefore yields 2^-125, a weight 1e-38 below any visible key's).

@@ -1,11 +1,10 @@
 """The FMA-pipe exponential of the prefill softmax (``ex2_poly2`` in
 lastkv_b200/csrc/common.cuh), restated bit for bit in numpy float32 and
 checked against 2^x: the committed coefficients are the ones the Remez fit
-beside the kernel produces, and the reconstruction (round-to-nearest split,
-polynomial, exponent add) stays within the fit's relative error over the whole
-range the softmax feeds it (x <= 8 after the lazy max; clamped at -125)."""
+below produces, and the reconstruction (round-to-nearest split, polynomial,
+exponent add) stays within the fit's relative error over the whole range the
+softmax feeds it (x <= 8 after the lazy max; clamped at -125)."""
 
-import importlib.util
 import os
 import re
 
@@ -14,6 +13,37 @@ import numpy as np
 from conftest import ROOT
 
 CSRC = os.path.join(ROOT, "lastkv_b200", "csrc")
+
+
+def remez_exp2(degree: int = 3, lo: float = -0.5, hi: float = 0.5, iters: int = 30):
+    """2^f on f in [-0.5, 0.5] with minimax *relative* error, by the Remez exchange
+    algorithm (solve for the equioscillating error on n + 2 reference points, move the
+    points to the new extrema, repeat); float32 coefficients c0..c3 (the constants
+    kExp2C0..kExp2C3 of common.cuh)."""
+    n = degree
+    k = np.arange(n + 2)
+    x = (lo + hi) / 2 + (hi - lo) / 2 * np.cos(np.pi * (n + 1 - k) / (n + 1))
+    grid = np.linspace(lo, hi, 200001)
+    c = None
+    for _ in range(iters):
+        a = np.zeros((n + 2, n + 2))
+        for i in range(n + 1):
+            a[:, i] = x ** i
+        a[:, n + 1] = -((-1.0) ** k) * np.exp2(x)
+        sol = np.linalg.solve(a, np.exp2(x))
+        c = sol[:n + 1]
+        err = (np.polyval(c[::-1], grid) - np.exp2(grid)) / np.exp2(grid)
+        idx = [0]
+        sign = np.sign(err)
+        for j in range(1, len(grid)):
+            if sign[j] != sign[idx[-1]]:
+                idx.append(j)
+            elif abs(err[j]) > abs(err[idx[-1]]):
+                idx[-1] = j
+        if len(idx) >= n + 2:
+            best = max(range(len(idx) - (n + 1)), key=lambda s: min(abs(err[idx[s:s + n + 2]])))
+            x = grid[idx[best:best + n + 2]]
+    return c.astype(np.float32)
 
 
 def _coefficients():
@@ -41,10 +71,7 @@ def ex2_poly_f32(x, c):
 
 
 def test_coefficients_are_the_remez_fit():
-    spec = importlib.util.spec_from_file_location("exp2_poly_fit", os.path.join(CSRC, "exp2_poly_fit.py"))
-    fit = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(fit)
-    np.testing.assert_array_equal(fit.remez_exp2(), _coefficients())
+    np.testing.assert_array_equal(remez_exp2(), _coefficients())
 
 
 def test_relative_error_over_the_softmax_range():
