@@ -189,3 +189,82 @@ def test_plugin_backend_reproduces_reference_calls(small_d128):
     finally:
         vllm_plugin.uninstall_fast_path()
         vllm_plugin._LEAN_BUILDER = None
+
+
+def test_captured_decode_graph_carries_boundary_commits():
+    """Uniform decode steps replayed from one CUDA graph (every layer's run_layer):
+    the boundary commits of the rows that cross a chunk boundary ride in layer 0's
+    append as a device-side row count, so the same graph serves steps with and
+    without commits.  Outputs and pools are bit-identical to eager steps with a
+    separate blend launch (fuse_commit = False)."""
+    from lastkv_b200.vllm_backend import Span
+
+    rng = np.random.default_rng(11)
+    L, slots, C, hkv, hq, d = 3, 4, 32, 2, 8, 128
+    max_tok = 128
+    order = rng.permutation(slots * (max_tok // 16))
+    alpha_logits = torch.from_numpy(rng.standard_normal((L, hkv)).astype(np.float32))
+    v_scale = torch.from_numpy(rng.uniform(0.4, 1.6, (L, hkv)).astype(np.float32))
+    prompt = [30, 31, 20, 45]  # rows cross the boundary at 32 (or 64) at different steps
+    steps = 24
+    inputs = []  # per call: q, k, v for every layer
+    spans_of = []
+    for phase in range(1 + steps):
+        if phase == 0:
+            spans = [Span(s, 0, prompt[s]) if prompt[s] <= C else None for s in range(slots)]
+            spans = [sp for sp in spans if sp is not None] + [Span(3, 0, C)]
+        else:
+            spans = [Span(s, prompt[s] + phase - 1, 1) for s in range(slots)]
+        spans_of.append(spans)
+    spans_of.insert(1, [Span(3, C, prompt[3] - C)])  # the rest of row 3's prompt
+    for spans in spans_of:
+        T = sum(sp.num_query_tokens for sp in spans)
+        inputs.append([(torch.from_numpy(O.bf16_round(rng.standard_normal((T, hq * d)))).cuda().bfloat16(),
+                        torch.from_numpy(O.bf16_round(rng.standard_normal((T, hkv * d)))).cuda().bfloat16(),
+                        torch.from_numpy(O.bf16_round(rng.standard_normal((T, hkv * d)))).cuda().bfloat16())
+                       for _ in range(L)])
+
+    def run(fuse, graph):
+        pool, fast = _fast(L, slots, max_tok, C, hkv, hq, d, order)
+        fast.fuse_commit = fuse
+        pool.bind_parameters(alpha_logits, v_scale, hq)
+        fast.register_layers([(None, None)] * L, None, 1e-6)
+        outs = []
+        static_in = [[torch.empty_like(t) for t in lay] for lay in inputs[-1]]
+        static_out = [torch.empty((slots, hq, d), dtype=torch.bfloat16, device="cuda") for _ in range(L)]
+        g = None
+        for spans, xs in zip(spans_of, inputs):
+            fast.prepare(spans)
+            decode = all(sp.num_query_tokens == 1 for sp in spans)
+            if graph and decode:
+                for l in range(L):
+                    for dst, src in zip(static_in[l], xs[l]):
+                        dst.copy_(src)
+                if g is None:  # captured on the first decode step, then replayed every step
+                    g = torch.cuda.CUDAGraph()
+                    s = torch.cuda.Stream()
+                    s.wait_stream(torch.cuda.current_stream())
+                    with torch.cuda.graph(g, stream=s):
+                        for l in range(L):
+                            fast.run_layer(l, *static_in[l], static_out[l])
+                    torch.cuda.current_stream().wait_stream(s)
+                g.replay()
+                outs.append(torch.stack([o.clone() for o in static_out]))
+            else:
+                T = sum(sp.num_query_tokens for sp in spans)
+                res = []
+                for l in range(L):
+                    out = torch.empty((T, hq, d), dtype=torch.bfloat16, device="cuda")
+                    fast.run_layer(l, *xs[l], out)
+                    res.append(out)
+                outs.append(torch.stack(res))
+        torch.cuda.synchronize()
+        fast.check_errors()
+        assert pool.committed == [32, 32, 32, 64]
+        return [o.cpu() for o in outs], pool.pool_k.cpu(), pool.pool_v.cpu()
+
+    want = run(False, False)
+    got = run(True, True)
+    for a, b in zip(want[0], got[0]):
+        assert torch.equal(a, b)
+    assert torch.equal(want[1], got[1]) and torch.equal(want[2], got[2])
