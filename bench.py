@@ -523,6 +523,19 @@ def measure_commit(device, reps: int = 5):
         count.fill_(B)
         dev_count[f"{per_sm}_per_sm"] = {"no_boundary_us": idle_us, "no_boundary_extra_us": idle_us - plain_us,
                                          "boundary_ms": timed(lambda: append(c))}
+    # parity at these shapes: the fused launch (host row count, then device row count) and
+    # the two separate launches from the same starting pools give the same bits
+    start_k, start_v = pool_k.clone(), pool_v.clone()
+    separate()
+    want_k, want_v = pool_k.clone(), pool_v.clone()
+    same = {}
+    for name, c in (("host_count", commit), ("device_count", commit._replace(count=count, blocks=8 * sms))):
+        pool_k.copy_(start_k)
+        pool_v.copy_(start_v)
+        count.fill_(B)
+        append(c)
+        same[name] = bool(torch.equal(pool_k, want_k) and torch.equal(pool_v, want_v))
+    del start_k, start_v, want_k, want_v
     if int(err[0]):
         raise RuntimeError(f"commit bench: device error word {err.tolist()}")
     page_bytes = 16 * Hkv * D * 2
@@ -541,6 +554,9 @@ def measure_commit(device, reps: int = 5):
             "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak,
             "peak_source": src_peak, "l2": f"{nbytes / 1e9:.1f} GB per launch (larger than L2); no flush",
             "append_alone_us": plain_us, "device_count": dev_count,
+            "parity": {"fused_equals_separate": same, "pass": all(same.values()),
+                       "reference": "append + lkv_blend_chunk as two launches on the same starting pools, "
+                                    "every pool byte compared"},
             "kernel": "append_commit_kernel<128> (vs rope_norm_append_kernel<128> + blend_chunk_kernel)"}
 
 
