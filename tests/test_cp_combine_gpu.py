@@ -129,3 +129,81 @@ def test_fused_exchange_missing_peer_times_out_into_error_word():
     words = peer.view(2, 2, -1)[1, 0, : rows * D].cpu().numpy().astype(np.uint64)
     assert np.all((words >> np.uint64(32)) == 1)
     assert float(torch.ones(4, device="cuda").sum()) == 4.0
+
+
+def _prefill_peer_words(recv, world, rows, D, epoch, parts):
+    """Write rank r's partial (o [rows, D], natural-log lse [rows]) into receive slot
+    [epoch & 1][r] as {value, epoch} words, as rank r's push would (peers 1..world-1)."""
+    part_words = (rows * (D + 1) + 1) // 2 * 2
+    slots = recv.view(2, world, -1)[:, :, :part_words]
+    for r, (o, lse) in parts.items():
+        vals = torch.cat([o.flatten(), lse.flatten()]).contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        slots[epoch & 1, r, : rows * (D + 1)] = vals | (epoch << 32)
+
+
+@pytest.mark.parametrize("world", [3, 8])
+def test_eight_rank_merge_from_arrived_words(world):
+    """The rank-order merge with more ranks than one batch of requested words (8 ranks:
+    two batches of four): every peer's words are already in this rank's receive buffer
+    (written here as their pushes would), so nothing waits on another kernel; the
+    combine equals merge_partials over the same parts bit for bit."""
+    from lastkv_b200 import ops
+
+    B, Hq, D = 2, 8, 128
+    rows = B * Hq
+    sizes = ops.cp_combine_sizes(rows, D, world)
+    parts = {r: _partial(rows, D, 40 + r) for r in range(world)}
+    send = torch.zeros(sizes["send_floats"], device="cuda")
+    send[: rows * D] = parts[0][0].flatten()
+    send[rows * D: rows * (D + 1)] = parts[0][1]
+    mine = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
+    peers = [torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda") for _ in range(world - 1)]
+    _prefill_peer_words(mine, world, rows, D, 1, {r: parts[r] for r in range(1, world)})
+    scale = torch.rand(Hq, device="cuda") + 0.5
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    got = ops.cp_combine(send, [mine.data_ptr()] + [p.data_ptr() for p in peers], 0, world, state, rows, D, Hq,
+                         out_scale=scale, error_word=err)
+    o_all = torch.stack([parts[r][0].view(B, Hq, D) for r in range(world)])
+    l_all = torch.stack([parts[r][1].view(B, Hq) for r in range(world)])
+    ref = ops.merge_partials(o_all, l_all, out_scale=scale)
+    torch.cuda.synchronize()
+    assert err.cpu().tolist() == [0, 0, 0, 0]
+    torch.testing.assert_close(got.view(B, Hq, D), ref.view(B, Hq, D), rtol=0, atol=0)
+
+
+def test_fused_decode_eight_ranks_from_arrived_words():
+    """lkv_decode_paged_cp as rank 0 of 8 (the decode kernel's own unit merge, push to all
+    eight buffers, then the poll-and-merge of two batches of four ranks): the seven peers'
+    words are in place before the launch, so the kernel waits on nothing; the output
+    equals this rank's partial decode merged with the peers' parts by merge_partials."""
+    from lastkv_b200 import ops
+    from tests.gpu_helpers import make_paged_case
+
+    world = 8
+    B, Hq, Hkv, D = 4, 32, 8, 128
+    rows = B * Hq
+    t, _ = make_paged_case(37, B, Hq, Hkv, D, [3000, 17, 900, 2048])
+    scale = torch.rand(Hq, device="cuda") + 0.5
+    sizes = ops.cp_combine_sizes(rows, D, world)
+    mine = torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda")
+    peers = [torch.zeros(sizes["recv_words"], dtype=torch.int64, device="cuda") for _ in range(world - 1)]
+    parts = {r: _partial(rows, D, 70 + r) for r in range(1, world)}
+    _prefill_peer_words(mine, world, rows, D, 1, parts)
+    state = torch.zeros(ops.decode_cp_state_words(B, Hkv), dtype=torch.int32, device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws = ops.Workspace.for_decode(B, Hq, D, t["bt"].shape[1], device="cuda")
+    got = ops.decode_paged_cp(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"],
+                              [mine.data_ptr()] + [p.data_ptr() for p in peers], 0, world, state,
+                              out_scale=scale, workspace=ws, error_word=err)
+    po, pl = ops.decode_paged(t["q"], t["pool_k"], t["pool_v"], t["bt"], t["seq_k"], partial=True)
+    o_all = torch.stack([po] + [parts[r][0].view(B, Hq, D) for r in range(1, world)])
+    l_all = torch.stack([pl] + [parts[r][1].view(B, Hq) for r in range(1, world)])
+    ref = ops.merge_partials(o_all, l_all, out_scale=scale)
+    torch.cuda.synchronize()
+    assert err.cpu().tolist() == [0, 0, 0, 0] and ws.error()[0] == 0
+    torch.testing.assert_close(got.view(B, Hq, D), ref.view(B, Hq, D), rtol=0, atol=0)
+    # this rank's merged rows reached every peer's buffer with the call's epoch
+    for p in peers:
+        words = p.view(2, world, -1)[1, 0, : rows * D].cpu().numpy().astype(np.uint64)
+        assert np.all((words >> np.uint64(32)) == 1)
