@@ -264,3 +264,34 @@ def test_graph_runner_multi_page_chunks_fused_equals_separate():
         runs.append((torch.cat(got, 1).cpu(), cache.pool_k.cpu(), cache.pool_v.cpu()))
     for a, b in zip(*runs):
         assert torch.equal(a, b)
+
+
+def test_queued_commit_is_flushed_by_reorder_and_reserve(small_d128):
+    """A prompt that ends exactly on a chunk boundary leaves its commit queued; beam
+    reordering and growing the cache run it first, and decoding continues with the same
+    logits as the cache that blended at the boundary."""
+    from tests.test_hf_model_gpu import build_small
+
+    data = small_d128
+    model = build_small(data)
+    tokens = torch.from_numpy(data["tokens"]).cuda()
+    order = torch.tensor([1, 0])
+    outs = []
+    for fuse in (True, False):
+        cache = model.new_cache(2, 48)
+        cache.fuse_commit = fuse
+        with torch.no_grad():
+            model(tokens[:, :32], cache)  # boundaries at 16 and 32 (chunk 16)
+            assert (cache._pending is not None) == fuse
+            cache.reorder_cache(order)
+            assert cache._pending is None
+            a, _ = model(tokens[order, 32:33], cache)
+            model(tokens[order, 33:48], cache)  # to 48 tokens: the next boundary, its commit queued
+            assert (cache._pending is not None) == fuse
+            cache.reserve(80)
+            assert cache._pending is None
+            b, _ = model(tokens[order, 48:52], cache)
+        cache.check_errors()
+        outs.append((a.float().cpu(), b.float().cpu()))
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
