@@ -569,8 +569,8 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   if (!p.cp_fused) return;
 
   // ---------------------------------------------------------------- fused exchange
-  // One fence and one round of arrival counting per CTA, after all its items (a
-  // fence and two barriers per item stall the consumers while the ring waits).
+  // The arrival counting runs once per CTA, after all its items (counting per
+  // item, with its barriers, stalls the consumers while the ring waits).
   // The last CTA to count a unit merges the unit's S split partials
   // (merge_partials_kernel's arithmetic) and pushes the merged rows to every
   // rank; then it polls the unit's rows from every rank and merges them in rank
