@@ -55,7 +55,7 @@ __device__ __forceinline__ void cp_merge_row(const uint64_t* slot_base, int64_t 
                                              const float* out_scale, __nv_bfloat16* out, int64_t out_stride_tok,
                                              uint32_t epoch, uint64_t start, bool& fail, int lane) {
   constexpr int PER = D / 32;
-  constexpr int G = 4;  // ranks whose o words are in flight together
+  constexpr int G = 8;  // ranks whose o words are in flight together
   constexpr float to2 = 1.4426950408889634f;
   const int64_t lse_off = rows * D;
   uint64_t wv[G][PER];

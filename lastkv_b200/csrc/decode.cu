@@ -90,7 +90,7 @@ __device__ __forceinline__ void merge_row_parts(const float* o_base, int64_t o_s
                                                 int64_t lse_step, int S, float to2, int lane,
                                                 float (&acc)[D / 32], float& inv, float& lse2) {
   constexpr int PER = D / 32;
-  constexpr int C = 8;  // parts whose o rows are requested together
+  constexpr int C = 16;  // parts whose o rows are requested together
   float v[C][PER];
   auto load_parts = [&](int s0) {
 #pragma unroll
