@@ -12,6 +12,10 @@
 // blend_chunk_kernel - at a chunk boundary, ring = a*raw + (1-a)*ring for every
 //   layer ring, K and V (V in V/s units), each product rounded to bf16 like the
 //   four eager torch ops (fused_qkv.py:158-201, batching.py:1099-1144).
+// append_commit_kernel - the append of a step's first layer and the blend of
+//   the chunk the previous step finished, in one launch (the reference runs
+//   that commit when the next step starts); the blend's row count may be read
+//   on the device, so a captured step carries a commit or none.
 // build_block_tables_kernel - bt_all[l][b][c] = bt[b][c] for the older pages and
 //   bt[b][c] + ring_base[l] for ring pages (fastpath.py:422-424).
 
