@@ -77,6 +77,20 @@ def test_argument_validation_needs_no_gpu(lib):
                                        1, 1, 1, 8, 8, 96, 1, 1.0, 2, None, None, None, None) == 2
 
 
+def test_append_commit_validation_needs_no_gpu(lib):
+    def call(T=0, hq=8, hkv=8, d=128, flags=0, layers=0, rows=0, ppc=0, blocks=0):
+        return lib.lkv_rope_norm_append_commit(
+            None, 0, None, 0, None, 0, None, None, 0, 0, None, None, 1e-6, None, None, 0, None, None, None, 0,
+            None, None, None, 0, T, hq, hkv, d, flags,
+            None, None, 0, None, None, 0, None, layers, rows, ppc, None, blocks, None, None)
+
+    assert call(d=96) == 2                       # head_dim 64 or 128 only
+    assert call(flags=4) == 2                    # fp32 pools: append, then lkv_blend_chunk_f32
+    assert call(blocks=-1) == 1                  # negative commit block count
+    assert call(layers=2, rows=1, ppc=4) == 1    # a commit without its pools and page lists
+    assert call() == 0                           # no tokens and no commit: nothing to launch
+
+
 def test_product_package_never_imports_oracle():
     pkg = os.path.join(ROOT, "lastkv_b200")
     for dirpath, _, files in os.walk(pkg):
