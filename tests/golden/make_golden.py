@@ -179,7 +179,12 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    ap.add_argument("--only", choices=["access_plan"], default=None,
+                    help="regenerate one fixture only (access_plan needs neither torch nor a model)")
     args = ap.parse_args()
+    if args.only == "access_plan":
+        access_plan_golden(args.reference, args.out)
+        return
     torch, Config, Model = build(args.reference)
     torch.set_num_threads(1)
 
@@ -249,6 +254,41 @@ def main():
     np.savez_compressed(os.path.join(args.out, "config1_124m.npz"), **out)
 
     wan_golden(args.reference, args.out, torch)
+    access_plan_golden(args.reference, args.out)
+
+
+def access_plan_golden(reference, out_dir):
+    """The reference's dependency-free access planner
+    (vllm/src/lastkv/vllm/backends/rmarin_flashinfer/access_plan.py:407-474) over a grid
+    of chunk sizes and query positions: each query's older / recent / current token
+    ranges and whether a source pass (and so an LSE merge) exists, for the top layer
+    and a lower one.  Written to access_plan.npz, rows
+    [chunk, position, top, older.start, older.end, recent.start, recent.end,
+     current.start, current.end, requires_lse_merge]."""
+    import importlib.util
+
+    path = os.path.join(reference, "vllm", "src", "lastkv", "vllm", "backends", "rmarin_flashinfer",
+                        "access_plan.py")
+    spec = importlib.util.spec_from_file_location("rmarin_access_plan", path)
+    ap = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = ap  # its dataclasses resolve the module by name
+    spec.loader.exec_module(ap)
+    rows = []
+    for chunk in (4, 16, 32, 64, 1024, 4096):
+        if chunk <= 64:
+            positions = range(0, 3 * chunk + 3)
+        else:
+            positions = sorted({0, 1, chunk - 1, chunk, chunk + 1, 2 * chunk - 1, 2 * chunk, 2 * chunk + 1,
+                                5 * chunk + 7, 8191, 8192, 8200, 131071})
+        for p in positions:
+            for top in (0, 1):
+                state = ap.RMarinRequestState.for_query(request_id="r", query_position=p, chunk_size=chunk)
+                layer = ap.RMarinLayerSpec(layer_index=1 if top else 0, num_layers=2, source_layer_index=1)
+                plan = ap.plan_rmarin_access(state, layer)
+                rows.append([chunk, p, top, plan.older.start, plan.older.end, plan.recent.start, plan.recent.end,
+                             plan.current.start, plan.current.end, int(plan.requires_lse_merge)])
+    np.savez_compressed(os.path.join(out_dir, "access_plan.npz"), rows=np.array(rows, dtype=np.int64))
+    print("access_plan:", len(rows), "rows")
 
 
 def _diffusers_stub() -> str:
