@@ -179,11 +179,12 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
-    ap.add_argument("--only", choices=["access_plan"], default=None,
-                    help="regenerate one fixture only (access_plan needs neither torch nor a model)")
+    ap.add_argument("--only", choices=["planner"], default=None,
+                    help="regenerate the planner fixtures only (they need neither torch nor a model)")
     args = ap.parse_args()
-    if args.only == "access_plan":
+    if args.only == "planner":
         access_plan_golden(args.reference, args.out)
+        history_golden(args.reference, args.out)
         return
     torch, Config, Model = build(args.reference)
     torch.set_num_threads(1)
@@ -255,6 +256,77 @@ def main():
 
     wan_golden(args.reference, args.out, torch)
     access_plan_golden(args.reference, args.out)
+    history_golden(args.reference, args.out)
+
+
+def _planner_modules(reference):
+    """access_plan.py and reference.py of the reference's vLLM backend, loaded as a
+    package of their own (the backend package's __init__ imports vLLM; these two
+    modules need neither vLLM nor torch)."""
+    import importlib.util
+    import types
+
+    pkg_dir = os.path.join(reference, "vllm", "src", "lastkv", "vllm", "backends", "rmarin_flashinfer")
+    pkg = types.ModuleType("rmarin_planner")
+    pkg.__path__ = [pkg_dir]
+    sys.modules["rmarin_planner"] = pkg
+    mods = []
+    for name in ("access_plan", "reference"):
+        spec = importlib.util.spec_from_file_location(f"rmarin_planner.{name}", os.path.join(pkg_dir, name + ".py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = mod  # its dataclasses resolve the module by name
+        spec.loader.exec_module(mod)
+        mods.append(mod)
+    return mods
+
+
+def history_golden(reference, out_dir):
+    """The reference's executable history oracle (reference.py:342-439,
+    resolve_reference_history with SourceScale mode "v") on seeded float values:
+    for each (chunk, query position, layer kind) the raw top-layer source K/V, the
+    layer's own K/V of recent + current, the per-head alpha logits and value scales,
+    and the effective history [older: scaled source | recent: blend | current: local]
+    it resolves, in float64.  Written to reference_history.npz."""
+    ap, ref = _planner_modules(reference)
+    rng = np.random.default_rng(2024)
+    hkv, d = 2, 8
+    out = {}
+    cases = [(4, p) for p in (0, 3, 4, 6, 7, 9, 13)] + [(8, p) for p in (5, 8, 17, 23, 31)] + [(16, 40)]
+    for i, (chunk, pos) in enumerate(cases):
+        top = i % 2
+        cur = (pos // chunk) * chunk
+        rec = max(0, cur - chunk)
+        src_end = pos + 1 if top else cur  # the top layer also holds its own raw current tokens
+        raw_k = rng.standard_normal((src_end, hkv, d)).astype(np.float32).astype(np.float64)
+        raw_v = rng.standard_normal((src_end, hkv, d)).astype(np.float32).astype(np.float64)
+        loc_k = rng.standard_normal((pos + 1 - rec, hkv, d)).astype(np.float32).astype(np.float64)
+        loc_v = rng.standard_normal((pos + 1 - rec, hkv, d)).astype(np.float32).astype(np.float64)
+        logits = rng.standard_normal(hkv).astype(np.float32).astype(np.float64)
+        scales = rng.uniform(0.3, 1.7, hkv).astype(np.float32).astype(np.float64)
+        state = ap.RMarinRequestState.for_query(request_id="r", query_position=pos, chunk_size=chunk,
+                                                source_initialized_end=src_end)
+        plan = ap.plan_rmarin_access(state, ap.RMarinLayerSpec(layer_index=1 if top else 0, num_layers=2,
+                                                              source_layer_index=1))
+
+        def tok(k, v):
+            return ref.ReferenceKVToken(key=tuple(map(tuple, k)), value=tuple(map(tuple, v)))
+
+        raw = ref.IndexedReferenceCache.from_mapping(
+            request_id="r", entries={t: tok(raw_k[t], raw_v[t]) for t in range(src_end)})
+        local = ref.IndexedReferenceCache.from_mapping(
+            request_id="r", entries={rec + t: tok(loc_k[t], loc_v[t]) for t in range(pos + 1 - rec)})
+        hist = ref.resolve_reference_history(plan, raw_source=raw, same_layer_local=local,
+                                             alpha_logits=tuple(logits.tolist()),
+                                             source_scale=ref.SourceScale(mode="v", value_scales=tuple(scales)))
+        eff_k = np.array([t.effective.key for t in hist.tokens])
+        eff_v = np.array([t.effective.value for t in hist.tokens])
+        for name, val in (("meta", np.array([chunk, pos, top], np.int64)), ("raw_k", raw_k), ("raw_v", raw_v),
+                          ("loc_k", loc_k), ("loc_v", loc_v), ("logits", logits), ("scales", scales),
+                          ("eff_k", eff_k), ("eff_v", eff_v)):
+            out[f"c{i}_{name}"] = val
+    out["n"] = np.int64(len(cases))
+    np.savez_compressed(os.path.join(out_dir, "reference_history.npz"), **out)
+    print("reference_history:", len(cases), "cases")
 
 
 def access_plan_golden(reference, out_dir):
@@ -265,14 +337,7 @@ def access_plan_golden(reference, out_dir):
     and a lower one.  Written to access_plan.npz, rows
     [chunk, position, top, older.start, older.end, recent.start, recent.end,
      current.start, current.end, requires_lse_merge]."""
-    import importlib.util
-
-    path = os.path.join(reference, "vllm", "src", "lastkv", "vllm", "backends", "rmarin_flashinfer",
-                        "access_plan.py")
-    spec = importlib.util.spec_from_file_location("rmarin_access_plan", path)
-    ap = importlib.util.module_from_spec(spec)
-    sys.modules[spec.name] = ap  # its dataclasses resolve the module by name
-    spec.loader.exec_module(ap)
+    ap, _ = _planner_modules(reference)
     rows = []
     for chunk in (4, 16, 32, 64, 1024, 4096):
         if chunk <= 64:
