@@ -183,3 +183,25 @@ def test_paged_cache_reserve_keeps_contents():
     for l in range(3):
         assert torch.equal(cache.pool_v[cache.ring_base[l]:cache.ring_base[l] + cache.ring_stride], rings[l])
     assert cache.num_pages == 2 * 13 + 3 * cache.ring_stride
+
+
+def test_published_8b_parameter_layout_without_allocating_weights():
+    """The reference's known answer for the published 8B layout
+    (llm/tests/test_llm_inference.py:137-150): 419 tensors, 8,030,269,952
+    parameters, the per-layer blend logits and value scales, built on the meta
+    device so no weight is allocated."""
+    from lastkv_b200.llm import CustomRecurrentMarinAKV254ReuseKVConfig as Config
+    from lastkv_b200.llm import CustomRecurrentMarinAKV254ReuseKVForCausalLM as Model
+
+    config = Config(hidden_size=4096, intermediate_size=14336, num_attention_heads=32, num_key_value_heads=8,
+                    num_hidden_layers=32, head_dim=128, vocab_size=128256, rms_norm_eps=1e-5,
+                    tie_word_embeddings=False)
+    with torch.device("meta"):
+        model = Model(config)
+    state = model.state_dict()
+    assert len(state) == 419
+    assert sum(t.numel() for t in state.values()) == 8_030_269_952
+    assert state["model.layers.31.self_attn.prev_chunk_alphas"].shape == (8,)
+    assert state["model.layers.0.self_attn.deep_v_scale"].shape == (8,)
+    assert state["model.layers.0.self_attn.q_norm.weight"].shape == (128,)
+    assert state["lm_head.weight"].shape == (128256, 4096)
