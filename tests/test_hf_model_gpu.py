@@ -130,3 +130,26 @@ def test_fused_parameters_alias_and_reload(small_d128):
     rel = np.linalg.norm(a - b) / np.linalg.norm(b)
     print(f"fused vs modules: rel_l2={rel:.3e}")
     assert rel <= 1e-2
+
+
+def test_full_prefill_in_one_call_matches_reference(small_d128):
+    """The reference's check that a full prefill equals the chunk recurrence
+    (llm/tests/test_llm_inference.py:96-103, fp32 there): all 64 tokens in one
+    call, split at the chunk boundaries inside, against the reference's recorded
+    incremental logits, at this file's bf16 tolerance (relative L2 2e-2, max
+    error 5% of the logit span)."""
+    data = small_d128
+    model = build_small(data, fused=True)
+    tokens = torch.from_numpy(data["tokens"]).cuda()
+    B, T = tokens.shape
+    with torch.no_grad():
+        cache = model.new_cache(B, T)
+        logits, cache = model(tokens, cache)
+    cache.check_errors()
+    got = logits.float().cpu().numpy()
+    ref = data["logits_incremental"]
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    span = ref.max() - ref.min()
+    err = np.abs(got - ref).max()
+    print(f"full prefill: rel_l2={rel:.3e} max_abs={err:.3e}")
+    assert rel <= 2e-2 and err <= 5e-2 * span
