@@ -19,9 +19,10 @@
 // Warp roles (384 threads; warp w runs on SM sub-partition w % 4):
 //   warps 0-3  softmax + epilogue of tile A, one thread per row (TMEM lane)
 //   warps 4-7  softmax + epilogue of tile B
-//   warp 8     TMA producer: Q tiles once, then K blocks (128 keys = 8 pages)
-//   warp 9     TMA producer: V blocks
-//   warp 10    idle (keeps the MMA warp off the producers' sub-partitions)
+//   warps 8,10 TMA producers of the K blocks (128 keys = 8 pages): pages 0-3
+//              and 4-7 of every block, each arriving with its half of the bytes
+//   warp 9     TMA producer: the Q tiles once, then the V blocks
+//              (so the first S waits for 8 copies per thread, not Q + 16)
 //   warp 11    TMEM allocator and MMA issuer: the whole warp runs the issue
 //              loop (warp-uniform descriptors, no per-MMA rebuild) and one
 //              elected lane issues every tcgen05.mma / commit
@@ -33,7 +34,11 @@
 // works on the other tile.  P (bf16, two per column) overwrites the first 64
 // columns of its own tile's S; the next S of that tile is issued after the PV
 // that reads P, and tcgen05.mma from one thread executes in issue order.
-// K and V stream through separate rings (2 and 3 stages).  The running max is
+// K and V stream through separate rings (2 and 3 stages).  A bf16 tile whose
+// rows are all tokens of the span is written back through shared memory (its Q
+// buffer) and two TMA stores; ragged tiles and fp32 split partials store row by
+// row (a warp store then touches 32 rows, which cost ~2,600 cycles per tile, on
+// the critical path of the CTA's last tile).  The running max is
 // only raised (and O rescaled in TMEM) when a row's max grows by more than
 // 2^8; otherwise exp2 is taken against the stale max, which stays exact
 // because the final normalisation uses the same reference.  The softmax takes
@@ -47,6 +52,7 @@
 // of a grid of few, long CTAs (Wan's block attention).
 
 #include <math.h>
+#include <string.h>
 
 #include <algorithm>
 
@@ -63,7 +69,7 @@ constexpr int kTiles = 2;  // query tiles per CTA
 constexpr int kBN = 128;  // keys per block
 constexpr int kPageTok = 16;
 constexpr int kPagesPerBlock = kBN / kPageTok;
-constexpr int kWarpK = 8, kWarpV = 9, kWarpMma = 11;
+constexpr int kWarpK = 8, kWarpV = 9, kWarpK2 = 10, kWarpMma = 11;
 constexpr int kThreads = 12 * 32;
 constexpr int kStagesK = 2, kStagesV = 3;
 constexpr float kRescaleLog2 = 8.0f;
@@ -87,6 +93,7 @@ struct PrefillParams {
   float* part_o;         // S > 1: fp32 partials [S][rows][D], rows = token * Hq + head
   float* part_lse;       // S > 1: natural-log LSE [S][rows]
   int64_t part_rows;     // rows per split
+  int tma_out;           // S == 1 and the output map is valid: full tiles leave by TMA stores
 };
 
 template <int D>
@@ -124,7 +131,8 @@ struct Bars {
 template <int D, int GROUP>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tcgen05_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                           const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
+                           const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
+                           const PrefillParams p) {
   using Cfg = PrefillCfg<D>;
   constexpr int TOK = kBM / GROUP;  // tokens per tile
   extern __shared__ uint8_t smem_raw[];
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     for (int s = 0; s < kStagesK; ++s) {
-      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_full[s], 2);
       mbar_init(&bars->k_empty[s], 1);
     }
     for (int s = 0; s < kStagesV; ++s) {
@@ -203,14 +211,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + Cfg::OFF_V;
   const int32_t* btrow = p.bt + (int64_t)b * p.bt_stride;
 
-  if (warp == kWarpK || warp == kWarpV) {
+  if (warp == kWarpK || warp == kWarpK2 || warp == kWarpV) {
     // ------------------------------------------------------------ producers
     if (lane == 0) {
-      const bool is_k = warp == kWarpK;
+      const bool is_k = warp != kWarpV;
       const int stages = is_k ? kStagesK : kStagesV;
       const CUtensorMap* map = is_k ? &tmk : &tmv;
+      const int pg0 = warp == kWarpK2 ? kPagesPerBlock / 2 : 0;
+      const int npg = is_k ? kPagesPerBlock / 2 : kPagesPerBlock;
       tma_prefetch_desc(map);
-      if (is_k) {
+      if (!is_k) {
         tma_prefetch_desc(&tmq);
         mbar_arrive_expect_tx(&bars->q_full, ntiles * Cfg::Q_BYTES);
         for (int t = 0; t < ntiles; ++t)
@@ -229,9 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           bars->fail = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], Cfg::KV_BYTES);
+        mbar_arrive_expect_tx(&full[s], npg * (Cfg::KV_BYTES / kPagesPerBlock));
         uint8_t* dst = ring + s * Cfg::KV_BYTES;
-        for (int pg = 0; pg < kPagesPerBlock; ++pg) {
+        for (int pg = pg0; pg < pg0 + npg; ++pg) {
           const int pi = (j0 + j) * kPagesPerBlock + pg;
           int pid = (int)p.num_pages;  // past the pool: TMA fills zeros
           if (pi < npages) {
@@ -401,7 +411,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) {
       report_error(p.err, DEVERR_WAIT_TIMEOUT, 4, 200);
       bars->fail = 1;
-    } else {
+    }
+    // A bf16 tile whose rows are all tokens of this span leaves through shared
+    // memory: each thread writes its row into the tile's Q buffer (free now: the
+    // tile's last S MMA completed before its last PV) in the 128-byte-swizzled
+    // layout of the Q copy, and one thread stores the tile with two TMA copies of
+    // the same geometry - whole lines instead of one 16-byte piece of 32 rows per
+    // warp store.  Ragged tiles (and the fp32 split partials) store row by row.
+    const bool staged = p.S == 1 && p.tma_out && t0 + (t + 1) * TOK <= Lq;
+    uint8_t* stile = sQ + t * Cfg::Q_BYTES;
+    if (ok) {
       const int hq = hk * GROUP + r % GROUP;
       const bool valid = tok < Lq;
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -411,16 +430,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         // this split's normalised partial (fp32) and its natural-log LSE
         float* orow = p.part_o + ((int64_t)split * p.part_rows + row) * D;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t raw[32];
-          tmem_ld32(lane_base + col_o + c * 32, raw);
+        for (int h = 0; h < D / 64; ++h) {
+          uint32_t raw[2][32];
+          tmem_ld32(lane_base + col_o + h * 64, raw[0]);
+          tmem_ld32(lane_base + col_o + h * 64 + 32, raw[1]);
           tmem_wait_ld();
           if (valid) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              *reinterpret_cast<float4*>(orow + c * 32 + e) =
-                  make_float4(__uint_as_float(raw[e]) * inv, __uint_as_float(raw[e + 1]) * inv,
-                              __uint_as_float(raw[e + 2]) * inv, __uint_as_float(raw[e + 3]) * inv);
+            for (int e = 0; e < 64; e += 4)
+              *reinterpret_cast<float4*>(orow + h * 64 + e) =
+                  make_float4(__uint_as_float(raw[e >> 5][e & 31]) * inv, __uint_as_float(raw[e >> 5][(e & 31) + 1]) * inv,
+                              __uint_as_float(raw[e >> 5][(e & 31) + 2]) * inv,
+                              __uint_as_float(raw[e >> 5][(e & 31) + 3]) * inv);
           }
         }
         if (valid) p.part_lse[(int64_t)split * p.part_rows + row] = lse_e;
@@ -428,23 +449,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sc = inv * (p.out_scale ? p.out_scale[hq] : 1.f);
         __nv_bfloat16* orow = p.out + (int64_t)(q0 + (valid ? tok : 0)) * p.out_stride_tok + (int64_t)hq * D;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t raw[32];
-          tmem_ld32(lane_base + col_o + c * 32, raw);
+        for (int h = 0; h < D / 64; ++h) {
+          uint32_t raw[2][32];
+          tmem_ld32(lane_base + col_o + h * 64, raw[0]);
+          tmem_ld32(lane_base + col_o + h * 64 + 32, raw[1]);
           tmem_wait_ld();
           if (valid) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 8) {
+            for (int c = 0; c < 8; ++c) {
+              const uint32_t* r8 = &raw[c >> 2][(c & 3) * 8];
               uint4 v;
-              v.x = pack_bf16(__uint_as_float(raw[e + 0]) * sc, __uint_as_float(raw[e + 1]) * sc);
-              v.y = pack_bf16(__uint_as_float(raw[e + 2]) * sc, __uint_as_float(raw[e + 3]) * sc);
-              v.z = pack_bf16(__uint_as_float(raw[e + 4]) * sc, __uint_as_float(raw[e + 5]) * sc);
-              v.w = pack_bf16(__uint_as_float(raw[e + 6]) * sc, __uint_as_float(raw[e + 7]) * sc);
-              *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+              v.x = pack_bf16(__uint_as_float(r8[0]) * sc, __uint_as_float(r8[1]) * sc);
+              v.y = pack_bf16(__uint_as_float(r8[2]) * sc, __uint_as_float(r8[3]) * sc);
+              v.z = pack_bf16(__uint_as_float(r8[4]) * sc, __uint_as_float(r8[5]) * sc);
+              v.w = pack_bf16(__uint_as_float(r8[6]) * sc, __uint_as_float(r8[7]) * sc);
+              if (staged)
+                *reinterpret_cast<uint4*>(stile + h * Cfg::Q_HALF + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+              else
+                *reinterpret_cast<uint4*>(orow + h * 64 + c * 8) = v;
             }
           }
         }
         if (valid && p.lse) p.lse[row] = lse_e;
+      }
+    }
+    if (staged) {
+      // every row written (or the tile failed) before one thread copies the tile out
+      fence_proxy_async_smem();
+      const bool all_ok = named_bar_and(1 + t, 128, ok);
+      if (all_ok && r == 0) {
+#pragma unroll
+        for (int h = 0; h < Cfg::HALVES; ++h)
+          tma_store_3d(&tmo, stile + h * Cfg::Q_HALF, h * 64, hk * GROUP, q0 + t0 + t * TOK);
+        bulk_commit_group();
+        bulk_wait_group_read0();  // shared memory is released when the CTA exits
       }
     }
   }
@@ -456,8 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int D, int GROUP>
-int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& prm,
-                   int max_q, cudaStream_t stream) {
+int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& to,
+                   const PrefillParams& prm, int max_q, cudaStream_t stream) {
   using Cfg = PrefillCfg<D>;
   constexpr int TOK = kTiles * kBM / GROUP;  // query tokens per CTA
   static bool attr_done[64] = {false};
@@ -470,7 +508,7 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
     attr_done[dev] = true;
   }
   dim3 grid((max_q + TOK - 1) / TOK, prm.Hkv, prm.B * prm.S);
-  prefill_tcgen05_kernel<D, GROUP><<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
+  prefill_tcgen05_kernel<D, GROUP><<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(tq, tk, tv, to, prm);
   return cudaGetLastError() == cudaSuccess ? LKV_OK : LKV_ERR_CUDA;
 }
 
@@ -503,6 +541,13 @@ int prefill_paged(const PrefillArgs& a) {
   if (st != LKV_OK) return st;
   st = make_pool_tensor_map(&tv, a.pool_v, a.num_pages, a.num_kv_heads, a.head_dim);
   if (st != LKV_OK) return st;
+  // The output has the query's [token][head][dim] geometry: full tiles are stored
+  // with the query map's boxes (unused when the map cannot be built).
+  CUtensorMap to;
+  memset(&to, 0, sizeof(to));
+  const int tma_out =
+      S == 1 && make_query_tensor_map(&to, a.out, a.total_q, a.out_stride_tok, a.num_q_heads, a.head_dim, group) ==
+                    LKV_OK;
 
   PrefillParams prm{};
   prm.bt = a.block_table;
@@ -525,9 +570,10 @@ int prefill_paged(const PrefillArgs& a) {
   prm.part_o = a.part_o;
   prm.part_lse = a.part_lse;
   prm.part_rows = (int64_t)a.total_q * a.num_q_heads;
+  prm.tma_out = tma_out;
   cudaStream_t stream = static_cast<cudaStream_t>(a.stream);
   int rc = LKV_OK;
-#define LKV_PF(DD, GG) rc = launch_prefill<DD, GG>(tq, tk, tv, prm, a.max_q, stream); break
+#define LKV_PF(DD, GG) rc = launch_prefill<DD, GG>(tq, tk, tv, to, prm, a.max_q, stream); break
   if (a.head_dim == 128) {
     switch (group) {
       case 1: LKV_PF(128, 1);
