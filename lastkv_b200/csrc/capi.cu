@@ -68,14 +68,15 @@ int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, 
 // (64-wide half of D) x GROUP heads x (128 / GROUP) tokens box: 128 rows of
 // 128 bytes, row = token * GROUP + head, 128-byte swizzled (a K-major UMMA tile).
 int make_query_tensor_map(CUtensorMap* map, const void* q, int64_t total_q, int64_t q_stride_tok, int num_q_heads,
-                          int head_dim, int group) {
+                          int head_dim, int group, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return LKV_ERR_TENSOR_MAP;
   if ((reinterpret_cast<uintptr_t>(q) & 15) || total_q < 1 || total_q > (int64_t)0x7fffffff) return LKV_ERR_INVALID_ARGUMENT;
   if (q_stride_tok < (int64_t)num_q_heads * head_dim) return LKV_ERR_INVALID_ARGUMENT;
+  if (group < 1 || box_rows < group || box_rows > 256 || box_rows % group) return LKV_ERR_INVALID_ARGUMENT;
   cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)total_q};
   cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)q_stride_tok * 2};
-  cuuint32_t box[3] = {64, (cuuint32_t)group, (cuuint32_t)(128 / group)};
+  cuuint32_t box[3] = {64, (cuuint32_t)group, (cuuint32_t)(box_rows / group)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

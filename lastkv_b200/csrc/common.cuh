@@ -160,19 +160,6 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// Named barrier `id` over `count` threads (a multiple of 32, warp-uniform
-// arrival) that returns whether `pred` held in every one of them.
-__device__ __forceinline__ bool named_bar_and(int id, int count, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

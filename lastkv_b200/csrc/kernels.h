@@ -15,8 +15,10 @@ constexpr size_t kWorkspaceHeader = 256;
 int make_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t num_pages, int num_kv_heads, int head_dim);
 int make_matrix_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride,
                            int box_rows);
+// box_rows: query rows (tokens x group heads) per copy - a 128-row tile, or a
+// warp's 32 rows for the output stores.
 int make_query_tensor_map(CUtensorMap* map, const void* q, int64_t total_q, int64_t q_stride_tok, int num_q_heads,
-                          int head_dim, int group);
+                          int head_dim, int group, int box_rows = 128);
 
 struct PrefillArgs {
   const void* q;

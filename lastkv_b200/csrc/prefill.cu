@@ -36,8 +36,8 @@
 // that reads P, and tcgen05.mma from one thread executes in issue order.
 // K and V stream through separate rings (2 and 3 stages).  A bf16 tile whose
 // rows are all tokens of the span is written back through shared memory (its Q
-// buffer) and two TMA stores; ragged tiles and fp32 split partials store row by
-// row (a warp store then touches 32 rows, which cost ~2,600 cycles per tile, on
+// buffer) and one TMA store per warp and 64-column half; ragged tiles and fp32
+// split partials store row by row (a warp store then touches 32 rows, which cost ~2,600 cycles per tile, on
 // the critical path of the CTA's last tile).  The running max is
 // only raised (and O rescaled in TMEM) when a row's max grows by more than
 // 2^8; otherwise exp2 is taken against the stale max, which stays exact
@@ -415,11 +415,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // A bf16 tile whose rows are all tokens of this span leaves through shared
     // memory: each thread writes its row into the tile's Q buffer (free now: the
     // tile's last S MMA completed before its last PV) in the 128-byte-swizzled
-    // layout of the Q copy, and one thread stores the tile with two TMA copies of
-    // the same geometry - whole lines instead of one 16-byte piece of 32 rows per
-    // warp store.  Ragged tiles (and the fp32 split partials) store row by row.
+    // layout of the Q copy, and each warp stores its 32 rows of a 64-column half
+    // with one TMA copy as soon as it has written them - whole lines instead of
+    // one 16-byte piece of 32 rows per warp store, and no wait for the other
+    // warps.  Ragged tiles (and the fp32 split partials) store row by row.
     const bool staged = p.S == 1 && p.tma_out && t0 + (t + 1) * TOK <= Lq;
-    uint8_t* stile = sQ + t * Cfg::Q_BYTES;
+    uint8_t* swarp = sQ + t * Cfg::Q_BYTES + (warp & 3) * 32 * 128;  // this warp's 32 rows of half 0
     if (ok) {
       const int hq = hk * GROUP + r % GROUP;
       const bool valid = tok < Lq;
@@ -464,25 +465,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               v.z = pack_bf16(__uint_as_float(r8[4]) * sc, __uint_as_float(r8[5]) * sc);
               v.w = pack_bf16(__uint_as_float(r8[6]) * sc, __uint_as_float(r8[7]) * sc);
               if (staged)
-                *reinterpret_cast<uint4*>(stile + h * Cfg::Q_HALF + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+                *reinterpret_cast<uint4*>(swarp + h * Cfg::Q_HALF + lane * 128 + ((c ^ (r & 7)) << 4)) = v;
               else
                 *reinterpret_cast<uint4*>(orow + h * 64 + c * 8) = v;
             }
           }
+          if (staged) {
+            fence_proxy_async_smem();  // this lane's rows, visible to the copy
+            __syncwarp();
+            if (lane == 0)
+              tma_store_3d(&tmo, swarp + h * Cfg::Q_HALF, h * 64, hk * GROUP,
+                           q0 + t0 + t * TOK + (warp & 3) * (32 / GROUP));
+          }
+        }
+        if (staged && lane == 0) {
+          bulk_commit_group();
+          bulk_wait_group_read0();  // shared memory is released when the CTA exits
         }
         if (valid && p.lse) p.lse[row] = lse_e;
-      }
-    }
-    if (staged) {
-      // every row written (or the tile failed) before one thread copies the tile out
-      fence_proxy_async_smem();
-      const bool all_ok = named_bar_and(1 + t, 128, ok);
-      if (all_ok && r == 0) {
-#pragma unroll
-        for (int h = 0; h < Cfg::HALVES; ++h)
-          tma_store_3d(&tmo, stile + h * Cfg::Q_HALF, h * 64, hk * GROUP, q0 + t0 + t * TOK);
-        bulk_commit_group();
-        bulk_wait_group_read0();  // shared memory is released when the CTA exits
       }
     }
   }
@@ -542,12 +542,11 @@ int prefill_paged(const PrefillArgs& a) {
   st = make_pool_tensor_map(&tv, a.pool_v, a.num_pages, a.num_kv_heads, a.head_dim);
   if (st != LKV_OK) return st;
   // The output has the query's [token][head][dim] geometry: full tiles are stored
-  // with the query map's boxes (unused when the map cannot be built).
+  // a warp's 32 rows at a time (unused when the map cannot be built).
   CUtensorMap to;
   memset(&to, 0, sizeof(to));
-  const int tma_out =
-      S == 1 && make_query_tensor_map(&to, a.out, a.total_q, a.out_stride_tok, a.num_q_heads, a.head_dim, group) ==
-                    LKV_OK;
+  const int tma_out = S == 1 && make_query_tensor_map(&to, a.out, a.total_q, a.out_stride_tok, a.num_q_heads,
+                                                      a.head_dim, group, 32) == LKV_OK;
 
   PrefillParams prm{};
   prm.bt = a.block_table;
