@@ -158,13 +158,28 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const __nv_
   const __nv_bfloat16* row = x + (int64_t)blockIdx.x * row_stride;
   ArgMax best{-INFINITY, 0x7fffffff};
   const int nvec = cols / 8;
-  for (int c = threadIdx.x; c < nvec; c += kArgmaxThreads) {
-    float f[8];
-    unpack8(*reinterpret_cast<const uint4*>(row + c * 8), f);
+  // Eight independent 16-byte loads per thread and pass (two L2 round trips for
+  // a 128K-column row instead of sixteen); the order of the comparisons does not
+  // matter, argmax_before being a strict total order.
+  constexpr int U = 8;
+  for (int c0 = threadIdx.x; c0 < nvec; c0 += U * kArgmaxThreads) {
+    uint4 v[U];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const ArgMax cand{f[j], c * 8 + j};
-      if (argmax_before(cand, best)) best = cand;
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * kArgmaxThreads;
+      if (c < nvec) v[u] = *reinterpret_cast<const uint4*>(row + (int64_t)c * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * kArgmaxThreads;
+      if (c >= nvec) break;
+      float f[8];
+      unpack8(v[u], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const ArgMax cand{f[j], c * 8 + j};
+        if (argmax_before(cand, best)) best = cand;
+      }
     }
   }
   for (int c = nvec * 8 + threadIdx.x; c < cols; c += kArgmaxThreads) {
