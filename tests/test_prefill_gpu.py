@@ -52,6 +52,11 @@ CASES = [
     (6, [77], [1000], 12, 12, 64, False),
     (7, [256], [256 + 4680], 32, 4, 128, False),
     (8, [16, 16, 16], [16, 100, 1024], 64, 8, 128, True),
+    # full output tiles (stored through shared memory by TMA) next to ragged ones,
+    # for the GQA groups and head dims the cases above leave out
+    (9, [300], [700], 8, 4, 128, True),              # group 2
+    (10, [256, 40], [256, 900], 8, 8, 128, True),    # group 1, 128-token tiles
+    (11, [130], [2000], 4, 4, 64, False),            # group 1, D 64
 ]
 
 
